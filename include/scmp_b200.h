@@ -1,0 +1,110 @@
+/*
+ * scmp_b200.h -- C ABI of the B200 stochastic-computing (SC) matmul engine.
+ *
+ * Plain pointers and sizes only; every pointer is device memory on the
+ * current CUDA device unless stated otherwise.  Every entry point returns
+ * SCMP_OK (0) or a negative SCMP_E* code and never aborts; the message of the
+ * last failure on the calling thread is available from scmp_last_error().
+ *
+ * The entry points replace the reference's kernel package `scmp_kernels`,
+ * which the reference imports but does not vendor (.gitmodules:4-7):
+ *   scmp_sc_matmul        <- scmp_kernels.sc.sc_matmul(a, b, granularity=,
+ *                            mode=, sc_prec=, config=, group_a=, group_b=,
+ *                            chunk_d=, stoc_len=)   as called at
+ *                            sc_integration/sc_linear.py:137-147,170-180,
+ *                            cls/sc_attention_patch.py:193-196,288-291,314-318,
+ *                            det/sc_patch/sc_matmul.py:129-134,151-158,189-194
+ *   row_stoc_len field    <- the per-level bucket loop of
+ *                            sc_integration/sc_linear.py:255-265 and
+ *                            cls/sc_attention_patch.py:217-240 (one launch
+ *                            instead of one per level)
+ *   slice_stoc_len field  <- the per-head bucket loop of
+ *                            cls/sc_attention_patch.py:168-197
+ *   scmp_sc_matmul_workspace_size: sizing helper (no reference counterpart;
+ *                            the Triton package allocated internally)
+ */
+#ifndef SCMP_B200_H
+#define SCMP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SCMP_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SCMP_API __attribute__((visibility("default")))
+#else
+#define SCMP_API
+#endif
+
+enum scmp_status {
+  SCMP_OK = 0,
+  SCMP_EINVAL = -1,       /* bad shape / argument */
+  SCMP_ECUDA = -2,        /* a CUDA runtime call failed */
+  SCMP_EWORKSPACE = -3,   /* workspace missing or too small */
+  SCMP_EUNSUPPORTED = -4, /* valid request this build does not implement */
+  SCMP_ETIMEOUT = -5      /* a bounded device-side wait gave up */
+};
+
+enum scmp_granularity { SCMP_PER_ROW = 0, SCMP_PER_HEAD = 1, SCMP_PER_TENSOR = 2 };
+enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
+enum scmp_engine {
+  SCMP_ENGINE_AUTO = 0,
+  SCMP_ENGINE_POPC = 1,    /* CUDA-core LOP3 + POPC over bit-packed streams */
+  SCMP_ENGINE_TCGEN05 = 2  /* tcgen05 kind::i8 tensor-core bit-product GEMM */
+};
+
+typedef struct scmp_matmul_args {
+  int32_t abi_version;      /* must be SCMP_ABI_VERSION */
+  int32_t engine;           /* enum scmp_engine */
+  /* a: [batch, M, K] fp32 contiguous; b: [batch_b, N, K] with batch_b in
+   * {1, batch} (1 = b shared by every slice, e.g. a weight). */
+  const float *a;
+  const float *b;
+  int64_t batch, batch_b, M, N, K;
+  int32_t granularity;      /* enum scmp_granularity */
+  int32_t mode;             /* enum scmp_mode */
+  int32_t sc_prec;          /* p in [1, 8] (bipolar needs p >= 2) */
+  int32_t stoc_len;         /* L in [1, 2^p]; used when no per-row table */
+  int64_t group_a, group_b; /* per_row: rows per scale group (>= 1) */
+  const uint8_t *pool;      /* stream pool R [pool_dims, 2^p] (uint8) */
+  int32_t pool_dims;        /* reduction index d reads pool row d % pool_dims */
+  int32_t reserved0;
+  /* Optional per-a-row stream length [batch * M]: > 0 computes the row with
+   * that L, 0 writes the pruned row (zeros + bias), < 0 leaves the output row
+   * untouched (it belongs to another call).  NULL = every row uses stoc_len. */
+  const int32_t *row_stoc_len;
+  /* Optional per-slice stream length [batch] (same meaning, per slice). */
+  const int32_t *slice_stoc_len;
+  const float *bias;        /* nullable [N], added after the rescale */
+  float *out;               /* [batch, M, N] fp32 */
+  int32_t *acc_out;         /* nullable [batch, M, N] signed popcount sums */
+  void *workspace;          /* device scratch, see scmp_sc_matmul_workspace_size */
+  size_t workspace_bytes;
+} scmp_matmul_args;
+
+/* Bytes of device scratch that scmp_sc_matmul needs for these arguments
+ * (pointers may be NULL when only sizing).  Returns 0 on invalid arguments. */
+SCMP_API size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args);
+
+/* SC estimate of a @ b^T per slice: quantise both operands, compare their
+ * magnitudes against the pool (enable window for a, Sobol/LFSR stream for b),
+ * accumulate signed popcounts, rescale to fp32.  Asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream). */
+SCMP_API int scmp_sc_matmul(const scmp_matmul_args *args, void *stream);
+
+/* Message of the last failure on this thread ("" if none). */
+SCMP_API const char *scmp_last_error(void);
+
+/* SCMP_ABI_VERSION of the loaded library. */
+SCMP_API int scmp_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCMP_B200_H */

@@ -1,0 +1,112 @@
+"""ctypes binding of the engine's C ABI (``include/scmp_b200.h``).
+
+The library is built in-tree (``scmp_vit_b200/libscmp_b200.so``).  There is
+no fallback: if it is missing or fails to load, every SC call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libscmp_b200.so"
+
+ABI_VERSION = 1
+
+SCMP_OK = 0
+STATUS_NAMES = {
+    -1: "SCMP_EINVAL", -2: "SCMP_ECUDA", -3: "SCMP_EWORKSPACE",
+    -4: "SCMP_EUNSUPPORTED", -5: "SCMP_ETIMEOUT",
+}
+GRANULARITY = {"per_row": 0, "per_head": 1, "per_tensor": 2}
+MODE = {"bipolar": 0, "unipolar": 1}
+ENGINE = {"auto": 0, "popc": 1, "tcgen05": 2}
+
+EXPORTED_SYMBOLS = (
+    "scmp_sc_matmul_workspace_size",
+    "scmp_sc_matmul",
+    "scmp_last_error",
+    "scmp_abi_version",
+)
+
+
+class MatmulArgs(ctypes.Structure):
+    """Mirror of ``scmp_matmul_args`` (field order and types must match)."""
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("engine", ctypes.c_int32),
+        ("a", ctypes.c_void_p),
+        ("b", ctypes.c_void_p),
+        ("batch", ctypes.c_int64),
+        ("batch_b", ctypes.c_int64),
+        ("M", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("granularity", ctypes.c_int32),
+        ("mode", ctypes.c_int32),
+        ("sc_prec", ctypes.c_int32),
+        ("stoc_len", ctypes.c_int32),
+        ("group_a", ctypes.c_int64),
+        ("group_b", ctypes.c_int64),
+        ("pool", ctypes.c_void_p),
+        ("pool_dims", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("row_stoc_len", ctypes.c_void_p),
+        ("slice_stoc_len", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("acc_out", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class EngineError(RuntimeError):
+    """A non-zero status returned by the engine."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the engine library once (raises if it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"SC engine library {LIB_PATH} is missing; build it with "
+                "`python -c 'import __graft_entry__ as g; g.build()'`. "
+                "There is no CPU fallback.")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.scmp_sc_matmul_workspace_size.argtypes = [ctypes.POINTER(MatmulArgs)]
+        lib.scmp_sc_matmul_workspace_size.restype = ctypes.c_size_t
+        lib.scmp_sc_matmul.argtypes = [ctypes.POINTER(MatmulArgs), ctypes.c_void_p]
+        lib.scmp_sc_matmul.restype = ctypes.c_int
+        lib.scmp_last_error.argtypes = []
+        lib.scmp_last_error.restype = ctypes.c_char_p
+        lib.scmp_abi_version.argtypes = []
+        lib.scmp_abi_version.restype = ctypes.c_int
+        if lib.scmp_abi_version() != ABI_VERSION:
+            raise RuntimeError(
+                f"engine ABI {lib.scmp_abi_version()} != expected {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().scmp_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int) -> None:
+    if status != SCMP_OK:
+        raise EngineError(status, last_error())

@@ -1,0 +1,217 @@
+// C ABI of the SC matmul engine (declared in include/scmp_b200.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "sc_common.cuh"
+
+namespace scmp {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(SCMP_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct OperandLayout {
+  GroupShape g;
+  size_t stat, gscale, ginv, gzero, code, rscale, rzero, rsum;  // offsets
+};
+
+// Bump allocator over the caller's workspace (or a null base when sizing).
+struct Carver {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    size_t at = off;
+    off = align_up(off + bytes);
+    return at;
+  }
+};
+
+GroupShape make_groups(int gran, int64_t slices, int64_t rows_per_slice, int64_t group) {
+  GroupShape g{};
+  g.rows = slices * rows_per_slice;
+  if (gran == SCMP_PER_TENSOR) {
+    g.slice_rows = g.rows;
+    g.group_rows = g.rows;
+  } else if (gran == SCMP_PER_HEAD) {
+    g.slice_rows = rows_per_slice;
+    g.group_rows = rows_per_slice;
+  } else {
+    g.slice_rows = rows_per_slice;
+    g.group_rows = group < rows_per_slice ? group : rows_per_slice;
+  }
+  g.groups_per_slice = (g.slice_rows + g.group_rows - 1) / g.group_rows;
+  g.ngroups = (g.rows / g.slice_rows) * g.groups_per_slice;
+  return g;
+}
+
+void layout_operand(Carver &c, OperandLayout &o, int64_t K) {
+  const int64_t rows = o.g.rows, ng = o.g.ngroups;
+  o.stat = c.take(sizeof(float2) * rows);
+  o.gscale = c.take(sizeof(float) * ng);
+  o.ginv = c.take(sizeof(float) * ng);
+  o.gzero = c.take(sizeof(int32_t) * ng);
+  o.code = c.take(sizeof(int16_t) * rows * K);
+  o.rscale = c.take(sizeof(float) * rows);
+  o.rzero = c.take(sizeof(int32_t) * rows);
+  o.rsum = c.take(sizeof(int32_t) * rows);
+}
+
+struct Plan {
+  OperandLayout A, B;
+  size_t table = 0;
+  size_t total = 0;
+};
+
+int validate(const scmp_matmul_args *x) {
+  if (!x) return fail(SCMP_EINVAL, "args is NULL");
+  if (x->abi_version != SCMP_ABI_VERSION)
+    return fail(SCMP_EINVAL, "abi_version %d != %d", x->abi_version, SCMP_ABI_VERSION);
+  if (x->batch < 0 || x->M < 0 || x->N < 0 || x->K <= 0)
+    return fail(SCMP_EINVAL, "bad shape batch=%lld M=%lld N=%lld K=%lld", (long long)x->batch,
+                (long long)x->M, (long long)x->N, (long long)x->K);
+  if (x->batch_b != 1 && x->batch_b != x->batch)
+    return fail(SCMP_EINVAL, "batch_b=%lld must be 1 or batch=%lld", (long long)x->batch_b,
+                (long long)x->batch);
+  if (x->granularity < SCMP_PER_ROW || x->granularity > SCMP_PER_TENSOR)
+    return fail(SCMP_EINVAL, "unknown granularity %d", x->granularity);
+  if (x->mode != SCMP_BIPOLAR && x->mode != SCMP_UNIPOLAR)
+    return fail(SCMP_EINVAL, "unknown mode %d", x->mode);
+  if (x->sc_prec < 1 || x->sc_prec > kMaxPrec || (x->mode == SCMP_BIPOLAR && x->sc_prec < 2))
+    return fail(SCMP_EINVAL, "sc_prec=%d out of range for mode %d", x->sc_prec, x->mode);
+  const int T = 1 << x->sc_prec;
+  if (!x->row_stoc_len && !x->slice_stoc_len && (x->stoc_len < 1 || x->stoc_len > T))
+    return fail(SCMP_EINVAL, "stoc_len=%d must be in [1, 2^sc_prec=%d]", x->stoc_len, T);
+  if (x->granularity == SCMP_PER_ROW && (x->group_a < 1 || x->group_b < 1))
+    return fail(SCMP_EINVAL, "group_a/group_b must be >= 1");
+  if (x->pool_dims <= 0) return fail(SCMP_EINVAL, "pool_dims must be positive");
+  if (x->engine != SCMP_ENGINE_AUTO && x->engine != SCMP_ENGINE_POPC &&
+      x->engine != SCMP_ENGINE_TCGEN05)
+    return fail(SCMP_EINVAL, "unknown engine %d", x->engine);
+  return SCMP_OK;
+}
+
+Plan make_plan(const scmp_matmul_args *x) {
+  Plan p;
+  Carver c;
+  p.A.g = make_groups(x->granularity, x->batch, x->M, x->group_a);
+  p.B.g = make_groups(x->granularity, x->batch_b, x->N, x->group_b);
+  layout_operand(c, p.A, x->K);
+  layout_operand(c, p.B, x->K);
+  const int T = 1 << x->sc_prec;
+  const int WT = T >= 32 ? T / 32 : 1;
+  p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
+  p.total = c.off;
+  return p;
+}
+
+int quantize_operand(const float *x, const OperandLayout &o, int64_t K, int mode, int prec,
+                     unsigned char *ws, cudaStream_t s) {
+  cudaError_t e;
+  auto *stat = reinterpret_cast<float2 *>(ws + o.stat);
+  auto *gscale = reinterpret_cast<float *>(ws + o.gscale);
+  auto *ginv = reinterpret_cast<float *>(ws + o.ginv);
+  auto *gzero = reinterpret_cast<int32_t *>(ws + o.gzero);
+  if ((e = launch_row_stats(x, o.g.rows, K, mode, stat, s)) != cudaSuccess)
+    return cuda_fail(e, "row_stats launch");
+  if ((e = launch_group_stats(stat, o.g, mode, prec, gscale, ginv, gzero, s)) != cudaSuccess)
+    return cuda_fail(e, "group_stats launch");
+  if ((e = launch_quantize(x, o.g, K, mode, prec, gscale, ginv, gzero,
+                           reinterpret_cast<int16_t *>(ws + o.code),
+                           reinterpret_cast<float *>(ws + o.rscale),
+                           reinterpret_cast<int32_t *>(ws + o.rzero),
+                           reinterpret_cast<int32_t *>(ws + o.rsum), s)) != cudaSuccess)
+    return cuda_fail(e, "quantize launch");
+  return SCMP_OK;
+}
+
+QuantPlane plane_of(const OperandLayout &o, unsigned char *ws) {
+  QuantPlane q;
+  q.code = reinterpret_cast<const int16_t *>(ws + o.code);
+  q.scale = reinterpret_cast<const float *>(ws + o.rscale);
+  q.zero = reinterpret_cast<const int32_t *>(ws + o.rzero);
+  q.rowsum = reinterpret_cast<const int32_t *>(ws + o.rsum);
+  return q;
+}
+
+}  // namespace
+}  // namespace scmp
+
+using namespace scmp;
+
+extern "C" {
+
+const char *scmp_last_error(void) { return g_last_error.c_str(); }
+
+int scmp_abi_version(void) { return SCMP_ABI_VERSION; }
+
+size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args) {
+  if (validate(args) != SCMP_OK) return 0;
+  if (args->batch == 0 || args->M == 0 || args->N == 0) return kAlign;
+  return make_plan(args).total;
+}
+
+int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
+  g_last_error.clear();
+  int rc = validate(args);
+  if (rc != SCMP_OK) return rc;
+  const scmp_matmul_args &x = *args;
+  if (x.batch == 0 || x.M == 0 || x.N == 0) return SCMP_OK;
+  if (!x.a || !x.b || !x.pool || !x.out)
+    return fail(SCMP_EINVAL, "a, b, pool and out must be non-NULL");
+  if (x.engine == SCMP_ENGINE_TCGEN05)
+    return fail(SCMP_EUNSUPPORTED, "tcgen05 engine is not built into this library");
+  const Plan plan = make_plan(&x);
+  if (!x.workspace || x.workspace_bytes < plan.total)
+    return fail(SCMP_EWORKSPACE, "workspace needs %zu bytes, got %zu", plan.total,
+                x.workspace ? x.workspace_bytes : (size_t)0);
+  auto *ws = static_cast<unsigned char *>(x.workspace);
+  auto s = static_cast<cudaStream_t>(stream);
+
+  if ((rc = quantize_operand(x.a, plan.A, x.K, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
+  if ((rc = quantize_operand(x.b, plan.B, x.K, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
+  auto *table = reinterpret_cast<uint32_t *>(ws + plan.table);
+  cudaError_t e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table, s);
+  if (e != cudaSuccess) return cuda_fail(e, "stream_table launch");
+
+  GemmProblem P{};
+  P.qa = plane_of(plan.A, ws);
+  P.qb = plane_of(plan.B, ws);
+  P.batch = x.batch;
+  P.batch_b = x.batch_b;
+  P.M = x.M;
+  P.N = x.N;
+  P.K = x.K;
+  P.mode = x.mode;
+  P.prec = x.sc_prec;
+  P.stoc_len = x.stoc_len;
+  P.pool = x.pool;
+  P.pool_dims = x.pool_dims;
+  P.row_L = x.row_stoc_len;
+  P.slice_L = x.slice_stoc_len;
+  P.bias = x.bias;
+  P.out = x.out;
+  P.acc_out = x.acc_out;
+  P.stream_table = table;
+  if ((e = launch_gemm_popc(P, s)) != cudaSuccess) return cuda_fail(e, "gemm_popc launch");
+  return SCMP_OK;
+}
+
+}  // extern "C"

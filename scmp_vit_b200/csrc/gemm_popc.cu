@@ -1,0 +1,171 @@
+// SC GEMM on CUDA cores: LOP3 + POPC over bit-packed streams.
+//
+// For every (m, n, d) the enable window of a (a prefix mask of k bits) is
+// ANDed with the Sobol/LFSR stream of b (bit t = [R[d][t] < c_b]) and the
+// popcount is accumulated with the sign product.  This is the integer-pipe
+// formulation of the SC inner product; it is kept as the baseline engine and
+// as the engine for shapes the tensor-core path does not take.
+#include "sc_common.cuh"
+
+namespace scmp {
+namespace {
+
+constexpr int BM = 64;
+constexpr int BN = 64;
+constexpr int kThreads = 256;
+
+template <int LW>
+struct PopcCfg {
+  static constexpr int BD = LW >= 8 ? 8 : 16;  // reduction dims per stage
+  static constexpr size_t smem_bytes =
+      (size_t)BD * (BM + BN) * LW * sizeof(uint32_t) + (size_t)BD * (BM + BN);
+};
+
+template <int LW>
+__global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
+  using Cfg = PopcCfg<LW>;
+  constexpr int BD = Cfg::BD;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint32_t *sA = reinterpret_cast<uint32_t *>(smem_raw);  // [BD][BM][LW]
+  uint32_t *sB = sA + BD * BM * LW;                        // [BD][BN][LW]
+  int8_t *gA = reinterpret_cast<int8_t *>(sB + BD * BN * LW);  // [BD][BM]
+  int8_t *gB = gA + BD * BM;                                    // [BD][BN]
+
+  const int64_t slice = blockIdx.z;
+  const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
+  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  const int64_t n0 = (int64_t)blockIdx.x * BN;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int T = 1 << P.prec;
+  const int WT = T >= 32 ? T / 32 : 1;
+
+  int32_t acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0;
+
+  for (int64_t d0 = 0; d0 < P.K; d0 += BD) {
+    // ---- stage A: enable windows (prefix masks) and signs
+    for (int idx = tid; idx < BM * BD; idx += kThreads) {
+      const int m = idx / BD, dd = idx % BD;
+      const int64_t gm = m0 + m, d = d0 + dd;
+      int k = 0, s = 1;
+      if (gm < P.M && d < P.K) {
+        const int64_t grow = slice * P.M + gm;
+        const int L = row_stream_len(P, slice, grow);
+        const int c = P.qa.code[grow * P.K + d];
+        s = c < 0 ? -1 : 1;
+        if (L > 0) k = ((c < 0 ? -c : c) * L) >> P.prec;
+      }
+      uint32_t *dst = sA + (dd * BM + m) * LW;
+#pragma unroll
+      for (int w = 0; w < LW; ++w) {
+        const int lo = 32 * w;
+        dst[w] = k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
+      }
+      gA[dd * BM + m] = (int8_t)s;
+    }
+    // ---- stage B: streams from the table, and signs
+    for (int idx = tid; idx < BN * BD; idx += kThreads) {
+      const int n = idx / BD, dd = idx % BD;
+      const int64_t gn = n0 + n, d = d0 + dd;
+      uint32_t *dst = sB + (dd * BN + n) * LW;
+      int s = 1;
+      if (gn < P.N && d < P.K) {
+        const int c = P.qb.code[(slice_b * P.N + gn) * P.K + d];
+        s = c < 0 ? -1 : 1;
+        const int v = c < 0 ? -c : c;
+        const uint32_t *st =
+            P.stream_table + ((int64_t)(d % P.pool_dims) * (T + 1) + v) * WT;
+#pragma unroll
+        for (int w = 0; w < LW; ++w) dst[w] = st[w];
+      } else {
+#pragma unroll
+        for (int w = 0; w < LW; ++w) dst[w] = 0u;
+      }
+      gB[dd * BN + n] = (int8_t)s;
+    }
+    __syncthreads();
+    // ---- popcount inner product
+#pragma unroll 2
+    for (int dd = 0; dd < BD; ++dd) {
+      uint32_t a[4][LW], b[4][LW];
+      int sa[4], sb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t *pa = sA + (dd * BM + ty + 16 * i) * LW;
+        const uint32_t *pb = sB + (dd * BN + tx + 16 * i) * LW;
+#pragma unroll
+        for (int w = 0; w < LW; ++w) { a[i][w] = pa[w]; b[i][w] = pb[w]; }
+        sa[i] = gA[dd * BM + ty + 16 * i];
+        sb[i] = gB[dd * BN + tx + 16 * i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int cnt = 0;
+#pragma unroll
+          for (int w = 0; w < LW; ++w) cnt += __popc(a[i][w] & b[j][w]);
+          acc[i][j] += (sa[i] * sb[j]) * cnt;
+        }
+    }
+    __syncthreads();
+  }
+
+  // ---- epilogue: rescale, bias, store
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gm = m0 + ty + 16 * i;
+    if (gm >= P.M) continue;
+    const int64_t grow = slice * P.M + gm;
+    const int L = row_stream_len(P, slice, grow);
+    if (L < 0) continue;
+    const float sa = P.qa.scale[grow];
+    const int32_t za = P.qa.zero[grow], rsa = P.qa.rowsum[grow];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gn = n0 + tx + 16 * j;
+      if (gn >= P.N) continue;
+      const int64_t brow = slice_b * P.N + gn;
+      float y = 0.0f;
+      const int32_t a = L > 0 ? acc[i][j] : 0;
+      if (L > 0)
+        y = sc_rescale(P.mode, P.prec, L, a, P.K, sa, za, rsa, P.qb.scale[brow], P.qb.zero[brow],
+                       P.qb.rowsum[brow]);
+      if (P.bias) y = __fadd_rn(y, P.bias[gn]);
+      const int64_t o = grow * P.N + gn;
+      P.out[o] = y;
+      if (P.acc_out) P.acc_out[o] = a;
+    }
+  }
+}
+
+template <int LW>
+cudaError_t launch_lw(const GemmProblem &P, cudaStream_t s) {
+  const size_t smem = PopcCfg<LW>::smem_bytes;
+  cudaError_t e = cudaFuncSetAttribute(gemm_popc_kernel<LW>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((P.N + BN - 1) / BN), (unsigned)((P.M + BM - 1) / BM), (unsigned)P.batch);
+  gemm_popc_kernel<LW><<<grid, kThreads, smem, s>>>(P);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s) {
+  if (P.M == 0 || P.N == 0 || P.batch == 0) return cudaSuccess;
+  // Words per stream: enough for the longest stream any row may use.
+  const int T = 1 << P.prec;
+  const int Lmax = (P.row_L || P.slice_L) ? T : P.stoc_len;
+  const int lw = (Lmax + 31) / 32;
+  if (lw <= 1) return launch_lw<1>(P, s);
+  if (lw <= 2) return launch_lw<2>(P, s);
+  if (lw <= 4) return launch_lw<4>(P, s);
+  return launch_lw<8>(P, s);
+}
+
+}  // namespace scmp

@@ -1,0 +1,209 @@
+// Quantisation of SC operands and the per-pool stream table.
+//
+// Bit-exact restatement of sco_quantize in oracle/sc_oracle.c: IEEE fp32
+// divide/multiply (no contraction), round-half-even, 1e-6 floor on the range
+// (reference sc_integration/sc_linear.py:95-111).
+#include "sc_common.cuh"
+
+namespace scmp {
+namespace {
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per row: (max|x|, -) for bipolar, (min x, max x) for unipolar.
+__global__ void row_stats_kernel(const float *__restrict__ x, int64_t rows, int64_t K, int mode,
+                                 float2 *__restrict__ stat) {
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float *xr = x + warp * K;
+  float lo = INFINITY, hi = -INFINITY;
+  if ((K & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+    for (int64_t i = lane; i < (K >> 2); i += 32) {
+      float4 v = __ldg(x4 + i);
+      if (mode == SCMP_BIPOLAR) {
+        hi = fmaxf(hi, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      } else {
+        lo = fminf(lo, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
+        hi = fmaxf(hi, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+      }
+    }
+  } else {
+    for (int64_t i = lane; i < K; i += 32) {
+      float v = __ldg(xr + i);
+      if (mode == SCMP_BIPOLAR) {
+        hi = fmaxf(hi, fabsf(v));
+      } else {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+      }
+    }
+  }
+  hi = warp_max(hi);
+  lo = warp_min(lo);
+  if (lane == 0) stat[warp] = make_float2(lo, hi);
+}
+
+// One block per scale group.
+__global__ void group_stats_kernel(const float2 *__restrict__ stat, GroupShape g, int mode,
+                                   int prec, float *__restrict__ gscale,
+                                   float *__restrict__ ginv, int32_t *__restrict__ gzero) {
+  const int64_t grp = blockIdx.x;
+  if (grp >= g.ngroups) return;
+  const int64_t slice = grp / g.groups_per_slice;
+  const int64_t j = grp % g.groups_per_slice;
+  const int64_t r0 = slice * g.slice_rows + j * g.group_rows;
+  int64_t r1 = r0 + g.group_rows;
+  const int64_t slice_end = (slice + 1) * g.slice_rows;
+  if (r1 > slice_end) r1 = slice_end;
+  float lo = INFINITY, hi = -INFINITY;
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    float2 s = stat[r];
+    lo = fminf(lo, s.x);
+    hi = fmaxf(hi, s.y);
+  }
+  __shared__ float slo[32], shi[32];
+  lo = warp_min(lo);
+  hi = warp_max(hi);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { slo[w] = lo; shi[w] = hi; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    lo = lane < nw ? slo[lane] : INFINITY;
+    hi = lane < nw ? shi[lane] : -INFINITY;
+    lo = warp_min(lo);
+    hi = warp_max(hi);
+    if (lane == 0) {
+      if (mode == SCMP_BIPOLAR) {
+        const float qmax = (float)((1 << (prec - 1)) - 1);
+        const float amax = hi > 1e-6f ? hi : 1e-6f;
+        gscale[grp] = __fdiv_rn(amax, qmax);
+        ginv[grp] = __fdiv_rn(qmax, amax);
+        gzero[grp] = 0;
+      } else {
+        const float qmax = (float)((1 << prec) - 1);
+        float rng = __fsub_rn(hi, lo);
+        if (!(rng > 1e-6f)) rng = 1e-6f;
+        const float inv = __fdiv_rn(qmax, rng);
+        gscale[grp] = __fdiv_rn(rng, qmax);
+        ginv[grp] = inv;
+        gzero[grp] = __float2int_rn(__fmul_rn(-lo, inv));
+      }
+    }
+  }
+}
+
+// One warp per row: signed codes, per-row scale/zero, magnitude row sum.
+__global__ void quantize_kernel(const float *__restrict__ x, GroupShape g, int64_t K, int mode,
+                                int prec, const float *__restrict__ gscale,
+                                const float *__restrict__ ginv, const int32_t *__restrict__ gzero,
+                                int16_t *__restrict__ code, float *__restrict__ rscale,
+                                int32_t *__restrict__ rzero, int32_t *__restrict__ rsum) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= g.rows) return;
+  const int64_t grp = group_of_row(g, row);
+  const float inv = ginv[grp];
+  const int32_t z = gzero[grp];
+  const float *xr = x + row * K;
+  int16_t *cr = code + row * K;
+  int acc = 0;
+  if (mode == SCMP_BIPOLAR) {
+    const int iq = (1 << (prec - 1)) - 1;
+    for (int64_t i = lane; i < K; i += 32) {
+      int q = __float2int_rn(__fmul_rn(__ldg(xr + i), inv));
+      q = max(-iq, min(iq, q));
+      cr[i] = (int16_t)(2 * q);
+      acc += 2 * abs(q);
+    }
+  } else {
+    const int iq = (1 << prec) - 1;
+    for (int64_t i = lane; i < K; i += 32) {
+      int q = __float2int_rn(__fmul_rn(__ldg(xr + i), inv)) + z;
+      q = max(0, min(iq, q));
+      cr[i] = (int16_t)q;
+      acc += q;
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    rscale[row] = gscale[grp];
+    rzero[row] = z;
+    rsum[row] = acc;
+  }
+}
+
+// ST[d][v][w]: bit j of word w = [R[d][32w+j] < v] for 32w+j < 2^p.
+__global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_dims, int prec,
+                                    uint32_t *__restrict__ table) {
+  const int T = 1 << prec;
+  const int WT = T >= 32 ? T / 32 : 1;
+  const int64_t total = (int64_t)pool_dims * (T + 1) * WT;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % WT);
+    const int v = (int)((i / WT) % (T + 1));
+    const int64_t d = i / ((int64_t)WT * (T + 1));
+    const uint8_t *R = pool + d * T;
+    uint32_t word = 0;
+    for (int j = 0; j < 32; ++j) {
+      const int t = 32 * w + j;
+      if (t < T && (int)R[t] < v) word |= 1u << j;
+    }
+    table[i] = word;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_row_stats(const float *x, int64_t rows, int64_t K, int mode, float2 *stat,
+                             cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (rows * 32 + threads - 1) / threads;
+  row_stats_kernel<<<(unsigned)blocks, threads, 0, s>>>(x, rows, K, mode, stat);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_group_stats(const float2 *stat, const GroupShape &g, int mode, int prec,
+                               float *gscale, float *ginv, int32_t *gzero, cudaStream_t s) {
+  if (g.ngroups == 0) return cudaSuccess;
+  group_stats_kernel<<<(unsigned)g.ngroups, 256, 0, s>>>(stat, g, mode, prec, gscale, ginv, gzero);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int mode, int prec,
+                            const float *gscale, const float *ginv, const int32_t *gzero,
+                            int16_t *code, float *rscale, int32_t *rzero, int32_t *rsum,
+                            cudaStream_t s) {
+  if (g.rows == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t blocks = (g.rows * 32 + threads - 1) / threads;
+  quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(x, g, K, mode, prec, gscale, ginv, gzero,
+                                                        code, rscale, rzero, rsum);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
+                                cudaStream_t s) {
+  stream_table_kernel<<<296, 256, 0, s>>>(pool, pool_dims, prec, table);
+  return cudaGetLastError();
+}
+
+}  // namespace scmp

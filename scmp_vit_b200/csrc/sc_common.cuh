@@ -1,0 +1,88 @@
+// Shared definitions of the SC matmul engine (internal; the C ABI lives in
+// include/scmp_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/scmp_b200.h"
+
+namespace scmp {
+
+constexpr int kMaxPrec = 8;
+constexpr int kMaxStream = 1 << kMaxPrec;  // 256
+
+// One operand after quantisation: signed codes sigma*c (int16, [rows, K]) and
+// per-row scale / zero point / magnitude row sum.
+struct QuantPlane {
+  const int16_t *code;
+  const float *scale;
+  const int32_t *zero;
+  const int32_t *rowsum;
+};
+
+// Scale groups are contiguous row ranges: rows are split into slices of
+// `slice_rows`, each slice into groups of `group_rows` (last one ragged).
+struct GroupShape {
+  int64_t rows;        // total rows
+  int64_t slice_rows;  // rows per slice
+  int64_t group_rows;  // rows per group (<= slice_rows)
+  int64_t groups_per_slice;
+  int64_t ngroups;
+};
+
+__host__ __device__ inline int64_t group_of_row(const GroupShape &g, int64_t r) {
+  return (r / g.slice_rows) * g.groups_per_slice + (r % g.slice_rows) / g.group_rows;
+}
+
+// Everything a GEMM engine needs after quantisation.
+struct GemmProblem {
+  QuantPlane qa, qb;
+  int64_t batch, batch_b, M, N, K;
+  int mode, prec, stoc_len;
+  const uint8_t *pool;  // [pool_dims, 2^prec]
+  int pool_dims;
+  const int32_t *row_L;    // nullable [batch*M]
+  const int32_t *slice_L;  // nullable [batch]
+  const float *bias;
+  float *out;
+  int32_t *acc_out;
+  // stream table ST[pool_dims][2^p + 1][2^p / 32] (bit t of threshold v)
+  const uint32_t *stream_table;
+};
+
+// Per-row stream length in the engine's convention (see scmp_matmul_args).
+__device__ __forceinline__ int row_stream_len(const GemmProblem &P, int64_t slice, int64_t grow) {
+  if (P.row_L) return P.row_L[grow];
+  if (P.slice_L) return P.slice_L[slice];
+  return P.stoc_len;
+}
+
+// Rescale of one accumulator (bit-exact restatement of oracle/sc_oracle.c).
+__device__ __forceinline__ float sc_rescale(int mode, int prec, int L, int32_t acc, int64_t K,
+                                            float sa, int32_t za, int32_t rsa, float sb,
+                                            int32_t zb, int32_t rsb) {
+  const float F = __fdiv_rn((float)(1u << (2 * prec)), (float)((mode == SCMP_BIPOLAR ? 4 : 1) * L));
+  if (mode == SCMP_BIPOLAR) {
+    const float fb = __fmul_rn(sb, F);
+    return __fmul_rn(__fmul_rn((float)acc, sa), fb);
+  }
+  const long long corr = (long long)za * rsb + (long long)zb * rsa - K * (long long)za * (long long)zb;
+  const float t = __fsub_rn(__fmul_rn((float)acc, F), __ll2float_rn(corr));
+  return __fmul_rn(__fmul_rn(t, sa), sb);
+}
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_row_stats(const float *x, int64_t rows, int64_t K, int mode, float2 *stat,
+                             cudaStream_t s);
+cudaError_t launch_group_stats(const float2 *stat, const GroupShape &g, int mode, int prec,
+                               float *gscale, float *ginv, int32_t *gzero, cudaStream_t s);
+cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int mode, int prec,
+                            const float *gscale, const float *ginv, const int32_t *gzero,
+                            int16_t *code, float *rscale, int32_t *rzero, int32_t *rsum,
+                            cudaStream_t s);
+cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
+                                cudaStream_t s);
+cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
+
+}  // namespace scmp

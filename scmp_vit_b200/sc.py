@@ -1,0 +1,173 @@
+"""``sc_matmul`` -- the ``scmp_kernels.sc`` entry point, on the sm_100a engine.
+
+Reference contract (the kernel package itself is not vendored; usage from
+``sc_integration/sc_linear.py:137-147``, ``cls/sc_attention_patch.py:288-291,
+314-318``, ``det/sc_patch/sc_matmul.py:187-194`` and the adapters at
+``sc_integration/sc_attention.py:39-81``):
+
+    sc_matmul(a, b, *, granularity="per_row"|"per_head"|"per_tensor",
+              mode="bipolar"|"unipolar", sc_prec, config, group_a=1,
+              group_b=1, chunk_d=0, stoc_len=None) -> fp32 tensor
+
+``a`` is ``[M, K]`` or ``[BH, M, K]``, ``b`` is ``[N, K]`` or ``[BH, N, K]``
+(a 2-D ``b`` is shared by every slice); the result is ``a @ b^T`` per slice,
+estimated by SC.  ``stoc_len=None`` means ``2**sc_prec``.  ``per_head``
+gives one scale per slice, ``per_tensor`` one per tensor, ``per_row`` one
+per ``group_*`` rows.  With ``chunk_d > 0`` the reduction index ``d`` reads
+pool row ``d % chunk_d`` of a ``(chunk_d, sc_prec)`` config.
+
+There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .config_helpers import make_sobol_simple_config, pool_table
+
+__all__ = ["sc_matmul", "device_pool", "default_config"]
+
+_POOL_LOCK = threading.Lock()
+_POOLS: dict = {}
+_DEFAULT_CFGS: dict = {}
+
+
+def default_config(D: int, sc_prec: int) -> dict:
+    """Process-wide ``(D, sc_prec)`` pool, created on first use."""
+    key = (int(D), int(sc_prec))
+    with _POOL_LOCK:
+        if key not in _DEFAULT_CFGS:
+            _DEFAULT_CFGS[key] = make_sobol_simple_config(D, D, sc_prec)
+        return _DEFAULT_CFGS[key]
+
+
+def device_pool(config: dict, device: torch.device) -> torch.Tensor:
+    """The config's pool as a uint8 device tensor, uploaded once per device."""
+    key = (config["uid"], device.index if device.index is not None else torch.cuda.current_device())
+    with _POOL_LOCK:
+        t = _POOLS.get(key)
+        if t is None:
+            tab = pool_table(config)
+            t = torch.from_numpy(tab.copy()).to(device=device, non_blocking=False)
+            _POOLS[key] = t
+        return t
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+@torch.no_grad()
+def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
+              mode: str = "bipolar", sc_prec: int = 8, config: Optional[dict] = None,
+              group_a: int = 1, group_b: int = 1, chunk_d: int = 0,
+              stoc_len: Optional[int] = None, bias: Optional[torch.Tensor] = None,
+              row_stoc_len: Optional[torch.Tensor] = None,
+              slice_stoc_len: Optional[torch.Tensor] = None,
+              out: Optional[torch.Tensor] = None,
+              acc_out: Optional[torch.Tensor] = None,
+              engine: str = "auto") -> torch.Tensor:
+    """SC estimate of ``a @ b^T`` (see module docstring).
+
+    Extra keyword arguments beyond the reference signature:
+    ``bias`` ([N], fused into the rescale), ``row_stoc_len`` (int32 per
+    a-row stream length, ``[BH*M]``; 0 = pruned row, < 0 = leave ``out``
+    row untouched), ``slice_stoc_len`` (int32 per slice), ``out``,
+    ``acc_out`` (int32 signed popcount sums, for parity checks), ``engine``.
+    """
+    if granularity not in _lib.GRANULARITY:
+        raise ValueError(f"unknown granularity {granularity!r}")
+    if mode not in _lib.MODE:
+        raise ValueError(f"unknown mode {mode!r}")
+    if engine not in _lib.ENGINE:
+        raise ValueError(f"unknown engine {engine!r}")
+    if a.dim() not in (2, 3) or b.dim() not in (2, 3):
+        raise ValueError(f"sc_matmul expects 2-D or 3-D operands, got {tuple(a.shape)} "
+                         f"and {tuple(b.shape)}")
+    if not a.is_cuda or not b.is_cuda:
+        raise RuntimeError("sc_matmul runs on the CUDA engine only (no CPU path); "
+                           f"got devices {a.device} and {b.device}")
+    if a.device != b.device:
+        raise ValueError(f"operands on different devices: {a.device} vs {b.device}")
+    batched = a.dim() == 3
+    a3 = a if batched else a.unsqueeze(0)
+    b3 = b if b.dim() == 3 else b.unsqueeze(0)
+    BH, M, K = a3.shape
+    BHb, N, Kb = b3.shape
+    if Kb != K:
+        raise ValueError(f"inner-dim mismatch: a K={K}, b K={Kb}")
+    if BHb not in (1, BH):
+        raise ValueError(f"b batch {BHb} must be 1 or {BH}")
+    p = int(sc_prec)
+    L = int(stoc_len) if stoc_len is not None else (1 << p)
+    if config is None:
+        config = default_config(chunk_d if chunk_d > 0 else K, p)
+    if int(config["sc_prec"]) != p:
+        raise ValueError(f"config sc_prec={config['sc_prec']} != sc_prec={p}")
+    dims = int(config["dims"])
+    if chunk_d and chunk_d > 0:
+        pool_dims = min(int(chunk_d), dims)
+    else:
+        if dims < K:
+            raise ValueError(f"config has {dims} stream dims < K={K}; pass chunk_d")
+        pool_dims = K
+    dev = a.device
+    a3 = a3.float().contiguous()
+    b3 = b3.float().contiguous()
+    if out is None:
+        out = torch.empty(BH, M, N, dtype=torch.float32, device=dev)
+    else:
+        out = out.view(BH, M, N)
+        if out.dtype != torch.float32 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 tensor")
+    if acc_out is not None:
+        if acc_out.dtype != torch.int32 or acc_out.numel() != BH * M * N or not acc_out.is_contiguous():
+            raise ValueError("acc_out must be a contiguous int32 tensor of BH*M*N elements")
+    if bias is not None:
+        bias = bias.to(device=dev, dtype=torch.float32).contiguous()
+        if bias.numel() != N:
+            raise ValueError(f"bias has {bias.numel()} elements, expected {N}")
+    if row_stoc_len is not None:
+        row_stoc_len = row_stoc_len.to(device=dev, dtype=torch.int32).contiguous()
+        if row_stoc_len.numel() != BH * M:
+            raise ValueError("row_stoc_len needs BH*M entries")
+    if slice_stoc_len is not None:
+        slice_stoc_len = slice_stoc_len.to(device=dev, dtype=torch.int32).contiguous()
+        if slice_stoc_len.numel() != BH:
+            raise ValueError("slice_stoc_len needs BH entries")
+    pool = device_pool(config, dev)
+
+    args = _lib.MatmulArgs()
+    args.abi_version = _lib.ABI_VERSION
+    args.engine = _lib.ENGINE[engine]
+    args.a = a3.data_ptr()
+    args.b = b3.data_ptr()
+    args.batch, args.batch_b, args.M, args.N, args.K = BH, BHb, M, N, K
+    args.granularity = _lib.GRANULARITY[granularity]
+    args.mode = _lib.MODE[mode]
+    args.sc_prec = p
+    args.stoc_len = L
+    args.group_a = max(int(group_a), 1)
+    args.group_b = max(int(group_b), 1)
+    args.pool = pool.data_ptr()
+    args.pool_dims = pool_dims
+    args.row_stoc_len = _ptr(row_stoc_len)
+    args.slice_stoc_len = _ptr(slice_stoc_len)
+    args.bias = _ptr(bias)
+    args.out = out.data_ptr()
+    args.acc_out = _ptr(acc_out)
+    lib = _lib.load()
+    nbytes = lib.scmp_sc_matmul_workspace_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(lib.scmp_sc_matmul(ctypes.byref(args), None))  # raises with the reason
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    args.workspace = ws.data_ptr()
+    args.workspace_bytes = nbytes
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(lib.scmp_sc_matmul(ctypes.byref(args), ctypes.c_void_p(stream)))
+    return out if batched else out[0]
