@@ -20,6 +20,8 @@
  *                            instead of one per level)
  *   slice_stoc_len field  <- the per-head bucket loop of
  *                            cls/sc_attention_patch.py:168-197
+ *   k_segment field       <- 16 per-head launches on 16 streams of
+ *                            sc_integration/head_aligned_comp.py:113-144
  *   scmp_sc_matmul_workspace_size: sizing helper (no reference counterpart;
  *                            the Triton package allocated internally)
  */
@@ -71,6 +73,13 @@ typedef struct scmp_matmul_args {
   int32_t sc_prec;          /* p in [1, 8] (bipolar needs p >= 2) */
   int32_t stoc_len;         /* L in [1, 2^p]; used when no per-row table */
   int64_t group_a, group_b; /* per_row: rows per scale group (>= 1) */
+  /* > 0: split K into K / k_segment segments (K % k_segment == 0, per_row
+   * with group 1 only).  Each segment is quantised per row on its own and
+   * rescaled on its own; the fp32 segment results are summed in segment
+   * order, then the bias is added -- the head-aligned compensation of
+   * sc_integration/head_aligned_comp.py:113-144 and the chunk-D summation of
+   * sc_integration/sc_attention.py:337-376 in one launch.  0 = one segment. */
+  int64_t k_segment;
   const uint8_t *pool;      /* stream pool R [pool_dims, 2^p] (uint8) */
   int32_t pool_dims;        /* reduction index d reads pool row d % pool_dims */
   int32_t reserved0;
@@ -102,6 +111,18 @@ SCMP_API const char *scmp_last_error(void);
 
 /* SCMP_ABI_VERSION of the loaded library. */
 SCMP_API int scmp_abi_version(void);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * threads, all devices).  Instrumentation for launch accounting; no
+ * reference counterpart. */
+SCMP_API uint64_t scmp_kernel_launches(void);
+
+/* Roofline probe (synchronous; allocates a small scratch buffer): runs a
+ * register-only loop of one instruction class on every SM of the current
+ * device and returns its rate.  kind 0 = LOP3+POPC (bit-products/s),
+ * 1 = mma.sync b1 AND.POPC (bit-products/s), 2 = mma.sync s8 (MACs/s).
+ * Instrumentation only; no reference counterpart. */
+SCMP_API int scmp_probe_int_peak(int kind, double *ops_per_second);
 
 #ifdef __cplusplus
 }

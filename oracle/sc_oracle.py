@@ -257,5 +257,31 @@ def sc_matmul_rows_ref(a, b, row_L, pools: dict, *, mode="bipolar", bias=None,
     return acc, y
 
 
+def sc_matmul_segments_ref(a, b, k_segment: int, *, mode="bipolar", sc_prec=8, pool=None,
+                           stoc_len=None, bias=None, L_row=None, nthreads: int = 0):
+    """Segmented K (head-aligned compensation, chunk-D summation): each
+    segment is a per-row SC matmul with pool rows ``0..k_segment-1``; the fp32
+    results are summed in segment order (reference
+    ``sc_integration/head_aligned_comp.py:128-144``), then the bias is added.
+    Returns (sum of segment accumulators, y)."""
+    a3, b3 = _as3(a), _as3(b)
+    K = a3.shape[-1]
+    if K % k_segment:
+        raise ValueError("k_segment must divide K")
+    acc_tot, y = None, None
+    for s0 in range(0, K, k_segment):
+        acc_s, y_s = sc_matmul_ref(a3[..., s0:s0 + k_segment], b3[..., s0:s0 + k_segment],
+                                   mode=mode, sc_prec=sc_prec, pool=pool, pool_dims=k_segment,
+                                   stoc_len=stoc_len, L_row=L_row, nthreads=nthreads)
+        if y is None:
+            acc_tot, y = acc_s.astype(np.int64), y_s
+        else:
+            acc_tot += acc_s
+            y = (y + y_s).astype(np.float32)
+    if bias is not None:
+        y = (y + np.asarray(bias, dtype=np.float32)[None, None, :]).astype(np.float32)
+    return acc_tot.astype(np.int32), y
+
+
 def num_threads() -> int:
     return int(lib().sco_num_threads())

@@ -27,6 +27,8 @@ EXPORTED_SYMBOLS = (
     "scmp_sc_matmul",
     "scmp_last_error",
     "scmp_abi_version",
+    "scmp_kernel_launches",
+    "scmp_probe_int_peak",
 )
 
 
@@ -48,6 +50,7 @@ class MatmulArgs(ctypes.Structure):
         ("stoc_len", ctypes.c_int32),
         ("group_a", ctypes.c_int64),
         ("group_b", ctypes.c_int64),
+        ("k_segment", ctypes.c_int64),
         ("pool", ctypes.c_void_p),
         ("pool_dims", ctypes.c_int32),
         ("reserved0", ctypes.c_int32),
@@ -95,11 +98,29 @@ def load() -> ctypes.CDLL:
         lib.scmp_last_error.restype = ctypes.c_char_p
         lib.scmp_abi_version.argtypes = []
         lib.scmp_abi_version.restype = ctypes.c_int
+        lib.scmp_kernel_launches.argtypes = []
+        lib.scmp_kernel_launches.restype = ctypes.c_uint64
+        lib.scmp_probe_int_peak.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+        lib.scmp_probe_int_peak.restype = ctypes.c_int
         if lib.scmp_abi_version() != ABI_VERSION:
             raise RuntimeError(
                 f"engine ABI {lib.scmp_abi_version()} != expected {ABI_VERSION}")
         _lib = lib
         return lib
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the engine library so far in this process."""
+    return int(load().scmp_kernel_launches())
+
+
+def probe_int_peak(kind: int) -> float:
+    """Measured rate of one integer instruction class on the current device
+    (0: LOP3+POPC bit-products/s, 1: mma.sync b1 bit-products/s,
+    2: mma.sync s8 MACs/s)."""
+    v = ctypes.c_double(0.0)
+    check(load().scmp_probe_int_peak(int(kind), ctypes.byref(v)))
+    return float(v.value)
 
 
 def last_error() -> str:

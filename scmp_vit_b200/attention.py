@@ -1,0 +1,279 @@
+"""SC attention core: Q@K^T and Attn@V on the engine, batched over (batch, head).
+
+Mirrors the reference's DINOv2 patch (``cls/sc_attention_patch.py:51-328``)
+and EVA ``SCMatMul`` (``det/sc_patch/sc_matmul.py:67-195``) with the same
+numerics per slice, but without their host loops:
+
+* Q@K^T: one ``per_head`` launch over all B*H slices (one scale per slice).
+  Per-head MP (``_classify_per_head``: metric ``|q|.amax((0,2,3))``) becomes
+  a per-slice stream-length table, one launch per precision.
+* Attn@V: one ``per_row`` launch over all B*H slices instead of the
+  reference's B*H Python loop (``cls/sc_attention_patch.py:311-318``).
+  Per-row MP (entropy / amax / ipr metric, ``:75-140``) is classified for
+  every slice at once and becomes a per-row stream-length table.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.nn as nn
+
+from . import sc_linear as _scl
+from .mp import (
+    AdaptiveMPConfig,
+    AutoMPBudgetLogger,
+    MPConfig,
+    adaptive_classify_rows,
+    classify_rows_by_metric,
+    get_current_block_idx,
+    quantile_levels_batched,
+)
+from .mp_linear import sc_prec_for_stoc_len
+from .noise_matmul import _noisy_matmul_core
+from .sc import sc_matmul
+
+CfgFor = Callable[[int, int], dict]
+
+AV_METRIC_REVERSE = False
+AV_METRIC_KIND = "entropy"  # "amax" | "entropy" | "ipr"
+
+
+def set_av_metric_reverse(flag: bool):
+    global AV_METRIC_REVERSE
+    AV_METRIC_REVERSE = bool(flag)
+
+
+def set_av_metric_kind(kind: str):
+    global AV_METRIC_KIND
+    if kind not in ("amax", "entropy", "ipr"):
+        raise ValueError(f"unknown AV metric: {kind}")
+    AV_METRIC_KIND = kind
+
+
+def av_row_score(attn: torch.Tensor) -> torch.Tensor:
+    """Per-row score over the last dim, higher = needs more precision
+    (reference ``cls/sc_attention_patch.py:106-126``)."""
+    if AV_METRIC_KIND == "amax":
+        m = attn.amax(-1)
+        return -m if AV_METRIC_REVERSE else m
+    if AV_METRIC_KIND == "entropy":
+        return -(attn * attn.clamp(min=1e-9).log()).sum(-1)
+    return 1.0 / (attn.pow(2).sum(-1) + 1e-9)
+
+
+def _levels_by_prec(levels):
+    by_prec: dict[int, list[int]] = {}
+    for L in sorted({int(v) for v in levels if int(v) > 0}):
+        by_prec.setdefault(sc_prec_for_stoc_len(L), []).append(L)
+    return by_prec
+
+
+def _run_levels(a, b, table: torch.Tensor, levels, per: str, *, granularity: str, mode: str,
+                D_pool: int, cfg_for: CfgFor, out: torch.Tensor) -> torch.Tensor:
+    """One engine launch per precision among ``levels``; ``table`` holds the
+    stream length per slice (``per='slice'``) or per row (``per='row'``)."""
+    by_prec = _levels_by_prec(levels)
+    if not by_prec:
+        return out.zero_()
+    first = True
+    for p, Ls in by_prec.items():
+        mask = torch.zeros_like(table, dtype=torch.bool)
+        for L in Ls:
+            mask |= table == L
+        if first:
+            mask |= table <= 0
+        sel = torch.where(mask, table.clamp(min=0), torch.full_like(table, -1))
+        kw = {"slice_stoc_len": sel} if per == "slice" else {"row_stoc_len": sel}
+        sc_matmul(a, b, granularity=granularity, mode=mode, sc_prec=p,
+                  config=cfg_for(D_pool, p), out=out, **kw)
+        first = False
+    return out
+
+
+def sc_qk(q: torch.Tensor, k: torch.Tensor, sc_prec: int, *, mp_cfg=None,
+          cfg_for: Optional[CfgFor] = None) -> torch.Tensor:
+    """SC ``q @ k^T`` for q, k ``[B, H, N, D]`` -> ``[B, H, N, N]`` fp32, unscaled."""
+    cfg_for = cfg_for or _scl._get_config
+    B, H, N, D = q.shape
+    qf = q.float().reshape(B * H, N, D)
+    kf = k.float().reshape(B * H, N, D)
+    if mp_cfg is None:
+        if _scl.USE_NOISE_MODEL:
+            return _noisy_matmul_core(q.float(), k.float(), L=2 ** sc_prec, mode="bipolar")
+        out = sc_matmul(qf, kf, granularity="per_head", sc_prec=sc_prec,
+                        config=cfg_for(D, sc_prec), stoc_len=2 ** sc_prec)
+        return out.reshape(B, H, N, N)
+    metric = q.float().abs().amax(dim=(0, 2, 3))  # per head
+    if isinstance(mp_cfg, AdaptiveMPConfig):
+        t, T = _scl.get_vit_timestep()
+        head_L = adaptive_classify_rows(metric, t, T, mp_cfg, operator="qk").row_levels
+    else:
+        head_L = classify_rows_by_metric(metric, mp_cfg.stoc_len_levels,
+                                         mp_cfg.level_fractions).row_levels
+    if AutoMPBudgetLogger.enabled:
+        maxL = max(int(v) for v in mp_cfg.stoc_len_levels)
+        AutoMPBudgetLogger.record(get_current_block_idx(), "qk", B * H * N * N * maxL,
+                                  head_L.clamp(min=0).to(torch.float64).sum() * B * N * N)
+    slice_L = head_L.to(torch.int32).repeat(B)  # slice b*H + h -> head h
+    out = torch.empty(B * H, N, N, dtype=torch.float32, device=q.device)
+    if _scl.USE_NOISE_MODEL:
+        for L in sorted({int(v) for v in mp_cfg.stoc_len_levels}):
+            sel = slice_L == L
+            if L > 0 and bool(sel.any()):
+                out[sel] = _noisy_matmul_core(qf[sel], kf[sel], L=L, mode="bipolar")
+            elif L <= 0:
+                out[sel] = 0.0
+        return out.reshape(B, H, N, N)
+    _run_levels(qf, kf, slice_L, mp_cfg.stoc_len_levels, "slice", granularity="per_head",
+                mode="bipolar", D_pool=D, cfg_for=cfg_for, out=out)
+    return out.reshape(B, H, N, N)
+
+
+def sc_av(attn: torch.Tensor, v: torch.Tensor, sc_prec: int, *, mode: str = "bipolar",
+          mp_cfg=None, cfg_for: Optional[CfgFor] = None) -> torch.Tensor:
+    """SC ``attn @ v`` for attn ``[B, H, N, N]``, v ``[B, H, N, D]`` ->
+    ``[B, H, N, D]`` fp32; per-row scales for attn rows and v columns."""
+    cfg_for = cfg_for or _scl._get_config
+    B, H, N, D = v.shape
+    a_flat = attn.float().reshape(B * H, N, N)
+    b_flat = v.float().transpose(-1, -2).reshape(B * H, D, N)
+    if mp_cfg is None:
+        if _scl.USE_NOISE_MODEL:
+            out = _noisy_matmul_core(a_flat, b_flat, L=2 ** sc_prec, mode=mode, per_row_scale=True)
+        else:
+            out = sc_matmul(a_flat, b_flat, granularity="per_row", group_a=1, group_b=1,
+                            mode=mode, sc_prec=sc_prec, config=cfg_for(N, sc_prec))
+        return out.reshape(B, H, N, D)
+    score = av_row_score(a_flat)  # [BH, N]
+    if isinstance(mp_cfg, AdaptiveMPConfig):
+        t, T = _scl.get_vit_timestep()
+        rows = [adaptive_classify_rows(score[i], t, T, mp_cfg, operator="av").row_levels
+                for i in range(B * H)]
+        row_L = torch.stack(rows)
+    else:
+        row_L = quantile_levels_batched(score, mp_cfg.stoc_len_levels, mp_cfg.level_fractions)
+    row_L = row_L.reshape(-1).to(torch.int32)
+    if AutoMPBudgetLogger.enabled:
+        maxL = max(int(x) for x in mp_cfg.stoc_len_levels)
+        AutoMPBudgetLogger.record(get_current_block_idx(), "av", B * H * N * D * maxL,
+                                  row_L.clamp(min=0).to(torch.float64).sum() * D)
+    out = torch.empty(B * H, N, D, dtype=torch.float32, device=v.device)
+    if _scl.USE_NOISE_MODEL:
+        out.zero_()
+        flat_a = a_flat.reshape(B * H * N, N)
+        for L in sorted({int(x) for x in mp_cfg.stoc_len_levels if int(x) > 0}):
+            sel = (row_L == L).reshape(B * H, N)
+            for i in range(B * H):
+                r = sel[i]
+                if bool(r.any()):
+                    out[i, r] = _noisy_matmul_core(a_flat[i][r], b_flat[i], L=L, mode=mode,
+                                                   per_row_scale=True)
+        del flat_a
+        return out.reshape(B, H, N, D)
+    _run_levels(a_flat, b_flat, row_L, mp_cfg.stoc_len_levels, "row", granularity="per_row",
+                mode=mode, D_pool=N, cfg_for=cfg_for, out=out)
+    return out.reshape(B, H, N, D)
+
+
+def make_sc_attention_forward(sc_prec: int, sc_av: bool, sc_qk: bool = True,
+                              qk_mp_cfg: MPConfig | None = None,
+                              av_mp_cfg: MPConfig | None = None, *,
+                              av_mode: str = "bipolar", cfg_for: Optional[CfgFor] = None):
+    """``forward(self, x)`` for a DINOv2-style attention module with
+    ``qkv``, ``proj``, ``proj_drop``, ``num_heads``, ``scale`` attributes
+    (same signature and numerics as ``cls/sc_attention_patch.py:248-328``)."""
+    do_av = sc_av
+
+    def forward(self, x, attn_bias=None):
+        B, N, C = x.shape
+        H = self.num_heads
+        D = C // H
+        qkv = self.qkv(x).reshape(B, N, 3, H, D)
+        q, k, v = torch.unbind(qkv, 2)
+        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        if sc_qk:
+            attn = sc_qk_fn(q, k, sc_prec, mp_cfg=qk_mp_cfg, cfg_for=cfg_for)
+            attn = attn.to(x.dtype) * self.scale
+        else:
+            attn = (q @ k.transpose(-2, -1)) * self.scale
+        attn = attn.softmax(dim=-1)
+        if do_av:
+            out = sc_av_fn(attn, v, sc_prec, mode=av_mode, mp_cfg=av_mp_cfg,
+                           cfg_for=cfg_for).to(x.dtype)
+        else:
+            out = attn @ v
+        out = out.transpose(1, 2).reshape(B, N, C)
+        out = self.proj(out)
+        return self.proj_drop(out)
+
+    return forward
+
+
+sc_qk_fn = sc_qk
+sc_av_fn = sc_av
+
+
+class SCMatMul(nn.Module):
+    """EVA ``MatMul`` replacement: ``A @ B`` (``A (..., M, K)``, ``B (..., K, N)``)
+    through SC in one batched launch (reference ``det/sc_patch/sc_matmul.py``)."""
+
+    def __init__(self, sc_prec: int = 8, mode: str = "bipolar", mp_cfg=None,
+                 adaptive_mp_cfg=None, op: str | None = None, stoc_len: int | None = None):
+        super().__init__()
+        if mode not in ("bipolar", "unipolar"):
+            raise ValueError(mode)
+        self.sc_prec = sc_prec
+        self.stoc_len = stoc_len
+        self.mode = mode
+        self.mp_cfg = mp_cfg
+        self.adaptive_mp_cfg = adaptive_mp_cfg
+        self.op = op
+
+    def _mp(self):
+        return self.adaptive_mp_cfg or self.mp_cfg
+
+    def forward(self, A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+        if A.dim() < 2 or B.dim() < 2:
+            raise ValueError(f"SCMatMul expects >=2-D, got A={tuple(A.shape)} B={tuple(B.shape)}")
+        if A.shape[-1] != B.shape[-2]:
+            raise ValueError(f"Inner-dim mismatch: A.shape[-1]={A.shape[-1]} "
+                             f"B.shape[-2]={B.shape[-2]}")
+        M, K = A.shape[-2], A.shape[-1]
+        N = B.shape[-1]
+        lead = A.shape[:-2]
+        if B.shape[:-2] != lead:
+            B = B.expand(*lead, K, N)
+        A_flat = A.reshape(-1, M, K).float().contiguous()
+        B_rm = B.reshape(-1, K, N).float().transpose(1, 2).contiguous()  # (BH, N, K)
+        BH = A_flat.shape[0]
+        cfg = self._mp()
+        out = torch.empty(BH, M, N, dtype=torch.float32, device=A.device)
+        if cfg is not None and self.op == "qk":
+            metric = A_flat.abs().amax(dim=(1, 2))
+            if isinstance(cfg, AdaptiveMPConfig):
+                t, T = _scl.get_vit_timestep()
+                sl = adaptive_classify_rows(metric, t, T, cfg, operator="qk").row_levels
+            else:
+                sl = classify_rows_by_metric(metric, cfg.stoc_len_levels,
+                                             cfg.level_fractions).row_levels
+            _run_levels(A_flat, B_rm, sl.to(torch.int32), cfg.stoc_len_levels, "slice",
+                        granularity="per_row", mode=self.mode, D_pool=K,
+                        cfg_for=_scl._get_config, out=out)
+        elif cfg is not None and self.op == "av":
+            row_max = A_flat.amax(dim=-1)  # (BH, M)
+            if isinstance(cfg, AdaptiveMPConfig):
+                t, T = _scl.get_vit_timestep()
+                rl = torch.stack([adaptive_classify_rows(row_max[i], t, T, cfg,
+                                                         operator="av").row_levels
+                                  for i in range(BH)])
+            else:
+                rl = quantile_levels_batched(row_max, cfg.stoc_len_levels, cfg.level_fractions)
+            _run_levels(A_flat, B_rm, rl.reshape(-1).to(torch.int32), cfg.stoc_len_levels,
+                        "row", granularity="per_row", mode=self.mode, D_pool=K,
+                        cfg_for=_scl._get_config, out=out)
+        else:
+            sc_matmul(A_flat, B_rm, granularity="per_row", group_a=1, group_b=1, mode=self.mode,
+                      sc_prec=self.sc_prec, config=_scl._get_config(K, self.sc_prec),
+                      stoc_len=self.stoc_len, out=out)
+        return out.reshape(*lead, M, N).to(A.dtype)

@@ -1,4 +1,5 @@
 // C ABI of the SC matmul engine (declared in include/scmp_b200.h).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -10,6 +11,9 @@ namespace scmp {
 namespace {
 
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+inline void count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char *fmt, ...) {
@@ -102,19 +106,32 @@ int validate(const scmp_matmul_args *x) {
   if (x->granularity == SCMP_PER_ROW && (x->group_a < 1 || x->group_b < 1))
     return fail(SCMP_EINVAL, "group_a/group_b must be >= 1");
   if (x->pool_dims <= 0) return fail(SCMP_EINVAL, "pool_dims must be positive");
+  if (x->k_segment < 0) return fail(SCMP_EINVAL, "k_segment must be >= 0");
+  if (x->k_segment > 0) {
+    if (x->K % x->k_segment != 0)
+      return fail(SCMP_EINVAL, "k_segment=%lld must divide K=%lld", (long long)x->k_segment,
+                  (long long)x->K);
+    if (x->k_segment != x->K &&
+        (x->granularity != SCMP_PER_ROW || x->group_a != 1 || x->group_b != 1))
+      return fail(SCMP_EINVAL, "k_segment needs granularity per_row with group_a=group_b=1");
+  }
   if (x->engine != SCMP_ENGINE_AUTO && x->engine != SCMP_ENGINE_POPC &&
       x->engine != SCMP_ENGINE_TCGEN05)
     return fail(SCMP_EINVAL, "unknown engine %d", x->engine);
   return SCMP_OK;
 }
 
+int64_t seg_len(const scmp_matmul_args *x) { return x->k_segment > 0 ? x->k_segment : x->K; }
+
 Plan make_plan(const scmp_matmul_args *x) {
   Plan p;
   Carver c;
-  p.A.g = make_groups(x->granularity, x->batch, x->M, x->group_a);
-  p.B.g = make_groups(x->granularity, x->batch_b, x->N, x->group_b);
-  layout_operand(c, p.A, x->K);
-  layout_operand(c, p.B, x->K);
+  // Segmented K is quantised as [rows * nseg, kseg] with one group per row.
+  const int64_t kseg = seg_len(x), nseg = x->K / kseg;
+  p.A.g = make_groups(x->granularity, x->batch, x->M * nseg, nseg > 1 ? 1 : x->group_a);
+  p.B.g = make_groups(x->granularity, x->batch_b, x->N * nseg, nseg > 1 ? 1 : x->group_b);
+  layout_operand(c, p.A, kseg);
+  layout_operand(c, p.B, kseg);
   const int T = 1 << x->sc_prec;
   const int WT = T >= 32 ? T / 32 : 1;
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
@@ -139,6 +156,7 @@ int quantize_operand(const float *x, const OperandLayout &o, int64_t K, int mode
                            reinterpret_cast<int32_t *>(ws + o.rzero),
                            reinterpret_cast<int32_t *>(ws + o.rsum), s)) != cudaSuccess)
     return cuda_fail(e, "quantize launch");
+  if (o.g.rows > 0) count_launches(3);
   return SCMP_OK;
 }
 
@@ -161,6 +179,8 @@ extern "C" {
 const char *scmp_last_error(void) { return g_last_error.c_str(); }
 
 int scmp_abi_version(void) { return SCMP_ABI_VERSION; }
+
+uint64_t scmp_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args) {
   if (validate(args) != SCMP_OK) return 0;
@@ -185,11 +205,13 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   auto *ws = static_cast<unsigned char *>(x.workspace);
   auto s = static_cast<cudaStream_t>(stream);
 
-  if ((rc = quantize_operand(x.a, plan.A, x.K, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
-  if ((rc = quantize_operand(x.b, plan.B, x.K, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
+  const int64_t kseg = seg_len(&x);
+  if ((rc = quantize_operand(x.a, plan.A, kseg, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
+  if ((rc = quantize_operand(x.b, plan.B, kseg, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
   auto *table = reinterpret_cast<uint32_t *>(ws + plan.table);
   cudaError_t e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table, s);
   if (e != cudaSuccess) return cuda_fail(e, "stream_table launch");
+  count_launches(1);
 
   GemmProblem P{};
   P.qa = plane_of(plan.A, ws);
@@ -199,6 +221,8 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.M = x.M;
   P.N = x.N;
   P.K = x.K;
+  P.kseg = kseg;
+  P.nseg = (int)(x.K / kseg);
   P.mode = x.mode;
   P.prec = x.sc_prec;
   P.stoc_len = x.stoc_len;
@@ -211,6 +235,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.acc_out = x.acc_out;
   P.stream_table = table;
   if ((e = launch_gemm_popc(P, s)) != cudaSuccess) return cuda_fail(e, "gemm_popc launch");
+  count_launches(1);
   return SCMP_OK;
 }
 

@@ -40,11 +40,12 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
   const int T = 1 << P.prec;
   const int WT = T >= 32 ? T / 32 : 1;
 
-  int32_t acc[4][4];
+  int32_t acc[4][4], acc_sum[4][4];
+  float y[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0;
+    for (int j = 0; j < 4; ++j) { acc[i][j] = 0; acc_sum[i][j] = 0; y[i][j] = 0.0f; }
 
   for (int64_t d0 = 0; d0 < P.K; d0 += BD) {
     // ---- stage A: enable windows (prefix masks) and signs
@@ -89,7 +90,6 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
     }
     __syncthreads();
     // ---- popcount inner product
-#pragma unroll 2
     for (int dd = 0; dd < BD; ++dd) {
       uint32_t a[4][LW], b[4][LW];
       int sa[4], sb[4];
@@ -111,11 +111,37 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
           for (int w = 0; w < LW; ++w) cnt += __popc(a[i][w] & b[j][w]);
           acc[i][j] += (sa[i] * sb[j]) * cnt;
         }
+      // ---- end of a segment: rescale it and add it to the fp32 sum
+      const int64_t d = d0 + dd;
+      if (d < P.K && (d + 1) % P.kseg == 0) {
+        const int64_t seg = d / P.kseg;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int64_t gm = m0 + ty + 16 * i;
+          if (gm >= P.M) continue;
+          const int64_t grow = slice * P.M + gm;
+          const int L = row_stream_len(P, slice, grow);
+          const int64_t ra = grow * P.nseg + seg;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int64_t gn = n0 + tx + 16 * j;
+            if (gn < P.N && L > 0) {
+              const int64_t rb = (slice_b * P.N + gn) * P.nseg + seg;
+              const float r = sc_rescale(P.mode, P.prec, L, acc[i][j], P.kseg, P.qa.scale[ra],
+                                         P.qa.zero[ra], P.qa.rowsum[ra], P.qb.scale[rb],
+                                         P.qb.zero[rb], P.qb.rowsum[rb]);
+              y[i][j] = seg == 0 ? r : __fadd_rn(y[i][j], r);
+              acc_sum[i][j] += acc[i][j];
+            }
+            acc[i][j] = 0;
+          }
+        }
+      }
     }
     __syncthreads();
   }
 
-  // ---- epilogue: rescale, bias, store
+  // ---- epilogue: bias, store
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t gm = m0 + ty + 16 * i;
@@ -123,22 +149,15 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
     const int64_t grow = slice * P.M + gm;
     const int L = row_stream_len(P, slice, grow);
     if (L < 0) continue;
-    const float sa = P.qa.scale[grow];
-    const int32_t za = P.qa.zero[grow], rsa = P.qa.rowsum[grow];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t gn = n0 + tx + 16 * j;
       if (gn >= P.N) continue;
-      const int64_t brow = slice_b * P.N + gn;
-      float y = 0.0f;
-      const int32_t a = L > 0 ? acc[i][j] : 0;
-      if (L > 0)
-        y = sc_rescale(P.mode, P.prec, L, a, P.K, sa, za, rsa, P.qb.scale[brow], P.qb.zero[brow],
-                       P.qb.rowsum[brow]);
-      if (P.bias) y = __fadd_rn(y, P.bias[gn]);
+      float v = L > 0 ? y[i][j] : 0.0f;
+      if (P.bias) v = __fadd_rn(v, P.bias[gn]);
       const int64_t o = grow * P.N + gn;
-      P.out[o] = y;
-      if (P.acc_out) P.acc_out[o] = a;
+      P.out[o] = v;
+      if (P.acc_out) P.acc_out[o] = L > 0 ? acc_sum[i][j] : 0;
     }
   }
 }

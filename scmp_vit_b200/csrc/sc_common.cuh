@@ -39,6 +39,8 @@ __host__ __device__ inline int64_t group_of_row(const GroupShape &g, int64_t r) 
 struct GemmProblem {
   QuantPlane qa, qb;
   int64_t batch, batch_b, M, N, K;
+  int64_t kseg;  // segment length (K when unsegmented); per-(row, segment) scales
+  int nseg;      // K / kseg
   int mode, prec, stoc_len;
   const uint8_t *pool;  // [pool_dims, 2^prec]
   int pool_dims;

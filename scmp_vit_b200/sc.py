@@ -70,6 +70,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
               slice_stoc_len: Optional[torch.Tensor] = None,
               out: Optional[torch.Tensor] = None,
               acc_out: Optional[torch.Tensor] = None,
+              k_segment: int = 0,
               engine: str = "auto") -> torch.Tensor:
     """SC estimate of ``a @ b^T`` (see module docstring).
 
@@ -77,7 +78,15 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     ``bias`` ([N], fused into the rescale), ``row_stoc_len`` (int32 per
     a-row stream length, ``[BH*M]``; 0 = pruned row, < 0 = leave ``out``
     row untouched), ``slice_stoc_len`` (int32 per slice), ``out``,
-    ``acc_out`` (int32 signed popcount sums, for parity checks), ``engine``.
+    ``acc_out`` (int32 signed popcount sums, for parity checks),
+    ``k_segment`` (split K into equal segments, each quantised and rescaled
+    on its own, fp32 results summed in order), ``engine``.
+
+    ``chunk_d > 0`` (bipolar, ``K > chunk_d``) runs the chunked form of the
+    reference's chunk-D summation (``sc_integration/sc_attention.py:337-376``):
+    ``k_segment = chunk_d`` with the ``(chunk_d, sc_prec)`` pool reused by
+    every chunk; a ragged last chunk is zero-padded, which leaves bipolar
+    scales and counts unchanged.
     """
     if granularity not in _lib.GRANULARITY:
         raise ValueError(f"unknown granularity {granularity!r}")
@@ -109,15 +118,32 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     if int(config["sc_prec"]) != p:
         raise ValueError(f"config sc_prec={config['sc_prec']} != sc_prec={p}")
     dims = int(config["dims"])
-    if chunk_d and chunk_d > 0:
-        pool_dims = min(int(chunk_d), dims)
-    else:
-        if dims < K:
-            raise ValueError(f"config has {dims} stream dims < K={K}; pass chunk_d")
-        pool_dims = K
     dev = a.device
     a3 = a3.float().contiguous()
     b3 = b3.float().contiguous()
+    if chunk_d and 0 < int(chunk_d) < K and mode == "bipolar":
+        chunk_d = int(chunk_d)
+        if dims < chunk_d:
+            raise ValueError(f"config has {dims} stream dims < chunk_d={chunk_d}")
+        pad = (-K) % chunk_d
+        if pad:
+            a3 = torch.nn.functional.pad(a3, (0, pad))
+            b3 = torch.nn.functional.pad(b3, (0, pad))
+            K += pad
+        k_segment = chunk_d
+        pool_dims = chunk_d
+    elif k_segment and int(k_segment) > 0:
+        k_segment = int(k_segment)
+        if K % k_segment:
+            raise ValueError(f"k_segment={k_segment} must divide K={K}")
+        if dims < k_segment:
+            raise ValueError(f"config has {dims} stream dims < k_segment={k_segment}")
+        pool_dims = k_segment
+    else:
+        k_segment = 0
+        if dims < K:
+            raise ValueError(f"config has {dims} stream dims < K={K}; pass chunk_d")
+        pool_dims = K
     if out is None:
         out = torch.empty(BH, M, N, dtype=torch.float32, device=dev)
     else:
@@ -153,6 +179,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     args.stoc_len = L
     args.group_a = max(int(group_a), 1)
     args.group_b = max(int(group_b), 1)
+    args.k_segment = k_segment
     args.pool = pool.data_ptr()
     args.pool_dims = pool_dims
     args.row_stoc_len = _ptr(row_stoc_len)

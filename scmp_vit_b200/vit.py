@@ -1,0 +1,233 @@
+"""DINOv2-style ViT-L/14 with a linear head, and the SC patcher the benchmark
+uses.
+
+The model carries the attribute names the reference's patchers rely on
+(``cls/sc_attention_patch.py:335-341,459-636``): ``backbone.blocks[i].attn``
+with ``qkv``, ``proj``, ``proj_drop``, ``num_heads``, ``scale``; an ``Mlp``
+class with ``fc1`` / ``fc2``; and a 1000-way head on the concatenation of the
+CLS token and the mean patch token (2048 -> 1000).  Weights are random
+(seeded); there are no checkpoints in this environment.
+
+``patch_vit`` installs the SC operators per block: ``qkv_proj`` /
+``out_proj`` / ``mlp_fc1`` / ``mlp_fc2`` as ``SCLinear``, Q@K^T and Attn@V
+through the batched attention core, optional per-block pools (e.g. an
+LFSR-16 pool seeded per block) and optional head-aligned compensation
+``out = block(x) + comp(x)``.
+"""
+from __future__ import annotations
+
+from typing import Callable, Dict, Iterable, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .attention import make_sc_attention_forward
+from .head_aligned_comp import HeadAlignedSCLinear
+from .mp import SeededRandomMPConfig, set_current_block_idx
+from .sc_linear import SCLinear, _get_config, sc_linear_rows
+
+
+class Mlp(nn.Module):
+    def __init__(self, dim: int, hidden: int):
+        super().__init__()
+        self.fc1 = nn.Linear(dim, hidden)
+        self.act = nn.GELU()
+        self.fc2 = nn.Linear(hidden, dim)
+
+    def forward(self, x):
+        return self.fc2(self.act(self.fc1(x)))
+
+
+class Attention(nn.Module):
+    def __init__(self, dim: int, num_heads: int):
+        super().__init__()
+        self.num_heads = num_heads
+        self.scale = (dim // num_heads) ** -0.5
+        self.qkv = nn.Linear(dim, 3 * dim)
+        self.proj = nn.Linear(dim, dim)
+        self.attn_drop = nn.Identity()
+        self.proj_drop = nn.Identity()
+
+    def forward(self, x, attn_bias=None):
+        B, N, C = x.shape
+        H = self.num_heads
+        qkv = self.qkv(x).reshape(B, N, 3, H, C // H).permute(2, 0, 3, 1, 4)
+        q, k, v = qkv.unbind(0)
+        out = F.scaled_dot_product_attention(q, k, v)
+        return self.proj_drop(self.proj(out.transpose(1, 2).reshape(B, N, C)))
+
+
+class LayerScale(nn.Module):
+    def __init__(self, dim: int, init: float):
+        super().__init__()
+        self.gamma = nn.Parameter(torch.full((dim,), float(init)))
+
+    def forward(self, x):
+        return x * self.gamma
+
+
+class Block(nn.Module):
+    def __init__(self, dim: int, heads: int, hidden: int, ls_init: float):
+        super().__init__()
+        self.norm1 = nn.LayerNorm(dim, eps=1e-6)
+        self.attn = Attention(dim, heads)
+        self.ls1 = LayerScale(dim, ls_init)
+        self.norm2 = nn.LayerNorm(dim, eps=1e-6)
+        self.mlp = Mlp(dim, hidden)
+        self.ls2 = LayerScale(dim, ls_init)
+        self.comp: Optional[nn.Module] = None  # head-aligned compensation, if installed
+        self.block_idx = 0
+
+    def forward(self, x):
+        set_current_block_idx(self.block_idx)
+        y = x + self.ls1(self.attn(self.norm1(x)))
+        y = y + self.ls2(self.mlp(self.norm2(y)))
+        if self.comp is not None:
+            y = y + self.comp(x).to(y.dtype)
+        return y
+
+
+class Backbone(nn.Module):
+    def __init__(self, img: int = 224, patch: int = 14, dim: int = 1024, depth: int = 24,
+                 heads: int = 16, hidden: int = 4096, ls_init: float = 1.0):
+        super().__init__()
+        self.patch_embed = nn.Conv2d(3, dim, kernel_size=patch, stride=patch)
+        n = (img // patch) ** 2
+        self.cls_token = nn.Parameter(torch.zeros(1, 1, dim))
+        self.pos_embed = nn.Parameter(torch.zeros(1, n + 1, dim))
+        self.blocks = nn.ModuleList([Block(dim, heads, hidden, ls_init) for _ in range(depth)])
+        for i, b in enumerate(self.blocks):
+            b.block_idx = i
+        self.norm = nn.LayerNorm(dim, eps=1e-6)
+
+    def forward(self, x):
+        x = self.patch_embed(x).flatten(2).transpose(1, 2)
+        x = torch.cat([self.cls_token.expand(x.shape[0], -1, -1), x], dim=1) + self.pos_embed
+        for b in self.blocks:
+            x = b(x)
+        return self.norm(x)
+
+
+class ViTClassifier(nn.Module):
+    """ViT-L/14 backbone + linear head on [CLS, mean(patch)] (2048 -> 1000)."""
+
+    def __init__(self, num_classes: int = 1000, **kw):
+        super().__init__()
+        self.backbone = Backbone(**kw)
+        dim = self.backbone.norm.normalized_shape[0]
+        self.linear_head = nn.Linear(2 * dim, num_classes)
+
+    def forward(self, x):
+        t = self.backbone(x)
+        feat = torch.cat([t[:, 0], t[:, 1:].mean(dim=1)], dim=-1)
+        return self.linear_head(feat)
+
+
+def vit_l14(seed: int = 0, num_classes: int = 1000, **kw) -> ViTClassifier:
+    """Random-initialised DINOv2-style ViT-L/14 (24 blocks, d=1024, 16 heads,
+    MLP 4096, 257 tokens at 224x224)."""
+    g = torch.Generator().manual_seed(seed)
+    m = ViTClassifier(num_classes=num_classes, **kw)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("gamma"):
+                continue
+            if p.dim() >= 2:
+                p.copy_(torch.nn.init.trunc_normal_(torch.empty_like(p), std=0.02, generator=g))
+            elif "norm" in name and name.endswith("weight"):
+                p.fill_(1.0)
+            else:
+                p.zero_()
+        m.backbone.pos_embed.copy_(torch.randn(m.backbone.pos_embed.shape, generator=g) * 0.02)
+        m.backbone.cls_token.copy_(torch.randn(m.backbone.cls_token.shape, generator=g) * 0.02)
+    return m.eval()
+
+
+class _RowMPLinear(nn.Module):
+    """SC linear whose rows carry a seeded random level in each call."""
+
+    def __init__(self, linear: nn.Linear, cfg: SeededRandomMPConfig, salt: int,
+                 cfg_for: Callable[[int, int], dict]):
+        super().__init__()
+        self.weight = linear.weight
+        self.bias = linear.bias
+        self.cfg = cfg
+        self.salt = salt
+        self.cfg_for = cfg_for
+        self.calls = 0
+
+    def forward(self, x):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1]).float()
+        row_L = self.cfg.assign(x2.shape[0], x2.device, salt=(self.salt << 16) + self.calls)
+        self.calls += 1
+        y = sc_linear_rows(x2, self.weight.float(), row_L, self.cfg.stoc_len_levels, "bipolar",
+                           bias=self.bias, cfg_for=self.cfg_for)
+        return y.to(x.dtype).reshape(*shp[:-1], -1)
+
+
+def patch_vit(model: ViTClassifier, sc_prec: int, ops: Iterable[str] = ("qk", "av", "proj"), *,
+              av_mode: str = "bipolar", attn_mp_spec: Optional[Dict] = None,
+              linear_random_mp: Optional[SeededRandomMPConfig] = None,
+              linear_ops: Iterable[str] = ("qkv_proj", "out_proj"),
+              block_cfg_for: Optional[Callable[[int], Callable[[int, int], dict]]] = None,
+              comp_blocks: Iterable[int] = (), comp_sc_prec: Optional[int] = None,
+              comp_seed: int = 1) -> dict:
+    """Install SC operators on every block (see module docstring).
+
+    ``ops`` uses the reference's op names (``cls/sc_attention_patch.py:332``,
+    with ``"proj"`` meaning qkv_proj + out_proj).  ``block_cfg_for(i)`` gives
+    block ``i`` its own pool factory ``(D, p) -> config``.  ``comp_blocks``
+    get a ``HeadAlignedSCLinear`` compensation (random weights) that reuses the
+    block's ``(head_dim, p)`` pool.
+    """
+    ops = set(ops)
+    stats = {"attn": 0, "qkv_proj": 0, "out_proj": 0, "mlp_fc1": 0, "mlp_fc2": 0, "comp": 0}
+    attn_mp_spec = attn_mp_spec or {}
+    linear_ops = set(linear_ops)
+    if "proj" in ops:
+        ops |= {"qkv_proj", "out_proj"}
+    comp_blocks = set(comp_blocks)
+    g = torch.Generator().manual_seed(comp_seed)
+    for i, blk in enumerate(model.backbone.blocks):
+        cfg_for = block_cfg_for(i) if block_cfg_for is not None else _get_config
+        attn = blk.attn
+        if "qk" in ops or "av" in ops:
+            fwd = make_sc_attention_forward(
+                sc_prec, sc_av="av" in ops, sc_qk="qk" in ops,
+                qk_mp_cfg=attn_mp_spec.get("qk"), av_mp_cfg=attn_mp_spec.get("av"),
+                av_mode=av_mode, cfg_for=cfg_for)
+            attn.forward = fwd.__get__(attn, type(attn))
+            stats["attn"] += 1
+
+        def wrap(lin: nn.Linear, op: str, salt: int):
+            if linear_random_mp is not None and op in linear_ops:
+                return _RowMPLinear(lin, linear_random_mp, salt, cfg_for)
+            cfg = None if block_cfg_for is None else cfg_for(lin.in_features, sc_prec)
+            return SCLinear(lin, sc_prec, mode="bipolar", cfg_override=cfg, operator=op)
+
+        if "qkv_proj" in ops:
+            attn.qkv = wrap(attn.qkv, "qkv_proj", 4 * i)
+            stats["qkv_proj"] += 1
+        if "out_proj" in ops:
+            attn.proj = wrap(attn.proj, "out_proj", 4 * i + 1)
+            stats["out_proj"] += 1
+        if "mlp_fc1" in ops:
+            blk.mlp.fc1 = wrap(blk.mlp.fc1, "mlp_fc1", 4 * i + 2)
+            stats["mlp_fc1"] += 1
+        if "mlp_fc2" in ops:
+            blk.mlp.fc2 = wrap(blk.mlp.fc2, "mlp_fc2", 4 * i + 3)
+            stats["mlp_fc2"] += 1
+        if i in comp_blocks:
+            dim = attn.proj.weight.shape[0] if hasattr(attn.proj, "weight") else 1024
+            lin = nn.Linear(dim, dim).to(next(model.parameters()).device)
+            with torch.no_grad():
+                lin.weight.copy_(torch.randn(dim, dim, generator=g) * 0.002)
+                lin.bias.zero_()
+            head_dim = dim // attn.num_heads
+            p = comp_sc_prec or sc_prec
+            blk.comp = HeadAlignedSCLinear(lin, p, n_heads=attn.num_heads,
+                                           cfg_override=cfg_for(head_dim, p))
+            stats["comp"] += 1
+    return stats

@@ -30,8 +30,8 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_struct_layout_matches_header():
-    # 2*i32 + 2 ptr + 5 i64 + 4 i32 + 2 i64 + ptr + 2 i32 + 6 ptr + size_t
-    assert ctypes.sizeof(_lib.MatmulArgs) == 8 + 16 + 40 + 16 + 16 + 8 + 8 + 48 + 8
+    # 2*i32 + 2 ptr + 5 i64 + 4 i32 + 3 i64 + ptr + 2 i32 + 6 ptr + size_t
+    assert ctypes.sizeof(_lib.MatmulArgs) == 8 + 16 + 40 + 16 + 16 + 8 + 8 + 8 + 48 + 8
     assert _lib.MatmulArgs.workspace_bytes.offset == ctypes.sizeof(_lib.MatmulArgs) - 8
 
 
