@@ -240,6 +240,9 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
 
     from scmp_vit_b200 import _lib
+    from scmp_vit_b200.sc import set_default_engine
+
+    set_default_engine(args.engine)
 
     wl = WORKLOADS[args.config]
     if args.batch:

@@ -117,6 +117,12 @@ SCMP_API int scmp_abi_version(void);
  * reference counterpart. */
 SCMP_API uint64_t scmp_kernel_launches(void);
 
+/* Sticky device-side error flags of the current device, read synchronously
+ * (bit 0: a bounded wait inside the tensor-core engine gave up, so some
+ * output of an earlier call is invalid); reset != 0 clears them.  No
+ * reference counterpart. */
+SCMP_API int scmp_engine_status(int reset, unsigned int *flags);
+
 /* Roofline probe (synchronous; allocates a small scratch buffer): runs a
  * register-only loop of one instruction class on every SM of the current
  * device and returns its rate.  kind 0 = LOP3+POPC (bit-products/s),

@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "scmp_last_error",
     "scmp_abi_version",
     "scmp_kernel_launches",
+    "scmp_engine_status",
     "scmp_probe_int_peak",
 )
 
@@ -100,6 +101,8 @@ def load() -> ctypes.CDLL:
         lib.scmp_abi_version.restype = ctypes.c_int
         lib.scmp_kernel_launches.argtypes = []
         lib.scmp_kernel_launches.restype = ctypes.c_uint64
+        lib.scmp_engine_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+        lib.scmp_engine_status.restype = ctypes.c_int
         lib.scmp_probe_int_peak.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
         lib.scmp_probe_int_peak.restype = ctypes.c_int
         if lib.scmp_abi_version() != ABI_VERSION:
@@ -112,6 +115,14 @@ def load() -> ctypes.CDLL:
 def kernel_launches() -> int:
     """Kernels launched by the engine library so far in this process."""
     return int(load().scmp_kernel_launches())
+
+
+def engine_status(reset: bool = False) -> int:
+    """Sticky device error flags (bit 0: a bounded wait in the tensor-core
+    engine gave up).  Synchronises the current device."""
+    v = ctypes.c_uint(0)
+    check(load().scmp_engine_status(int(reset), ctypes.byref(v)))
+    return int(v.value)
 
 
 def probe_int_peak(kind: int) -> float:

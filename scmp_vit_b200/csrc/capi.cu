@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "sc_common.cuh"
@@ -14,6 +15,32 @@ thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
 
 inline void count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// Sticky device-side error word (bit 0: a bounded wait of the tensor-core
+// engine gave up).  Read with scmp_engine_status.
+__device__ unsigned int g_engine_error;
+std::mutex g_err_mu;
+unsigned int *g_err_ptr[64] = {};
+
+unsigned int *engine_error_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_err_mu);
+  if (!g_err_ptr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_engine_error) != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<unsigned int *>(p);
+  }
+  return g_err_ptr[dev];
+}
+
+// Rows of the tail that the CUDA-core engine takes instead of padding a
+// tensor-core tile (e.g. the 257th token).
+int64_t tc_rows(int64_t rows, int64_t tile) {
+  const int64_t tail = rows % tile;
+  if (tail != 0 && tail <= tile / 8 && rows > tile) return rows - tail;
+  return rows;
+}
 
 int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char *fmt, ...) {
@@ -170,6 +197,7 @@ QuantPlane plane_of(const OperandLayout &o, unsigned char *ws) {
 }
 
 }  // namespace
+
 }  // namespace scmp
 
 using namespace scmp;
@@ -181,6 +209,18 @@ const char *scmp_last_error(void) { return g_last_error.c_str(); }
 int scmp_abi_version(void) { return SCMP_ABI_VERSION; }
 
 uint64_t scmp_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int scmp_engine_status(int reset, unsigned int *flags) {
+  if (!flags) return fail(SCMP_EINVAL, "flags is NULL");
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_engine_error, sizeof(unsigned int));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the engine error word");
+  if (reset) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_engine_error, &zero, sizeof(unsigned int));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the engine error word");
+  }
+  return SCMP_OK;
+}
 
 size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args) {
   if (validate(args) != SCMP_OK) return 0;
@@ -209,9 +249,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   if ((rc = quantize_operand(x.a, plan.A, kseg, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
   if ((rc = quantize_operand(x.b, plan.B, kseg, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
   auto *table = reinterpret_cast<uint32_t *>(ws + plan.table);
-  cudaError_t e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table, s);
-  if (e != cudaSuccess) return cuda_fail(e, "stream_table launch");
-  count_launches(1);
+  cudaError_t e;
 
   GemmProblem P{};
   P.qa = plane_of(plan.A, ws);
@@ -234,8 +272,54 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.out = x.out;
   P.acc_out = x.acc_out;
   P.stream_table = table;
-  if ((e = launch_gemm_popc(P, s)) != cudaSuccess) return cuda_fail(e, "gemm_popc launch");
-  count_launches(1);
+  P.m_lo = 0;
+  P.m_hi = x.M;
+  P.n_lo = 0;
+  P.n_hi = x.N;
+
+  bool use_tc = false;
+  if (x.engine == SCMP_ENGINE_TCGEN05) {
+    if (!tc_supported(P))
+      return fail(SCMP_EUNSUPPORTED,
+                  "tcgen05 engine needs 5 <= sc_prec <= 8, one K segment, and not unipolar at p=8");
+    use_tc = true;
+  }
+  int64_t m_tc = 0, n_tc = 0;
+  if (use_tc) {
+    unsigned int *err = engine_error_ptr();
+    if (!err) return fail(SCMP_ECUDA, "cannot resolve the engine error word");
+    m_tc = tc_rows(x.M, 256);
+    n_tc = tc_rows(x.N, tc_block_n(x.N));
+    if ((e = launch_gemm_tc(P, m_tc, n_tc, err, s)) != cudaSuccess)
+      return cuda_fail(e, "gemm_tc launch");
+    count_launches(1);
+  }
+  // CUDA-core engine: everything (no tensor-core path) or the ragged strips
+  // the tensor-core tiles leave (rows >= m_tc; columns >= n_tc of rows < m_tc).
+  const bool strip_m = use_tc && m_tc < x.M;
+  const bool strip_n = use_tc && n_tc < x.N && m_tc > 0;
+  if (!use_tc || strip_m || strip_n) {
+    if ((e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table, s)) != cudaSuccess)
+      return cuda_fail(e, "stream_table launch");
+    count_launches(1);
+  }
+  if (!use_tc) {
+    if ((e = launch_gemm_popc(P, s)) != cudaSuccess) return cuda_fail(e, "gemm_popc launch");
+    count_launches(1);
+  }
+  if (strip_m) {
+    GemmProblem Q = P;
+    Q.m_lo = m_tc;
+    if ((e = launch_gemm_popc(Q, s)) != cudaSuccess) return cuda_fail(e, "gemm_popc launch");
+    count_launches(1);
+  }
+  if (strip_n) {
+    GemmProblem Q = P;
+    Q.m_hi = m_tc;
+    Q.n_lo = n_tc;
+    if ((e = launch_gemm_popc(Q, s)) != cudaSuccess) return cuda_fail(e, "gemm_popc launch");
+    count_launches(1);
+  }
   return SCMP_OK;
 }
 

@@ -33,8 +33,8 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
 
   const int64_t slice = blockIdx.z;
   const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
-  const int64_t m0 = (int64_t)blockIdx.y * BM;
-  const int64_t n0 = (int64_t)blockIdx.x * BN;
+  const int64_t m0 = P.m_lo + (int64_t)blockIdx.y * BM;
+  const int64_t n0 = P.n_lo + (int64_t)blockIdx.x * BN;
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   const int T = 1 << P.prec;
@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
       const int m = idx / BD, dd = idx % BD;
       const int64_t gm = m0 + m, d = d0 + dd;
       int k = 0, s = 1;
-      if (gm < P.M && d < P.K) {
+      if (gm < P.m_hi && d < P.K) {
         const int64_t grow = slice * P.M + gm;
         const int L = row_stream_len(P, slice, grow);
         const int c = P.qa.code[grow * P.K + d];
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
       const int64_t gn = n0 + n, d = d0 + dd;
       uint32_t *dst = sB + (dd * BN + n) * LW;
       int s = 1;
-      if (gn < P.N && d < P.K) {
+      if (gn < P.n_hi && d < P.K) {
         const int c = P.qb.code[(slice_b * P.N + gn) * P.K + d];
         s = c < 0 ? -1 : 1;
         const int v = c < 0 ? -c : c;
@@ -118,14 +118,14 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int64_t gm = m0 + ty + 16 * i;
-          if (gm >= P.M) continue;
+          if (gm >= P.m_hi) continue;
           const int64_t grow = slice * P.M + gm;
           const int L = row_stream_len(P, slice, grow);
           const int64_t ra = grow * P.nseg + seg;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int64_t gn = n0 + tx + 16 * j;
-            if (gn < P.N && L > 0) {
+            if (gn < P.n_hi && L > 0) {
               const int64_t rb = (slice_b * P.N + gn) * P.nseg + seg;
               const float r = sc_rescale(P.mode, P.prec, L, acc[i][j], P.kseg, P.qa.scale[ra],
                                          P.qa.zero[ra], P.qa.rowsum[ra], P.qb.scale[rb],
@@ -145,14 +145,14 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t gm = m0 + ty + 16 * i;
-    if (gm >= P.M) continue;
+    if (gm >= P.m_hi) continue;
     const int64_t grow = slice * P.M + gm;
     const int L = row_stream_len(P, slice, grow);
     if (L < 0) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t gn = n0 + tx + 16 * j;
-      if (gn >= P.N) continue;
+      if (gn >= P.n_hi) continue;
       float v = L > 0 ? y[i][j] : 0.0f;
       if (P.bias) v = __fadd_rn(v, P.bias[gn]);
       const int64_t o = grow * P.N + gn;
@@ -168,7 +168,8 @@ cudaError_t launch_lw(const GemmProblem &P, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(gemm_popc_kernel<LW>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((P.N + BN - 1) / BN), (unsigned)((P.M + BM - 1) / BM), (unsigned)P.batch);
+  dim3 grid((unsigned)((P.n_hi - P.n_lo + BN - 1) / BN), (unsigned)((P.m_hi - P.m_lo + BM - 1) / BM),
+            (unsigned)P.batch);
   gemm_popc_kernel<LW><<<grid, kThreads, smem, s>>>(P);
   return cudaGetLastError();
 }
@@ -176,7 +177,7 @@ cudaError_t launch_lw(const GemmProblem &P, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s) {
-  if (P.M == 0 || P.N == 0 || P.batch == 0) return cudaSuccess;
+  if (P.m_hi <= P.m_lo || P.n_hi <= P.n_lo || P.batch == 0) return cudaSuccess;
   // Words per stream: enough for the longest stream any row may use.
   const int T = 1 << P.prec;
   const int Lmax = (P.row_L || P.slice_L) ? T : P.stoc_len;

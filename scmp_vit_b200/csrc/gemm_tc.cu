@@ -1,0 +1,451 @@
+// SC GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8).
+//
+// The SC inner product of row m of a and row n of b is
+//     acc[m,n] = sum_d sum_{t < Lp} A'[m,(d,t)] * B'[n,(d,t)]
+//     A'[m,(d,t)] = sigma_a(m,d) * [t < k(m,d)]           (enable window)
+//     B'[n,(d,t)] = sigma_b(n,d) * [R[d'][t] < c_b(n,d)]   (Sobol/LFSR stream)
+// i.e. an exact integer GEMM over an inner dimension of K * Lp with operands in
+// {-1, 0, +1}.  Each AND of two stream bits is one int8 multiply-add, each
+// popcount is the s32 accumulation in tensor memory.  The operands are never
+// stored in HBM: producer warps generate each 128-byte k-block of both
+// operands from the int16 codes straight into shared memory, in the
+// K-major 128-byte-swizzled layout the UMMA descriptors describe, and one
+// thread issues tcgen05.mma for the stage.
+//
+// CTA tile: 256 rows of a (two 128-row UMMA accumulators) x BN rows of b,
+// all 2*BN TMEM columns; 3-stage smem ring; warp 0 issues MMAs, warps 1..8
+// generate operands and run the epilogue (rescale + bias + store).  Every wait
+// is bounded: on timeout the kernel raises the error flag and drains.
+#include <stdint.h>
+
+#include "sc_common.cuh"
+
+namespace scmp {
+namespace {
+
+constexpr int kBM = 256;           // a rows per tile (2 x UMMA_M 128)
+constexpr int kKB = 128;           // bytes (= inner elements) per k-block
+constexpr int kStages = 3;
+constexpr int kProducerWarps = 8;
+constexpr int kProducers = 32 * kProducerWarps;
+constexpr int kThreads = 32 + kProducers;
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+template <int BN>
+struct TcCfg {
+  static constexpr uint32_t kStageA = kBM * kKB;  // 32 KB
+  static constexpr uint32_t kStageB = BN * kKB;
+  static constexpr uint32_t kStage = kStageA + kStageB;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 128
+  static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct TcParams {
+  GemmProblem P;
+  int lp_log2;      // log2 of the padded stream length Lp (>= 5)
+  int shift_pool;   // 1: compare R >> 1 against |c_b| / 2 (bipolar, p == 8)
+  int64_t nkb;      // k-blocks per tile = ceil(K * Lp / 128)
+  int64_t m_rows;   // rows of a handled per slice (window [0, m_rows))
+  int64_t n_rows;   // rows of b handled per slice (window [0, n_rows))
+  int64_t tiles_m, tiles_n, tiles;
+  unsigned int *error;
+};
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when it gave up (timeout or another thread aborted).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (now_ns() - t0 > kTimeoutNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// K-major, 128-byte-swizzled UMMA shared-memory descriptor: 8-row atoms of
+// 128 B (1024 B apart), version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);        // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused here)
+  d |= (uint64_t)(1024u >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = BN.
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc_i8() {
+  return (2u << 4)                      // D format S32
+         | (1u << 7)                    // A format S8
+         | (1u << 10)                   // B format S8
+         | ((uint32_t)(BN >> 3) << 17)  // N >> 3
+         | ((uint32_t)(128 >> 4) << 24);  // M >> 4
+}
+
+// Byte offset of 16-byte chunk `c` of row `r` in a SW128 K-major tile.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm) {
+  using Cfg = TcCfg<BN>;
+  const GemmProblem &P = prm.P;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + kStages * Cfg::kStage);
+  uint64_t *empty_bar = full_bar + kStages;
+  uint64_t *tfull_bar = empty_bar + kStages;
+  uint64_t *tempty_bar = tfull_bar + 1;
+  uint64_t *drain_bar = tempty_bar + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], kProducers);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, kProducers);
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(Cfg::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int T = 1 << P.prec;
+  const int64_t Lp = (int64_t)1 << prm.lp_log2;
+
+  if (warp == 0) {
+    // ================================================= MMA issuer (lane 0)
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8<BN>();
+      const uint32_t smem0 = smem_u32(smem);
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++it) {
+        if (it > 0) ok = mbar_wait(tempty_bar, (uint32_t)((it - 1) & 1), abort);
+        if (!ok) break;
+        tc_fence_after();
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem0 + stage * Cfg::kStage;
+          const uint32_t b0 = a0 + Cfg::kStageA;
+#pragma unroll
+          for (int kk = 0; kk < kKB / 32; ++kk) {
+            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+              tc_mma_i8(tmem_base + j * BN, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar);
+      }
+      // Drain: everything this thread issued has completed before TMEM is freed.
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, abort);
+    }
+    __syncwarp();
+  } else {
+    // ===================================== producers + epilogue (8 warps)
+    const int pt = threadIdx.x - 32;  // 0..255
+    const int chunk = pt & 7;         // 16-byte chunk of the 128-byte k-block row
+    const int rsub = pt >> 3;         // 0..31: rows rsub + 32 * i
+    int stage = 0;
+    uint32_t phase = 0;
+    int64_t it = 0;
+    bool ok = true;
+    const uint32_t tword0 = 0x03020100u, tstep = 0x04040404u;
+    for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++it) {
+      const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
+      const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+      const int64_t m0 = (rem % prm.tiles_m) * kBM;
+      const int64_t n0 = (rem / prm.tiles_m) * BN;
+      const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
+      // per-row stream length (a rows) for the 8 rows this thread fills
+      int Lrow[8];
+      const int16_t *arow[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t gm = m0 + rsub + 32 * i;
+        Lrow[i] = 0;
+        arow[i] = nullptr;
+        if (gm < prm.m_rows) {
+          const int64_t grow = slice * P.M + gm;
+          Lrow[i] = row_stream_len(P, slice, grow);
+          arow[i] = P.qa.code + grow * P.K;
+        }
+      }
+      const int16_t *brow[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const int64_t gn = n0 + rsub + 32 * i;
+        brow[i] = gn < prm.n_rows ? P.qb.code + (slice_b * P.N + gn) * P.K : nullptr;
+      }
+
+      for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+        const int64_t i0 = kb * kKB + chunk * 16;
+        const int64_t d = i0 >> prm.lp_log2;
+        const int t0 = (int)(i0 & (Lp - 1));
+        const bool dval = d < P.K;
+        // pool chunk R[d'][t0 .. t0+15] (shared by every b row of this lane)
+        uint4 rr = make_uint4(0, 0, 0, 0);
+        if (dval) {
+          rr = __ldg(reinterpret_cast<const uint4 *>(P.pool + (d % P.pool_dims) * T + t0));
+          if (prm.shift_pool) {
+            rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
+            rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
+          }
+        }
+        int16_t ca[8], cb[BN / 32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ca[i] = (dval && arow[i]) ? __ldg(arow[i] + d) : (int16_t)0;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) cb[i] = (dval && brow[i]) ? __ldg(brow[i] + d) : (int16_t)0;
+
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) { ok = false; break; }
+        unsigned char *sa = smem + stage * Cfg::kStage;
+        unsigned char *sb = sa + Cfg::kStageA;
+        // ---- A: enable windows, sigma * [t < k]
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = rsub + 32 * i;
+          const int c = ca[i];
+          const int mag = c < 0 ? -c : c;
+          const int k = (mag * Lrow[i]) >> P.prec;
+          const int q = min(max(k - t0, 0), 16);
+          const uint32_t rep = (uint32_t)(0x7F + q) * 0x01010101u;
+          const uint32_t sm = c < 0 ? 0xFFFFFFFFu : 0x01010101u;
+          uint4 w;
+          w.x = prmt(rep - tword0, 0u, 0xBA98u) & sm;
+          w.y = prmt(rep - (tword0 + tstep), 0u, 0xBA98u) & sm;
+          w.z = prmt(rep - (tword0 + 2 * tstep), 0u, 0xBA98u) & sm;
+          w.w = prmt(rep - (tword0 + 3 * tstep), 0u, 0xBA98u) & sm;
+          *reinterpret_cast<uint4 *>(sa + sw128_offset(r, chunk)) = w;
+        }
+        // ---- B: streams, sigma * [R[d'][t] < c_b]
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) {
+          const int r = rsub + 32 * i;
+          const int c = cb[i];
+          int u = c < 0 ? -c : c;
+          if (prm.shift_pool) u >>= 1;
+          const uint32_t rep = (uint32_t)(0x7F + u) * 0x01010101u;
+          const uint32_t sm = c < 0 ? 0xFFFFFFFFu : 0x01010101u;
+          uint4 w;
+          w.x = prmt(rep - rr.x, 0u, 0xBA98u) & sm;
+          w.y = prmt(rep - rr.y, 0u, 0xBA98u) & sm;
+          w.z = prmt(rep - rr.z, 0u, 0xBA98u) & sm;
+          w.w = prmt(rep - rr.w, 0u, 0xBA98u) & sm;
+          *reinterpret_cast<uint4 *>(sb + sw128_offset(r, chunk)) = w;
+        }
+        fence_async_smem();
+        mbar_arrive(&full_bar[stage]);
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+
+      // ---- epilogue: TMEM -> rescale -> bias -> global
+      if (!mbar_wait(tfull_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
+      tc_fence_after();
+      const int pw = warp - 1;            // producer warp 0..7
+      const int acc_j = pw >> 2;          // accumulator (a rows 0-127 or 128-255)
+      const int quarter = warp & 3;       // TMEM lanes this warp may access
+      const int64_t gm = m0 + acc_j * 128 + quarter * 32 + lane;
+      const bool row_ok = gm < prm.m_rows;
+      int L = -1;
+      float sa_ = 0.f;
+      int32_t za_ = 0, rsa_ = 0;
+      int64_t grow = 0;
+      if (row_ok) {
+        grow = slice * P.M + gm;
+        L = row_stream_len(P, slice, grow);
+        sa_ = P.qa.scale[grow];
+        za_ = P.qa.zero[grow];
+        rsa_ = P.qa.rowsum[grow];
+      }
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t v[32];
+        const uint32_t taddr =
+            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+              "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+              "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+              "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+              "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row_ok && L >= 0) {
+          const int64_t nb = n0 + cc * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int64_t gn = nb + i;
+            if (gn >= prm.n_rows) continue;
+            const int32_t a = L > 0 ? (int32_t)v[i] : 0;
+            float y = 0.0f;
+            if (L > 0) {
+              const int64_t brw = slice_b * P.N + gn;
+              y = sc_rescale(P.mode, P.prec, L, a, P.K, sa_, za_, rsa_, P.qb.scale[brw],
+                             P.qb.zero[brw], P.qb.rowsum[brw]);
+            }
+            if (P.bias) y = __fadd_rn(y, P.bias[gn]);
+            const int64_t o = grow * P.N + gn;
+            P.out[o] = y;
+            if (P.acc_out) P.acc_out[o] = a;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(Cfg::kTmemCols));
+  }
+  if (threadIdx.x == 0 && *abort) atomicOr(prm.error, 1u);
+}
+
+template <int BN>
+cudaError_t launch_bn(const TcParams &prm, int sms, cudaStream_t s) {
+  const size_t smem = TcCfg<BN>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = prm.tiles < sms ? prm.tiles : sms;
+  gemm_tc_kernel<BN><<<(unsigned)grid, kThreads, smem, s>>>(prm);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_supported(const GemmProblem &P) {
+  if (P.prec < 5 || P.prec > 8) return false;           // pool rows >= 32 bytes
+  if (P.nseg != 1) return false;                        // segmented K: popc engine
+  if (P.mode == SCMP_UNIPOLAR && P.prec == 8) return false;  // 8-bit thresholds
+  return true;
+}
+
+int tc_block_n(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
+                           unsigned int *error, cudaStream_t s) {
+  if (P.M == 0 || P.N == 0 || P.batch == 0 || m_rows == 0 || n_rows == 0) return cudaSuccess;
+  TcParams prm{};
+  prm.P = P;
+  const int T = 1 << P.prec;
+  const int Lmax = (P.row_L || P.slice_L) ? T : P.stoc_len;
+  int lg = 5;
+  while ((1 << lg) < Lmax) ++lg;
+  prm.lp_log2 = lg;
+  prm.shift_pool = (P.mode == SCMP_BIPOLAR && P.prec == 8) ? 1 : 0;
+  prm.nkb = (P.K * ((int64_t)1 << lg) + kKB - 1) / kKB;
+  prm.m_rows = m_rows;
+  prm.n_rows = n_rows;
+  const int bn = tc_block_n(n_rows);
+  prm.tiles_m = (m_rows + kBM - 1) / kBM;
+  prm.tiles_n = (n_rows + bn - 1) / bn;
+  prm.tiles = P.batch * prm.tiles_m * prm.tiles_n;
+  prm.error = error;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (bn == 64) return launch_bn<64>(prm, sms, s);
+  if (bn == 128) return launch_bn<128>(prm, sms, s);
+  return launch_bn<256>(prm, sms, s);
+}
+
+}  // namespace scmp

@@ -51,6 +51,8 @@ struct GemmProblem {
   int32_t *acc_out;
   // stream table ST[pool_dims][2^p + 1][2^p / 32] (bit t of threshold v)
   const uint32_t *stream_table;
+  // window of (a row, b row) pairs per slice this launch computes
+  int64_t m_lo, m_hi, n_lo, n_hi;
 };
 
 // Per-row stream length in the engine's convention (see scmp_matmul_args).
@@ -86,5 +88,9 @@ cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int 
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
+bool tc_supported(const GemmProblem &P);
+int tc_block_n(int64_t N);
+cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
+                           unsigned int *error, cudaStream_t s);
 
 }  // namespace scmp

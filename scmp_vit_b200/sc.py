@@ -29,7 +29,20 @@ import torch
 from . import _lib
 from .config_helpers import make_sobol_simple_config, pool_table
 
-__all__ = ["sc_matmul", "device_pool", "default_config"]
+__all__ = ["sc_matmul", "device_pool", "default_config", "set_default_engine"]
+
+_DEFAULT_ENGINE = "auto"
+
+
+def set_default_engine(engine: str) -> None:
+    """Engine used when ``sc_matmul(engine=None)``: ``auto`` (the library
+    picks), ``tcgen05`` (tensor cores) or ``popc`` (CUDA cores)."""
+    global _DEFAULT_ENGINE
+    engine = _DEFAULT_ENGINE if engine is None else engine
+    if engine not in _lib.ENGINE:
+        raise ValueError(f"unknown engine {engine!r}")
+    _DEFAULT_ENGINE = engine
+
 
 _POOL_LOCK = threading.Lock()
 _POOLS: dict = {}
@@ -71,7 +84,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
               out: Optional[torch.Tensor] = None,
               acc_out: Optional[torch.Tensor] = None,
               k_segment: int = 0,
-              engine: str = "auto") -> torch.Tensor:
+              engine: Optional[str] = None) -> torch.Tensor:
     """SC estimate of ``a @ b^T`` (see module docstring).
 
     Extra keyword arguments beyond the reference signature:
@@ -92,6 +105,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
         raise ValueError(f"unknown granularity {granularity!r}")
     if mode not in _lib.MODE:
         raise ValueError(f"unknown mode {mode!r}")
+    engine = _DEFAULT_ENGINE if engine is None else engine
     if engine not in _lib.ENGINE:
         raise ValueError(f"unknown engine {engine!r}")
     if a.dim() not in (2, 3) or b.dim() not in (2, 3):

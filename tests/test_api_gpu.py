@@ -34,9 +34,9 @@ def test_sclinear_uniform(cuda_device):
     m = SCLinear(lin, 7, cfg_override=cfg).to(cuda_device)
     x = torch.randn(3, 11, 96, generator=torch.Generator().manual_seed(1))
     y = m(x.to(cuda_device)).cpu().numpy().reshape(33, 80)
-    _, y_ref = sc_oracle.sc_matmul_ref(x.reshape(33, 96).numpy(), lin.weight.detach().numpy(),
+    _, y_ref = sc_oracle.sc_matmul_ref(x.reshape(33, 96).numpy(), lin.weight.detach().cpu().numpy(),
                                        sc_prec=7, pool=cfg["table"],
-                                       bias=lin.bias.detach().numpy())
+                                       bias=lin.bias.detach().cpu().numpy())
     np.testing.assert_allclose(y, y_ref[0], rtol=RTOL, atol=1e-30)
 
 
@@ -52,8 +52,8 @@ def test_sclinear_fixed_mp_matches_bucket_loop(cuda_device):
     row_L = classify_input_rows(x, mp).row_levels.numpy()
     assert sorted(set(row_L.tolist())) == [128, 192, 256]
     pools = {p: sc_linear._get_config(64, p)["table"] for p in (7, 8)}
-    _, y_ref = sc_oracle.sc_matmul_rows_ref(x.numpy(), lin.weight.detach().numpy(), row_L,
-                                            pools, bias=lin.bias.detach().numpy())
+    _, y_ref = sc_oracle.sc_matmul_rows_ref(x.numpy(), lin.weight.detach().cpu().numpy(), row_L,
+                                            pools, bias=lin.bias.detach().cpu().numpy())
     np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
 
 
@@ -65,8 +65,8 @@ def test_head_aligned_is_ordered_segment_sum(cuda_device):
     x = torch.randn(2, 21, 128, generator=torch.Generator().manual_seed(6))
     y = m(x.to(cuda_device)).cpu().numpy().reshape(42, 72)
     _, y_ref = sc_oracle.sc_matmul_segments_ref(x.reshape(42, 128).numpy(),
-                                                lin.weight.detach().numpy(), 16, sc_prec=8,
-                                                pool=cfg["table"], bias=lin.bias.detach().numpy())
+                                                lin.weight.detach().cpu().numpy(), 16, sc_prec=8,
+                                                pool=cfg["table"], bias=lin.bias.detach().cpu().numpy())
     np.testing.assert_allclose(y, y_ref[0], rtol=RTOL, atol=1e-30)
 
 
@@ -77,10 +77,10 @@ def test_chunk_d_path(cuda_device):
     x = torch.randn(30, 200, generator=torch.Generator().manual_seed(8))
     y = m(x.to(cuda_device)).cpu().numpy()
     xp = np.pad(x.numpy(), ((0, 0), (0, 56)))
-    wp = np.pad(lin.weight.detach().numpy(), ((0, 0), (0, 56)))
+    wp = np.pad(lin.weight.detach().cpu().numpy(), ((0, 0), (0, 56)))
     _, y_ref = sc_oracle.sc_matmul_segments_ref(xp, wp, 64, sc_prec=7,
                                                 pool=sc_linear._get_config(64, 7)["table"],
-                                                bias=lin.bias.detach().numpy())
+                                                bias=lin.bias.detach().cpu().numpy())
     np.testing.assert_allclose(y, y_ref[0], rtol=RTOL, atol=1e-30)
 
 

@@ -99,12 +99,21 @@ def test_groups_and_shared_b(cuda_device):
     _run(cuda_device, a, b, _cfg("sobol", 48, 8), sc_prec=8, stoc_len=256, group_a=4, group_b=7)
 
 
-def test_chunk_d_pool_reuse(cuda_device):
+def test_chunk_d_is_chunk_sum(cuda_device):
+    """chunk_d=64 over K=192: three 64-wide chunks, each quantised per row and
+    rescaled on its own with the (64, p) pool, summed in chunk order."""
+    dev = cuda_device
     g = torch.Generator().manual_seed(4)
-    a = torch.randn(40, 200, generator=g)
-    b = torch.randn(30, 200, generator=g)
+    a = torch.randn(40, 192, generator=g)
+    b = torch.randn(30, 192, generator=g)
     cfg = _cfg("sobol", 64, 7)
-    _run(cuda_device, a, b, cfg, pool_dims=64, sc_prec=7, stoc_len=128, chunk_d=64)
+    acc = torch.empty(40 * 30, dtype=torch.int32, device=dev)
+    y = sc_matmul(a.to(dev), b.to(dev), sc_prec=7, config=cfg, chunk_d=64, acc_out=acc)
+    torch.cuda.synchronize()
+    acc_ref, y_ref = sc_oracle.sc_matmul_segments_ref(a.numpy(), b.numpy(), 64, sc_prec=7,
+                                                      pool=cfg["table"])
+    np.testing.assert_array_equal(acc.view(40, 30).cpu().numpy(), acc_ref[0])
+    np.testing.assert_allclose(y.cpu().numpy(), y_ref[0], rtol=RTOL, atol=1e-30)
 
 
 def test_bias_fused(cuda_device):
