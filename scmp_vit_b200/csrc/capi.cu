@@ -236,8 +236,6 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   if (x.batch == 0 || x.M == 0 || x.N == 0) return SCMP_OK;
   if (!x.a || !x.b || !x.pool || !x.out)
     return fail(SCMP_EINVAL, "a, b, pool and out must be non-NULL");
-  if (x.engine == SCMP_ENGINE_TCGEN05)
-    return fail(SCMP_EUNSUPPORTED, "tcgen05 engine is not built into this library");
   const Plan plan = make_plan(&x);
   if (!x.workspace || x.workspace_bytes < plan.total)
     return fail(SCMP_EWORKSPACE, "workspace needs %zu bytes, got %zu", plan.total,
