@@ -96,6 +96,9 @@ typedef struct scmp_matmul_args {
   size_t workspace_bytes;
 } scmp_matmul_args;
 
+/* Size of the static scratch array behind scmp_sc_matmul_noalloc. */
+#define SCMP_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
 /* Bytes of device scratch that scmp_sc_matmul needs for these arguments
  * (pointers may be NULL when only sizing).  Returns 0 on invalid arguments. */
 SCMP_API size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args);
@@ -105,6 +108,21 @@ SCMP_API size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args);
  * accumulate signed popcounts, rescale to fp32.  Asynchronous on `stream`
  * (a cudaStream_t; NULL = legacy default stream). */
 SCMP_API int scmp_sc_matmul(const scmp_matmul_args *args, void *stream);
+
+/* scmp_sc_matmul for callers that cannot allocate device memory (no
+ * reference counterpart).  A host binding the C ABI from plain C or an FFI
+ * has no caching allocator, a cudaMalloc/cudaFree per call would synchronise
+ * the device, and some runtimes reserve the whole memory budget up front; so
+ * this variant ignores args->workspace and uses a fixed array compiled into
+ * the library (SCMP_NOALLOC_SCRATCH_BYTES on every device that loads it, held
+ * until exit).  It allocates nothing.  Problems needing more scratch than the
+ * array holds (see scmp_sc_matmul_workspace_size) fail with SCMP_EWORKSPACE.
+ * Every call on a device shares the array, which keeps the last call's
+ * contents (the engine writes all scratch before reading it); calls whose
+ * kernels overlap on the GPU race on it, so keep them on one stream.  The
+ * first call on each device looks up the array's address with that device
+ * current; make it before any stream capture begins. */
+SCMP_API int scmp_sc_matmul_noalloc(const scmp_matmul_args *args, void *stream);
 
 /* Message of the last failure on this thread ("" if none). */
 SCMP_API const char *scmp_last_error(void);

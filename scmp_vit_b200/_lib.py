@@ -12,6 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libscmp_b200.so"
 
 ABI_VERSION = 1
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # SCMP_NOALLOC_SCRATCH_BYTES
 
 SCMP_OK = 0
 STATUS_NAMES = {
@@ -25,6 +26,7 @@ ENGINE = {"auto": 0, "popc": 1, "tcgen05": 2}
 EXPORTED_SYMBOLS = (
     "scmp_sc_matmul_workspace_size",
     "scmp_sc_matmul",
+    "scmp_sc_matmul_noalloc",
     "scmp_last_error",
     "scmp_abi_version",
     "scmp_kernel_launches",
@@ -95,6 +97,8 @@ def load() -> ctypes.CDLL:
         lib.scmp_sc_matmul_workspace_size.restype = ctypes.c_size_t
         lib.scmp_sc_matmul.argtypes = [ctypes.POINTER(MatmulArgs), ctypes.c_void_p]
         lib.scmp_sc_matmul.restype = ctypes.c_int
+        lib.scmp_sc_matmul_noalloc.argtypes = [ctypes.POINTER(MatmulArgs), ctypes.c_void_p]
+        lib.scmp_sc_matmul_noalloc.restype = ctypes.c_int
         lib.scmp_last_error.argtypes = []
         lib.scmp_last_error.restype = ctypes.c_char_p
         lib.scmp_abi_version.argtypes = []

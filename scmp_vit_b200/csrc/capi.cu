@@ -198,6 +198,8 @@ QuantPlane plane_of(const OperandLayout &o, unsigned char *ws) {
 
 }  // namespace
 
+void set_last_error(const char *msg) { g_last_error = msg ? msg : ""; }
+
 }  // namespace scmp
 
 using namespace scmp;
