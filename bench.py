@@ -156,6 +156,53 @@ def cpu_baseline(sc_prec: int = 7, L: int = 128, budget_s: float = 10.0) -> dict
             "bitops_per_s": bitops / dt}
 
 
+# --------------------------------------------------------------- roofline
+
+def int8_tensor_peak(dev) -> float:
+    """Measured dense int8 tensor-core rate (ops/s, 2 per multiply-add):
+    cuBLAS int8 GEMM 8192^3 through torch._int_mm, best of 10."""
+    import torch
+    n = 8192
+    a = torch.randint(-3, 3, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-3, 3, (n, n), dtype=torch.int8, device=dev).t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1) / 1e3)
+    del a, b
+    return 2.0 * n ** 3 / best
+
+
+def roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops) -> dict:
+    """Roofline of the dominant kernel (the qkv_proj SC matmul).  One SC
+    bit-product = one int8 multiply-add on the tensor-core engine (2 ops) and
+    one counted AND bit on the CUDA-core engine."""
+    base = {"kernel": "sc_matmul qkv_proj", "per_launch_ms": qkv_ms,
+            "algorithmic_per_launch": qkv_bitops, "algorithmic_unit": "bit-products",
+            "traffic": None,
+            "int_pipe_peak_tbitops": peak_popc / 1e12,
+            "x_int_pipe_roofline": (achieved / peak_popc) if achieved else None}
+    if on_tc:
+        base.update({"bound": "tensor", "engine": "tcgen05 kind::i8",
+                     "achieved": 2 * achieved / 1e12 if achieved else None,
+                     "peak": peak_i8 / 1e12, "unit": "TOP/s (int8)",
+                     "frac": (2 * achieved / peak_i8) if achieved else None,
+                     "peak_source": "measured cuBLAS int8 GEMM 8192^3 (torch._int_mm), best of 10"})
+    else:
+        base.update({"bound": "int", "engine": "CUDA-core LOP3+POPC",
+                     "achieved": achieved / 1e12 if achieved else None,
+                     "peak": peak_popc / 1e12, "unit": "Tbit-op/s",
+                     "frac": (achieved / peak_popc) if achieved else None,
+                     "peak_source": "measured LOP3+POPC probe (scmp_probe_int_peak kind 0)"})
+    return base
+
+
 # ------------------------------------------------------------ reference arm
 
 def run_reference(args):
@@ -282,6 +329,30 @@ def main():
         blk.attn.qkv.register_forward_pre_hook(pre)
         blk.attn.qkv.register_forward_hook(post)
 
+    # per-operator time split (CUDA events around modules, timed region only)
+    split_events: dict = {"qkv_proj": [], "out_proj": [], "attention": []}
+
+    def timed(name):
+        def pre_h(mod, inp):
+            if recording["on"]:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                split_events[name].append([e, None])
+
+        def post_h(mod, inp, out):
+            if recording["on"]:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                split_events[name][-1][1] = e
+        return pre_h, post_h
+
+    for blk in model.backbone.blocks:
+        for name, mod in (("qkv_proj", blk.attn.qkv), ("out_proj", blk.attn.proj),
+                          ("attention", blk.attn)):
+            h0, h1 = timed(name)
+            mod.register_forward_pre_hook(h0)
+            mod.register_forward_hook(h1)
+
     def step(x):
         with torch.no_grad():
             y = model(x.to(dtype)).float()
@@ -320,6 +391,11 @@ def main():
     ms = float(ms_t.item())
     value = gbatch * args.steps / (ms / 1000.0)
 
+    split = {k: sum(a.elapsed_time(b) for a, b in v if b is not None) / args.steps
+             for k, v in split_events.items()}
+    split["attention_core"] = split.pop("attention") - split["qkv_proj"] - split["out_proj"]
+    split["rest_of_forward"] = ms / args.steps - sum(split.values())
+
     # roofline of the dominant SC matmul (qkv_proj): bit-products per call
     durs = [a.elapsed_time(b) for a, b in qkv_events if b is not None]
     qkv_ms = statistics.mean(durs) if durs else float("nan")
@@ -329,6 +405,8 @@ def main():
     qkv_bitops = bl * TOKENS * 1024 * 3072 * L_qkv
     achieved = qkv_bitops / (qkv_ms * 1e-3) if durs else None
     peak_popc = _lib.probe_int_peak(0)
+    peak_i8 = int8_tensor_peak(dev)
+    on_tc = args.engine in ("auto", "tcgen05") and 5 <= WORKLOADS[args.config]["sc_prec"] <= 8
 
     # end to end: pinned host images in, logits out, through the public API
     e2e = None
@@ -369,13 +447,8 @@ def main():
                              "activations per step)"},
             "e2e": e2e,
             "gpu_launches": int(launches),
-            "roofline": {"bound": "int", "kernel": "sc_matmul qkv_proj (popc engine)",
-                         "achieved": achieved / 1e12 if achieved else None,
-                         "peak": peak_popc / 1e12, "unit": "Tbit-op/s",
-                         "frac": (achieved / peak_popc) if achieved else None,
-                         "traffic": None, "per_launch_ms": qkv_ms,
-                         "algorithmic_per_launch": qkv_bitops,
-                         "peak_source": "measured LOP3+POPC probe (scmp_probe_int_peak kind 0)"},
+            "roofline": roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops),
+            "ms_per_step_split": split,
             "cpu_baseline": cpu,
             "clocks": clk,
             "build_s": build_s,

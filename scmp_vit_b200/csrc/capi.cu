@@ -283,6 +283,8 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
       return fail(SCMP_EUNSUPPORTED,
                   "tcgen05 engine needs 5 <= sc_prec <= 8, one K segment, and not unipolar at p=8");
     use_tc = true;
+  } else if (x.engine == SCMP_ENGINE_AUTO) {
+    use_tc = tc_supported(P);
   }
   int64_t m_tc = 0, n_tc = 0;
   if (use_tc) {

@@ -162,6 +162,66 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
   }
 }
 
+// Thin windows (the 257th row or column next to tensor-core tiles): one warp
+// per output, lanes split the reduction index, warp-sum of the signed counts.
+template <int LW>
+__global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t wm = P.m_hi - P.m_lo, wn = P.n_hi - P.n_lo;
+  const int64_t total = P.batch * wm * wn;
+  const int T = 1 << P.prec;
+  const int WT = T >= 32 ? T / 32 : 1;
+  for (int64_t o = wid; o < total; o += nwarps) {
+    const int64_t slice = o / (wm * wn);
+    const int64_t r = o % (wm * wn);
+    const int64_t gm = P.m_lo + r / wn, gn = P.n_lo + r % wn;
+    const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
+    const int64_t grow = slice * P.M + gm, brow = slice_b * P.N + gn;
+    const int L = row_stream_len(P, slice, grow);
+    if (L < 0) continue;  // warp-uniform
+    int acc = 0;
+    if (L > 0) {
+      const int16_t *ca = P.qa.code + grow * P.K;
+      const int16_t *cb = P.qb.code + brow * P.K;
+      for (int64_t d = lane; d < P.K; d += 32) {
+        const int a = ca[d], b = cb[d];
+        const int k = ((a < 0 ? -a : a) * L) >> P.prec;
+        const uint32_t *st = P.stream_table + ((d % P.pool_dims) * (T + 1) + (b < 0 ? -b : b)) * WT;
+        int cnt = 0;
+#pragma unroll
+        for (int w = 0; w < LW; ++w) {
+          const int lo = 32 * w;
+          const uint32_t win = k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
+          cnt += __popc(win & st[w]);
+        }
+        acc += ((a < 0) != (b < 0) ? -cnt : cnt);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    }
+    if (lane == 0) {
+      float y = 0.0f;
+      if (L > 0)
+        y = sc_rescale(P.mode, P.prec, L, acc, P.K, P.qa.scale[grow], P.qa.zero[grow],
+                       P.qa.rowsum[grow], P.qb.scale[brow], P.qb.zero[brow], P.qb.rowsum[brow]);
+      if (P.bias) y = __fadd_rn(y, P.bias[gn]);
+      P.out[grow * P.N + gn] = y;
+      if (P.acc_out) P.acc_out[grow * P.N + gn] = L > 0 ? acc : 0;
+    }
+  }
+}
+
+template <int LW>
+cudaError_t launch_thin(const GemmProblem &P, cudaStream_t s) {
+  const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
+  int64_t blocks = (total + 7) / 8;  // 8 warps per block, one output per warp
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  gemm_popc_thin_kernel<LW><<<(unsigned)blocks, 256, 0, s>>>(P);
+  return cudaGetLastError();
+}
+
 template <int LW>
 cudaError_t launch_lw(const GemmProblem &P, cudaStream_t s) {
   const size_t smem = PopcCfg<LW>::smem_bytes;
@@ -182,6 +242,13 @@ cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s) {
   const int T = 1 << P.prec;
   const int Lmax = (P.row_L || P.slice_L) ? T : P.stoc_len;
   const int lw = (Lmax + 31) / 32;
+  const bool thin = P.nseg == 1 && (P.m_hi - P.m_lo <= 16 || P.n_hi - P.n_lo <= 16);
+  if (thin) {
+    if (lw <= 1) return launch_thin<1>(P, s);
+    if (lw <= 2) return launch_thin<2>(P, s);
+    if (lw <= 4) return launch_thin<4>(P, s);
+    return launch_thin<8>(P, s);
+  }
   if (lw <= 1) return launch_lw<1>(P, s);
   if (lw <= 2) return launch_lw<2>(P, s);
   if (lw <= 4) return launch_lw<4>(P, s);

@@ -67,12 +67,13 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("engine", ["popc", "auto"])
 @pytest.mark.parametrize("M,N,K,p,L,mode", CASES)
-def test_per_row_parity(cuda_device, M, N, K, p, L, mode):
+def test_per_row_parity(cuda_device, M, N, K, p, L, mode, engine):
     g = torch.Generator().manual_seed(M * 1000 + N)
     a = torch.randn(M, K, generator=g)
     b = torch.randn(N, K, generator=g) * 0.05
-    _run(cuda_device, a, b, _cfg("sobol", K, p), sc_prec=p, stoc_len=L, mode=mode)
+    _run(cuda_device, a, b, _cfg("sobol", K, p), sc_prec=p, stoc_len=L, mode=mode, engine=engine)
 
 
 @pytest.mark.parametrize("kind", ["anti", "alt", "lfsr"])
@@ -174,6 +175,14 @@ def test_slice_stream_lengths(cuda_device):
                                                  sc_prec=8, pool=cfg["table"], stoc_len=L)
         np.testing.assert_array_equal(acc[s], acc_ref[0])
         np.testing.assert_allclose(y[s].cpu().numpy(), y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+@pytest.mark.parametrize("M,N", [(257, 16), (16, 300), (3, 257)])
+def test_thin_windows_on_cuda_cores(cuda_device, M, N):
+    g = torch.Generator().manual_seed(M + N)
+    a = torch.randn(2, M, 96, generator=g)
+    b = torch.randn(2, N, 96, generator=g)
+    _run(cuda_device, a, b, _cfg("sobol", 96, 7), sc_prec=7, stoc_len=128, engine="popc")
 
 
 def test_qkv_shape_full_size(cuda_device):
