@@ -13,7 +13,7 @@
 // thread issues tcgen05.mma for the stage.
 //
 // CTA tile: 256 rows of a (two 128-row UMMA accumulators) x BN rows of b,
-// all 2*BN TMEM columns; 3-stage smem ring; warp 0 issues MMAs, warps 1..8
+// all 2*BN TMEM columns; 3-stage smem ring; warp 0 issues MMAs, warps 1..16
 // generate operands and run the epilogue (rescale + bias + store).  Every wait
 // is bounded: on timeout the kernel raises the error flag and drains.
 #include <stdint.h>
@@ -26,7 +26,7 @@ namespace {
 constexpr int kBM = 256;           // a rows per tile (2 x UMMA_M 128)
 constexpr int kKB = 128;           // bytes (= inner elements) per k-block
 constexpr int kStages = 3;
-constexpr int kProducerWarps = 8;
+constexpr int kProducerWarps = 16;
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kThreads = 32 + kProducers;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -230,86 +230,110 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
     }
     __syncwarp();
   } else {
-    // ===================================== producers + epilogue (8 warps)
-    const int pt = threadIdx.x - 32;  // 0..255
-    const int chunk = pt & 7;         // 16-byte chunk of the 128-byte k-block row
-    const int rsub = pt >> 3;         // 0..31: rows rsub + 32 * i
+    // ============================ producers + epilogue (kProducerWarps warps)
+    // Thread pt fills 16-byte chunk `chunk` of a-rows rsub + 64 i (i < 4) and
+    // b-rows rsub + 64 i (i < kNB) of every k-block.  Codes and pool bytes of
+    // k-block kb + 1 are loaded while k-block kb is generated.
+    constexpr int kRowsA = kBM / 64;                 // 4
+    constexpr int kNB = BN >= 64 ? BN / 64 : 1;      // b rows per thread
+    const int pt = threadIdx.x - 32;                 // 0 .. kProducers-1
+    const int chunk = pt & 7;
+    const int rsub = pt >> 3;                        // 0 .. 63
     int stage = 0;
     uint32_t phase = 0;
     int64_t it = 0;
     bool ok = true;
-    const uint32_t tword0 = 0x03020100u, tstep = 0x04040404u;
+    const uint32_t tw0 = 0x03020100u, tw1 = 0x07060504u, tw2 = 0x0B0A0908u, tw3 = 0x0F0E0D0Cu;
+    // byte offsets of this thread's chunks inside the A / B stage (row r = rsub + 64 i)
+    const uint32_t offA0 = sw128_offset(rsub, chunk);
     for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++it) {
       const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
       const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
       const int64_t m0 = (rem % prm.tiles_m) * kBM;
       const int64_t n0 = (rem / prm.tiles_m) * BN;
       const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
-      // per-row stream length (a rows) for the 8 rows this thread fills
-      int Lrow[8];
-      const int16_t *arow[8];
+      int Lrow[kRowsA];
+      const int16_t *arow[kRowsA];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int64_t gm = m0 + rsub + 32 * i;
+      for (int i = 0; i < kRowsA; ++i) {
+        const int64_t gm = m0 + rsub + 64 * i;
         Lrow[i] = 0;
-        arow[i] = nullptr;
+        arow[i] = P.qa.code;  // dummy, never read when Lrow = 0 / invalid
         if (gm < prm.m_rows) {
           const int64_t grow = slice * P.M + gm;
           Lrow[i] = row_stream_len(P, slice, grow);
           arow[i] = P.qa.code + grow * P.K;
         }
       }
-      const int16_t *brow[BN / 32];
+      bool bval[kNB];
+      const int16_t *brow[kNB];
 #pragma unroll
-      for (int i = 0; i < BN / 32; ++i) {
-        const int64_t gn = n0 + rsub + 32 * i;
-        brow[i] = gn < prm.n_rows ? P.qb.code + (slice_b * P.N + gn) * P.K : nullptr;
+      for (int i = 0; i < kNB; ++i) {
+        const int64_t gn = n0 + rsub + 64 * i;
+        bval[i] = (rsub + 64 * i < BN) && gn < prm.n_rows;
+        brow[i] = bval[i] ? P.qb.code + (slice_b * P.N + gn) * P.K : P.qb.code;
       }
-
-      for (int64_t kb = 0; kb < prm.nkb; ++kb) {
-        const int64_t i0 = kb * kKB + chunk * 16;
+      // ---- prefetch k-block 0
+      int16_t ca_n[kRowsA], cb_n[kNB];
+      uint4 rr_n = make_uint4(0, 0, 0, 0);
+      int t0_n = 0;
+      {
+        const int64_t i0 = (int64_t)chunk * 16;
         const int64_t d = i0 >> prm.lp_log2;
-        const int t0 = (int)(i0 & (Lp - 1));
-        const bool dval = d < P.K;
-        // pool chunk R[d'][t0 .. t0+15] (shared by every b row of this lane)
-        uint4 rr = make_uint4(0, 0, 0, 0);
-        if (dval) {
-          rr = __ldg(reinterpret_cast<const uint4 *>(P.pool + (d % P.pool_dims) * T + t0));
-          if (prm.shift_pool) {
-            rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
-            rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
-          }
+        t0_n = (int)(i0 & (Lp - 1));
+        const bool dv = d < P.K;
+#pragma unroll
+        for (int i = 0; i < kRowsA; ++i) ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
+#pragma unroll
+        for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
+        if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (d % P.pool_dims) * T + t0_n));
+      }
+      for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+        int16_t ca[kRowsA], cb[kNB];
+#pragma unroll
+        for (int i = 0; i < kRowsA; ++i) ca[i] = ca_n[i];
+#pragma unroll
+        for (int i = 0; i < kNB; ++i) cb[i] = cb_n[i];
+        uint4 rr = rr_n;
+        const int t0 = t0_n;
+        if (kb + 1 < prm.nkb) {
+          const int64_t i0 = (kb + 1) * kKB + chunk * 16;
+          const int64_t d = i0 >> prm.lp_log2;
+          t0_n = (int)(i0 & (Lp - 1));
+          const bool dv = d < P.K;
+#pragma unroll
+          for (int i = 0; i < kRowsA; ++i) ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
+#pragma unroll
+          for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
+          rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (d % P.pool_dims) * T + t0_n))
+                    : make_uint4(0, 0, 0, 0);
         }
-        int16_t ca[8], cb[BN / 32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ca[i] = (dval && arow[i]) ? __ldg(arow[i] + d) : (int16_t)0;
-#pragma unroll
-        for (int i = 0; i < BN / 32; ++i) cb[i] = (dval && brow[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-
+        if (prm.shift_pool) {
+          rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
+          rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
+        }
         if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) { ok = false; break; }
         unsigned char *sa = smem + stage * Cfg::kStage;
         unsigned char *sb = sa + Cfg::kStageA;
         // ---- A: enable windows, sigma * [t < k]
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = rsub + 32 * i;
+        for (int i = 0; i < kRowsA; ++i) {
           const int c = ca[i];
-          const int mag = c < 0 ? -c : c;
-          const int k = (mag * Lrow[i]) >> P.prec;
+          const int k = ((c < 0 ? -c : c) * Lrow[i]) >> P.prec;
           const int q = min(max(k - t0, 0), 16);
           const uint32_t rep = (uint32_t)(0x7F + q) * 0x01010101u;
           const uint32_t sm = c < 0 ? 0xFFFFFFFFu : 0x01010101u;
           uint4 w;
-          w.x = prmt(rep - tword0, 0u, 0xBA98u) & sm;
-          w.y = prmt(rep - (tword0 + tstep), 0u, 0xBA98u) & sm;
-          w.z = prmt(rep - (tword0 + 2 * tstep), 0u, 0xBA98u) & sm;
-          w.w = prmt(rep - (tword0 + 3 * tstep), 0u, 0xBA98u) & sm;
-          *reinterpret_cast<uint4 *>(sa + sw128_offset(r, chunk)) = w;
+          w.x = prmt(rep - tw0, 0u, 0xBA98u) & sm;
+          w.y = prmt(rep - tw1, 0u, 0xBA98u) & sm;
+          w.z = prmt(rep - tw2, 0u, 0xBA98u) & sm;
+          w.w = prmt(rep - tw3, 0u, 0xBA98u) & sm;
+          *reinterpret_cast<uint4 *>(sa + offA0 + i * 8192) = w;  // +64 rows = 8 atoms
         }
         // ---- B: streams, sigma * [R[d'][t] < c_b]
 #pragma unroll
-        for (int i = 0; i < BN / 32; ++i) {
-          const int r = rsub + 32 * i;
+        for (int i = 0; i < kNB; ++i) {
+          if (rsub + 64 * i >= BN) break;
           const int c = cb[i];
           int u = c < 0 ? -c : c;
           if (prm.shift_pool) u >>= 1;
@@ -320,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
           w.y = prmt(rep - rr.y, 0u, 0xBA98u) & sm;
           w.z = prmt(rep - rr.z, 0u, 0xBA98u) & sm;
           w.w = prmt(rep - rr.w, 0u, 0xBA98u) & sm;
-          *reinterpret_cast<uint4 *>(sb + sw128_offset(r, chunk)) = w;
+          *reinterpret_cast<uint4 *>(sb + offA0 + i * 8192) = w;
         }
         fence_async_smem();
         mbar_arrive(&full_bar[stage]);
@@ -331,9 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       // ---- epilogue: TMEM -> rescale -> bias -> global
       if (!mbar_wait(tfull_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
       tc_fence_after();
-      const int pw = warp - 1;            // producer warp 0..7
-      const int acc_j = pw >> 2;          // accumulator (a rows 0-127 or 128-255)
-      const int quarter = warp & 3;       // TMEM lanes this warp may access
+      const int pw = warp - 1;                 // producer warp 0..15
+      const int quarter = warp & 3;            // TMEM lanes this warp may access
+      const int acc_j = (pw >> 2) & 1;         // accumulator (a rows 0-127 / 128-255)
+      const int col_half = pw >> 3;            // which half of the BN columns
       const int64_t gm = m0 + acc_j * 128 + quarter * 32 + lane;
       const bool row_ok = gm < prm.m_rows;
       int L = -1;
@@ -348,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
         rsa_ = P.qa.rowsum[grow];
       }
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
         uint32_t v[32];
         const uint32_t taddr =
             tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32);
@@ -388,7 +413,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       mbar_arrive(tempty_bar);
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
