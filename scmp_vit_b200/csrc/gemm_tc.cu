@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   uint64_t *tfull_bar = empty_bar + kStages;
   uint64_t *tempty_bar = tfull_bar + 1;
   uint64_t *drain_bar = tempty_bar + 1;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  uint64_t *epi_bar = drain_bar + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epi_bar + 1);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
     mbar_init(tfull_bar, 1);
     mbar_init(tempty_bar, kProducers);
     mbar_init(drain_bar, 1);
+    mbar_init(epi_bar, kProducers);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -352,63 +354,90 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       }
       if (!ok) break;
 
-      // ---- epilogue: TMEM -> rescale -> bias -> global
+      // ---- epilogue: TMEM -> smem transpose -> rescale -> bias -> coalesced stores.
+      // The stage ring is idle now (every MMA of this tile has completed), so
+      // each warp stages its 32x32 blocks there; a producer-only barrier
+      // below keeps the next tile's operand writes out until all are done.
       if (!mbar_wait(tfull_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
       tc_fence_after();
-      const int pw = warp - 1;                 // producer warp 0..15
-      const int quarter = warp & 3;            // TMEM lanes this warp may access
-      const int acc_j = (pw >> 2) & 1;         // accumulator (a rows 0-127 / 128-255)
-      const int col_half = pw >> 3;            // which half of the BN columns
-      const int64_t gm = m0 + acc_j * 128 + quarter * 32 + lane;
-      const bool row_ok = gm < prm.m_rows;
-      int L = -1;
-      float sa_ = 0.f;
-      int32_t za_ = 0, rsa_ = 0;
-      int64_t grow = 0;
-      if (row_ok) {
-        grow = slice * P.M + gm;
-        L = row_stream_len(P, slice, grow);
-        sa_ = P.qa.scale[grow];
-        za_ = P.qa.zero[grow];
-        rsa_ = P.qa.rowsum[grow];
-      }
+      {
+        const int pw = warp - 1;                 // producer warp 0..15
+        const int quarter = warp & 3;            // TMEM lanes this warp may access
+        const int acc_j = (pw >> 2) & 1;         // accumulator (a rows 0-127 / 128-255)
+        const int col_half = pw >> 3;            // which half of the BN columns
+        float *stg = reinterpret_cast<float *>(smem) + pw * (32 * 33);
+        int4 *rowp = reinterpret_cast<int4 *>(smem + kProducerWarps * 32 * 33 * 4) + pw * 32;
+        const int64_t mrow0 = m0 + acc_j * 128 + quarter * 32;  // first row of this warp
+        {
+          const int64_t gm = mrow0 + lane;
+          int L = -1, za = 0, rsa = 0;
+          float sa = 0.f;
+          if (gm < prm.m_rows) {
+            const int64_t grow = slice * P.M + gm;
+            L = row_stream_len(P, slice, grow);
+            sa = P.qa.scale[grow];
+            za = P.qa.zero[grow];
+            rsa = P.qa.rowsum[grow];
+          }
+          rowp[lane] = make_int4(L, __float_as_int(sa), za, rsa);
+        }
+        __syncwarp();
+        const int64_t grow0 = slice * P.M + mrow0;
 #pragma unroll 1
-      for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
-        uint32_t v[32];
-        const uint32_t taddr =
-            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-              "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
-              "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
-              "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
-              "=r"(v[30]), "=r"(v[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row_ok && L >= 0) {
-          const int64_t nb = n0 + cc * 32;
+        for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
+          uint32_t v[32];
+          const uint32_t taddr =
+              tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32);
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+                "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+                "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+                "=r"(v[30]), "=r"(v[31])
+              : "r"(taddr));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int64_t gn = nb + i;
-            if (gn >= prm.n_rows) continue;
-            const int32_t a = L > 0 ? (int32_t)v[i] : 0;
+          for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __int_as_float((int)v[i]);
+          __syncwarp();
+          // lane = column now
+          const int64_t gn = n0 + cc * 32 + lane;
+          const bool col_ok = gn < prm.n_rows;
+          float sb = 0.f;
+          int32_t zb = 0, rsb = 0;
+          float bias = 0.f;
+          if (col_ok) {
+            const int64_t brw = slice_b * P.N + gn;
+            sb = P.qb.scale[brw];
+            zb = P.qb.zero[brw];
+            rsb = P.qb.rowsum[brw];
+            if (P.bias) bias = P.bias[gn];
+          }
+#pragma unroll 4
+          for (int r = 0; r < 32; ++r) {
+            const int4 rp = rowp[r];  // broadcast
+            if (!col_ok || rp.x < 0) continue;
+            const int32_t a = rp.x > 0 ? __float_as_int(stg[r * 33 + lane]) : 0;
             float y = 0.0f;
-            if (L > 0) {
-              const int64_t brw = slice_b * P.N + gn;
-              y = sc_rescale(P.mode, P.prec, L, a, P.K, sa_, za_, rsa_, P.qb.scale[brw],
-                             P.qb.zero[brw], P.qb.rowsum[brw]);
-            }
-            if (P.bias) y = __fadd_rn(y, P.bias[gn]);
-            const int64_t o = grow * P.N + gn;
+            if (rp.x > 0)
+              y = sc_rescale(P.mode, P.prec, rp.x, a, P.K, __int_as_float(rp.y), rp.z, rp.w, sb,
+                             zb, rsb);
+            if (P.bias) y = __fadd_rn(y, bias);
+            const int64_t o = (grow0 + r) * P.N + gn;
             P.out[o] = y;
             if (P.acc_out) P.acc_out[o] = a;
           }
+          __syncwarp();
         }
       }
+      // every producer is done with the staging area before anyone refills it
+      // (a bounded mbarrier wait, not bar.sync: an aborting thread must not
+      // leave the others blocked)
+      mbar_arrive(epi_bar);
+      if (!mbar_wait(epi_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
       tc_fence_before();
       mbar_arrive(tempty_bar);
     }
