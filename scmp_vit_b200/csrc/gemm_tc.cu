@@ -18,6 +18,9 @@
 // is bounded: on timeout the kernel raises the error flag and drains.
 #include <stdint.h>
 
+#include <mutex>
+#include <vector>
+
 #include "sc_common.cuh"
 
 namespace scmp {
@@ -37,7 +40,8 @@ struct TcCfg {
   static constexpr uint32_t kStageB = BN * kKB;
   static constexpr uint32_t kStage = kStageA + kStageB;
   static constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 128
-  static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t kTherm = 2 * 129 * 128;  // enable-window rows (table path)
+  static constexpr size_t kSmem = (size_t)kStages * kStage + kTherm + 1024 /*align*/ + 256;
 };
 
 struct TcParams {
@@ -49,6 +53,7 @@ struct TcParams {
   int64_t n_rows;   // rows of b handled per slice (window [0, n_rows))
   int64_t tiles_m, tiles_n, tiles;
   unsigned int *error;
+  const unsigned char *therm;  // enable-window rows (table path), see therm_table
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -149,14 +154,15 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
 
 // ------------------------------------------------------------------ kernel
 
-template <int BN>
+template <int BN, bool kBulkA>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm) {
   using Cfg = TcCfg<BN>;
   const GemmProblem &P = prm.P;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + kStages * Cfg::kStage);
+  unsigned char *therm_s = smem + kStages * Cfg::kStage;  // [sign][window 0..128][128 B]
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(therm_s + Cfg::kTherm);
   uint64_t *empty_bar = full_bar + kStages;
   uint64_t *tfull_bar = empty_bar + kStages;
   uint64_t *tempty_bar = tfull_bar + 1;
@@ -170,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], kProducers);
+      mbar_init(&full_bar[s], kProducerWarps);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(tfull_bar, 1);
@@ -186,12 +192,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
                  "r"(Cfg::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  if constexpr (kBulkA) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(prm.therm);
+    uint4 *dst = reinterpret_cast<uint4 *>(therm_s);
+    for (int i = threadIdx.x; i < (int)(Cfg::kTherm / 16); i += blockDim.x) dst[i] = __ldg(src + i);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int T = 1 << P.prec;
   const int64_t Lp = (int64_t)1 << prm.lp_log2;
+  // 32-bit index math in the k-block loop: K * Lp < 2^31 and pool_dims >= K
+  // are guaranteed by the launcher (tc_supported / launch_gemm_tc).
+  const int lg = prm.lp_log2;
+  const int Lp32 = 1 << lg;
+  const int K32 = (int)P.K;
 
   if (warp == 0) {
     // ================================================= MMA issuer (lane 0)
@@ -280,15 +296,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       uint4 rr_n = make_uint4(0, 0, 0, 0);
       int t0_n = 0;
       {
-        const int64_t i0 = (int64_t)chunk * 16;
-        const int64_t d = i0 >> prm.lp_log2;
-        t0_n = (int)(i0 & (Lp - 1));
-        const bool dv = d < P.K;
+        const int i0 = chunk * 16;
+        const int d = i0 >> lg;
+        t0_n = i0 & (Lp32 - 1);
+        const bool dv = d < K32;
 #pragma unroll
-        for (int i = 0; i < kRowsA; ++i) ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
+        for (int i = 0; i < kRowsA; ++i)
+          ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
 #pragma unroll
         for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-        if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (d % P.pool_dims) * T + t0_n));
+        if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (d * T + t0_n)));
       }
       for (int64_t kb = 0; kb < prm.nkb; ++kb) {
         int16_t ca[kRowsA], cb[kNB];
@@ -298,28 +315,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
         for (int i = 0; i < kNB; ++i) cb[i] = cb_n[i];
         uint4 rr = rr_n;
         const int t0 = t0_n;
+        // k-block start inside its reduction index (table path: one d per k-block)
+        const int t0_blk = ((int)kb * kKB) & (Lp32 - 1);
         if (kb + 1 < prm.nkb) {
-          const int64_t i0 = (kb + 1) * kKB + chunk * 16;
-          const int64_t d = i0 >> prm.lp_log2;
-          t0_n = (int)(i0 & (Lp - 1));
-          const bool dv = d < P.K;
+          const int i0 = ((int)kb + 1) * kKB + chunk * 16;
+          const int d = i0 >> lg;
+          t0_n = i0 & (Lp32 - 1);
+          const bool dv = d < K32;
 #pragma unroll
-          for (int i = 0; i < kRowsA; ++i) ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
+          for (int i = 0; i < kRowsA; ++i)
+            ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
 #pragma unroll
           for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-          rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (d % P.pool_dims) * T + t0_n))
+          rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (d * T + t0_n)))
                     : make_uint4(0, 0, 0, 0);
         }
         if (prm.shift_pool) {
           rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
           rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
         }
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) { ok = false; break; }
+        {
+          int w_ok = 1;
+          if (lane == 0) w_ok = mbar_wait(&empty_bar[stage], phase ^ 1, abort) ? 1 : 0;
+          w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+          if (!w_ok) { ok = false; break; }
+        }
         unsigned char *sa = smem + stage * Cfg::kStage;
         unsigned char *sb = sa + Cfg::kStageA;
         // ---- A: enable windows, sigma * [t < k]
+        if constexpr (kBulkA) {
+          // one k-block = 128 stream positions of one reduction index: copy
+          // chunk `chunk` of the window row (sign, q) from the smem table
 #pragma unroll
-        for (int i = 0; i < kRowsA; ++i) {
+          for (int i = 0; i < kRowsA; ++i) {
+            const int c = ca[i];
+            const int k = ((c < 0 ? -c : c) * Lrow[i]) >> P.prec;
+            const int q = min(max(k - t0_blk, 0), 128);
+            const uint4 w = *reinterpret_cast<const uint4 *>(
+                therm_s + ((((c < 0 ? 129 : 0) + q) << 7) + (chunk << 4)));
+            *reinterpret_cast<uint4 *>(sa + offA0 + i * 8192) = w;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < (kBulkA ? 0 : kRowsA); ++i) {
           const int c = ca[i];
           const int k = ((c < 0 ? -c : c) * Lrow[i]) >> P.prec;
           const int q = min(max(k - t0, 0), 16);
@@ -348,8 +386,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
           w.w = prmt(rep - rr.w, 0u, 0xBA98u) & sm;
           *reinterpret_cast<uint4 *>(sb + offA0 + i * 8192) = w;
         }
+        // every lane publishes its writes to the async proxy, then one lane
+        // per warp arrives (release covers the warp's writes via __syncwarp)
         fence_async_smem();
-        mbar_arrive(&full_bar[stage]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_bar[stage]);
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
@@ -452,21 +493,51 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   if (threadIdx.x == 0 && *abort) atomicOr(prm.error, 1u);
 }
 
-template <int BN>
+template <int BN, bool kBulkA>
 cudaError_t launch_bn(const TcParams &prm, int sms, cudaStream_t s) {
   const size_t smem = TcCfg<BN>::kSmem;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN>,
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, kBulkA>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int64_t grid = prm.tiles < sms ? prm.tiles : sms;
-  gemm_tc_kernel<BN><<<(unsigned)grid, kThreads, smem, s>>>(prm);
+  gemm_tc_kernel<BN, kBulkA><<<(unsigned)grid, kThreads, smem, s>>>(prm);
   return cudaGetLastError();
+}
+
+// Enable-window rows for the table path: [sign 0/1][window 0..128] x 128
+// bytes, byte t = (t < window) ? (sign ? -1 : +1) : 0.  Copied into shared
+// memory by every CTA; a producer copies chunk c of row (sign, window).
+constexpr size_t kThermBytes = (size_t)2 * 129 * 128;
+__device__ __align__(128) unsigned char g_therm[kThermBytes];
+std::mutex g_therm_mu;
+const unsigned char *g_therm_ptr[64] = {};
+
+const unsigned char *therm_table(cudaError_t *err) {
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_therm_mu);
+  if (!g_therm_ptr[dev]) {
+    std::vector<unsigned char> h(kThermBytes, 0);
+    for (int sg = 0; sg < 2; ++sg)
+      for (int q = 0; q <= 128; ++q) {
+        unsigned char *row = h.data() + ((size_t)(sg * 129 + q) << 7);
+        for (int t = 0; t < 128; ++t) row[t] = t < q ? (sg ? 0xFF : 0x01) : 0x00;
+      }
+    if ((*err = cudaMemcpyToSymbol(g_therm, h.data(), kThermBytes)) != cudaSuccess) return nullptr;
+    void *p = nullptr;
+    if ((*err = cudaGetSymbolAddress(&p, g_therm)) != cudaSuccess) return nullptr;
+    g_therm_ptr[dev] = static_cast<const unsigned char *>(p);
+  }
+  return g_therm_ptr[dev];
 }
 
 }  // namespace
 
 bool tc_supported(const GemmProblem &P) {
   if (P.prec < 5 || P.prec > 8) return false;           // pool rows >= 32 bytes
+  if (P.pool_dims < P.K) return false;                  // reduction index = pool row
+  if (P.K * 256 >= (int64_t)1 << 31) return false;      // 32-bit k-block index math
   if (P.nseg != 1) return false;                        // segmented K: popc engine
   if (P.mode == SCMP_UNIPOLAR && P.prec == 8) return false;  // 8-bit thresholds
   return true;
@@ -496,9 +567,19 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (bn == 64) return launch_bn<64>(prm, sms, s);
-  if (bn == 128) return launch_bn<128>(prm, sms, s);
-  return launch_bn<256>(prm, sms, s);
+  // Table path: every k-block lies inside one reduction index, and the tile is
+  // narrow, so enable windows dominate the operand generation.
+  if (lg >= 7 && bn == 64) {
+    cudaError_t e;
+    prm.therm = therm_table(&e);
+    if (!prm.therm) return e != cudaSuccess ? e : cudaErrorUnknown;
+    if (bn == 64) return launch_bn<64, true>(prm, sms, s);
+    if (bn == 128) return launch_bn<128, true>(prm, sms, s);
+    return launch_bn<256, true>(prm, sms, s);
+  }
+  if (bn == 64) return launch_bn<64, false>(prm, sms, s);
+  if (bn == 128) return launch_bn<128, false>(prm, sms, s);
+  return launch_bn<256, false>(prm, sms, s);
 }
 
 }  // namespace scmp
