@@ -296,9 +296,9 @@ def main():
         gbatch = args.batch * (world if wl["scaling"] == "weak" else 1)
     else:
         gbatch = wl["batch"] * (world if wl["scaling"] == "weak" else 1)
-    if gbatch % world:
-        raise SystemExit(f"global batch {gbatch} not divisible by {world} ranks")
-    bl = gbatch // world
+    from scmp_vit_b200.dist import gather_logits, shard_range
+    lo, hi = shard_range(gbatch, rank, world)
+    bl = hi - lo
     dtype = torch.bfloat16
     t_build = time.perf_counter()
     model = build_model(args.config, dev, dtype)
@@ -356,10 +356,7 @@ def main():
     def step(x):
         with torch.no_grad():
             y = model(x.to(dtype)).float()
-        if world > 1:
-            dist.all_gather_into_tensor(logits_all, y.contiguous())
-        else:
-            logits_all.copy_(y)
+        gather_logits(y, gbatch, world, out=logits_all)
         return y
 
     def barrier():
