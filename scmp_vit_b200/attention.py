@@ -27,6 +27,7 @@ from .mp import (
     adaptive_classify_rows,
     classify_rows_by_metric,
     get_current_block_idx,
+    quantile_counts,
     quantile_levels_batched,
 )
 from .mp_linear import sc_prec_for_stoc_len
@@ -91,6 +92,59 @@ def _run_levels(a, b, table: torch.Tensor, levels, per: str, *, granularity: str
     return out
 
 
+def _qk_slices_by_prec(qf, kf, head_L: torch.Tensor, B: int, levels, counts, *, D: int,
+                       cfg_for: CfgFor, out: torch.Tensor) -> torch.Tensor:
+    """Per-head levels with host-known counts: the slices of each precision
+    class are gathered, run in one launch, and scattered back."""
+    H = head_L.numel()
+    order = torch.sort(head_L.to(torch.int32), stable=True).indices  # heads by level
+    Ls = head_L.to(torch.int32).index_select(0, order)
+    base = torch.arange(B, device=qf.device).unsqueeze(1) * H
+    start = sum(c for L, c in counts.items() if int(L) <= 0)
+    if start:
+        idx = (base + order[:start].unsqueeze(0)).reshape(-1)
+        out.index_fill_(0, idx, 0.0)
+    for p, Lset in _levels_by_prec(levels).items():
+        n = sum(counts.get(L, 0) for L in Lset)
+        if n == 0:
+            continue
+        heads = order[start:start + n]
+        idx = (base + heads.unsqueeze(0)).reshape(-1)            # slices b*H + h
+        sl = Ls[start:start + n].unsqueeze(0).expand(B, n).reshape(-1)
+        res = sc_matmul(qf.index_select(0, idx), kf.index_select(0, idx), granularity="per_head",
+                        mode="bipolar", sc_prec=p, config=cfg_for(D, p), slice_stoc_len=sl)
+        out.index_copy_(0, idx, res)
+        start += n
+    return out
+
+
+def _av_rows_by_prec(a_flat, b_flat, row_L: torch.Tensor, levels, counts, *, mode: str,
+                     D_pool: int, cfg_for: CfgFor, out: torch.Tensor) -> torch.Tensor:
+    """Per-row levels inside every slice with the same host-known counts per
+    slice: rows are sorted by level inside each slice, each precision class
+    runs as one batched launch over its rows, results are scattered back."""
+    S, M, K = a_flat.shape
+    order = torch.sort(row_L, dim=1, stable=True).indices          # [S, M]
+    Ls = torch.gather(row_L, 1, order)
+    a_sorted = torch.gather(a_flat, 1, order.unsqueeze(-1).expand(S, M, K))
+    N = b_flat.shape[1]
+    out_sorted = torch.empty(S, M, N, dtype=torch.float32, device=a_flat.device)
+    start = sum(c for L, c in counts.items() if int(L) <= 0)
+    if start:
+        out_sorted[:, :start] = 0.0
+    for p, Lset in _levels_by_prec(levels).items():
+        n = sum(counts.get(L, 0) for L in Lset)
+        if n == 0:
+            continue
+        res = sc_matmul(a_sorted[:, start:start + n].contiguous(), b_flat, granularity="per_row",
+                        mode=mode, sc_prec=p, config=cfg_for(D_pool, p),
+                        row_stoc_len=Ls[:, start:start + n].reshape(-1))
+        out_sorted[:, start:start + n] = res
+        start += n
+    out.scatter_(1, order.unsqueeze(-1).expand(S, M, N), out_sorted)
+    return out
+
+
 def sc_qk(q: torch.Tensor, k: torch.Tensor, sc_prec: int, *, mp_cfg=None,
           cfg_for: Optional[CfgFor] = None) -> torch.Tensor:
     """SC ``q @ k^T`` for q, k ``[B, H, N, D]`` -> ``[B, H, N, N]`` fp32, unscaled."""
@@ -117,6 +171,14 @@ def sc_qk(q: torch.Tensor, k: torch.Tensor, sc_prec: int, *, mp_cfg=None,
                                   head_L.clamp(min=0).to(torch.float64).sum() * B * N * N)
     slice_L = head_L.to(torch.int32).repeat(B)  # slice b*H + h -> head h
     out = torch.empty(B * H, N, N, dtype=torch.float32, device=q.device)
+    counts = None if isinstance(mp_cfg, AdaptiveMPConfig) and mp_cfg.target_fractions is None \
+        else quantile_counts(H, mp_cfg.stoc_len_levels,
+                             getattr(mp_cfg, "level_fractions", None)
+                             if not isinstance(mp_cfg, AdaptiveMPConfig) else mp_cfg.target_fractions)
+    if counts is not None and not _scl.USE_NOISE_MODEL and len(_levels_by_prec(mp_cfg.stoc_len_levels)) > 1:
+        _qk_slices_by_prec(qf, kf, head_L, B, mp_cfg.stoc_len_levels, counts, D=D,
+                           cfg_for=cfg_for, out=out)
+        return out.reshape(B, H, N, N)
     if _scl.USE_NOISE_MODEL:
         for L in sorted({int(v) for v in mp_cfg.stoc_len_levels}):
             sel = slice_L == L
@@ -159,6 +221,12 @@ def sc_av(attn: torch.Tensor, v: torch.Tensor, sc_prec: int, *, mode: str = "bip
         AutoMPBudgetLogger.record(get_current_block_idx(), "av", B * H * N * D * maxL,
                                   row_L.clamp(min=0).to(torch.float64).sum() * D)
     out = torch.empty(B * H, N, D, dtype=torch.float32, device=v.device)
+    if (not isinstance(mp_cfg, AdaptiveMPConfig) and not _scl.USE_NOISE_MODEL
+            and len(_levels_by_prec(mp_cfg.stoc_len_levels)) > 1):
+        counts = quantile_counts(N, mp_cfg.stoc_len_levels, mp_cfg.level_fractions)
+        _av_rows_by_prec(a_flat, b_flat, row_L.reshape(B * H, N), mp_cfg.stoc_len_levels, counts,
+                         mode=mode, D_pool=N, cfg_for=cfg_for, out=out)
+        return out.reshape(B, H, N, D)
     if _scl.USE_NOISE_MODEL:
         out.zero_()
         flat_a = a_flat.reshape(B * H * N, N)

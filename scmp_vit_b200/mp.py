@@ -36,6 +36,7 @@ __all__ = [
     "classify_rows_by_metric", "adaptive_classify_rows", "classify_groups_by_range",
     "set_current_block_idx", "get_current_block_idx", "AutoMPBudgetLogger",
     "MPDistributionLogger", "MetricProfiler", "quantile_levels_batched", "SeededRandomMPConfig",
+    "quantile_counts",
 ]
 
 _BLOCK = threading.local()
@@ -141,9 +142,13 @@ class RowAssignment:
     ``r`` (device tensor); ``level_row_indices`` maps every level to the
     ascending LongTensor of its rows (built lazily, needs a host sync)."""
 
-    def __init__(self, row_levels: torch.Tensor, levels: Sequence[int]):
+    def __init__(self, row_levels: torch.Tensor, levels: Sequence[int],
+                 host_counts: Optional[Dict[int, int]] = None):
         self.row_levels = row_levels
         self.levels = [int(v) for v in levels]
+        # rows per level when the split fixes them without looking at the
+        # data (quantile splits); None when only the device knows
+        self.host_counts = host_counts
         self._idx: Optional[Dict[int, torch.Tensor]] = None
 
     @property
@@ -178,11 +183,13 @@ def _quantile_split(metric: torch.Tensor, levels, fractions) -> RowAssignment:
     order = torch.sort(metric, descending=True, stable=True).indices
     row_levels = torch.empty(n, dtype=torch.int32, device=metric.device)
     start = 0
+    host = {}
     for L, c in zip(lv, counts):
         if c:
             row_levels[order[start:start + c]] = L
+        host[L] = host.get(L, 0) + c
         start += c
-    return RowAssignment(row_levels, lv)
+    return RowAssignment(row_levels, lv, host_counts=host)
 
 
 def _normalise(metric: torch.Tensor) -> torch.Tensor:
@@ -207,6 +214,24 @@ def classify_rows_by_metric(metric: torch.Tensor, stoc_len_levels, level_fractio
                             ) -> RowAssignment:
     """Fixed-quantile split (higher metric -> longer stream)."""
     return _quantile_split(metric, stoc_len_levels, level_fractions)
+
+
+def quantile_counts(n: int, levels, fractions=None) -> Dict[int, int]:
+    """Rows per level of a quantile split of ``n`` rows (host-side)."""
+    if fractions is None:
+        fractions = [1.0 / len(levels)] * len(levels)
+    total = float(sum(fractions)) or 1.0
+    lv, fr = _sorted_levels(list(levels), [f / total for f in fractions])
+    counts = [int(round(f * n)) for f in fr[:-1]]
+    used = 0
+    for i, c in enumerate(counts):
+        counts[i] = max(0, min(c, n - used))
+        used += counts[i]
+    counts.append(n - used)
+    out: Dict[int, int] = {}
+    for L, c in zip(lv, counts):
+        out[L] = out.get(L, 0) + c
+    return out
 
 
 def quantile_levels_batched(metric: torch.Tensor, levels, fractions=None) -> torch.Tensor:

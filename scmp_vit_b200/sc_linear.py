@@ -121,10 +121,16 @@ def _mm_one_bucket(x_sub: torch.Tensor, w_sub: torch.Tensor, stoc_len: int, sc_p
 def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
                    levels: Iterable[int], mode: str, *, bias: Optional[torch.Tensor] = None,
                    out: Optional[torch.Tensor] = None, chunk_d: int = 0,
-                   cfg_for: Optional[Callable[[int, int], dict]] = None) -> torch.Tensor:
+                   cfg_for: Optional[Callable[[int, int], dict]] = None,
+                   host_counts: Optional[dict] = None) -> torch.Tensor:
     """Per-row stream lengths in grouped launches: one engine call per
     distinct precision among ``levels`` (the host-known set of values that
-    ``row_L`` may hold; 0 = pruned row -> bias only)."""
+    ``row_L`` may hold; 0 = pruned row -> bias only).
+
+    With ``host_counts`` (rows per level, known without a device sync for
+    quantile splits) the rows are sorted by level once and every call runs
+    on its own contiguous rows only; otherwise every call spans all rows and
+    skips the others (``row_stoc_len = -1``)."""
     M, K = x2.shape
     N = w.shape[0]
     if out is None:
@@ -139,6 +145,27 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
             out += bias.float()
         return out
     row_L = row_L.to(torch.int32)
+    use_chunk = chunk_d > 0 and mode == "bipolar" and K > chunk_d
+    if host_counts is not None and len(by_prec) > 1:
+        # rows ordered by level: pruned first, then each precision's levels
+        order = torch.sort(row_L, stable=True).indices
+        xs = x2.index_select(0, order)
+        Ls = row_L.index_select(0, order)
+        ys = torch.empty(M, N, dtype=torch.float32, device=x2.device)
+        start = sum(c for L, c in host_counts.items() if int(L) <= 0)
+        if start:
+            ys[:start] = 0.0 if bias is None else bias.float()
+        for p, Lset in by_prec.items():
+            n_rows = sum(host_counts.get(L, 0) for L in Lset)
+            if n_rows == 0:
+                continue
+            cfg = cfg_for(chunk_d if use_chunk else K, p)
+            sc_matmul(xs[start:start + n_rows], w, granularity="per_row", mode=mode, sc_prec=p,
+                      config=cfg, chunk_d=chunk_d if use_chunk else 0, bias=bias,
+                      row_stoc_len=Ls[start:start + n_rows], out=ys[start:start + n_rows])
+            start += n_rows
+        out.index_copy_(0, order, ys)
+        return out
     first = True
     for p, Ls in by_prec.items():
         mask = torch.zeros_like(row_L, dtype=torch.bool)
@@ -147,7 +174,6 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
         if first:
             mask |= row_L <= 0  # the first launch writes the pruned rows
         sel = torch.where(mask, row_L.clamp(min=0), torch.full_like(row_L, -1))
-        use_chunk = chunk_d > 0 and mode == "bipolar" and K > chunk_d
         cfg = cfg_for(chunk_d if use_chunk else K, p)
         sc_matmul(x2, w, granularity="per_row", mode=mode, sc_prec=p, config=cfg,
                   chunk_d=chunk_d if use_chunk else 0, bias=bias, row_stoc_len=sel, out=out)
@@ -214,7 +240,8 @@ def _sc_linear_mp(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int, mod
         return result.to(x.dtype).reshape(*orig_shape[:-1], D_out)
 
     if range_entries is None:
-        result = sc_linear_rows(x_flat, w, row_L, levels, mode, bias=bias, chunk_d=chunk_d)
+        result = sc_linear_rows(x_flat, w, row_L, levels, mode, bias=bias, chunk_d=chunk_d,
+                                host_counts=None if assign is None else assign.host_counts)
     else:
         result = torch.empty(M, D_out, dtype=torch.float32, device=x.device)
         for e in range_entries:

@@ -24,7 +24,7 @@ import torch.nn.functional as F
 
 from .attention import make_sc_attention_forward
 from .head_aligned_comp import HeadAlignedSCLinear
-from .mp import SeededRandomMPConfig, set_current_block_idx
+from .mp import SeededRandomMPConfig, quantile_counts, set_current_block_idx
 from .sc_linear import SCLinear, _get_config, sc_linear_rows
 
 
@@ -162,8 +162,9 @@ class _RowMPLinear(nn.Module):
         x2 = x.reshape(-1, shp[-1]).float()
         row_L = self.cfg.assign(x2.shape[0], x2.device, salt=(self.salt << 16) + self.calls)
         self.calls += 1
+        counts = quantile_counts(x2.shape[0], self.cfg.stoc_len_levels, self.cfg.level_fractions)
         y = sc_linear_rows(x2, self.weight.float(), row_L, self.cfg.stoc_len_levels, "bipolar",
-                           bias=self.bias, cfg_for=self.cfg_for)
+                           bias=self.bias, cfg_for=self.cfg_for, host_counts=counts)
         return y.to(x.dtype).reshape(*shp[:-1], -1)
 
 
