@@ -291,7 +291,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
     unsigned int *err = engine_error_ptr();
     if (!err) return fail(SCMP_ECUDA, "cannot resolve the engine error word");
     m_tc = tc_rows(x.M, 256);
-    n_tc = tc_rows(x.N, tc_block_n(x.N));
+    n_tc = tc_rows(x.N, tc_tile_n(P, x.N));
     if ((e = launch_gemm_tc(P, m_tc, n_tc, err, s)) != cudaSuccess)
       return cuda_fail(e, "gemm_tc launch");
     count_launches(1);

@@ -39,7 +39,7 @@ struct TcCfg {
   static constexpr uint32_t kStageA = kBM * kKB;  // 32 KB
   static constexpr uint32_t kStageB = BN * kKB;
   static constexpr uint32_t kStage = kStageA + kStageB;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 128
+  static constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 128 (x2 when segmented)
   static constexpr uint32_t kTherm = 2 * 129 * 128;  // enable-window rows (table path)
   static constexpr size_t kSmem = (size_t)kStages * kStage + kTherm + 1024 /*align*/ + 256;
 };
@@ -54,6 +54,9 @@ struct TcParams {
   int64_t tiles_m, tiles_n, tiles;
   unsigned int *error;
   const unsigned char *therm;  // enable-window rows (table path), see therm_table
+  int nseg;                    // K segments (1 = unsegmented)
+  int kseg;                    // reduction indices per segment
+  int64_t nkb_seg;             // k-blocks per segment (nkb = nseg * nkb_seg)
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -125,6 +128,38 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
+// 32 consecutive TMEM columns of this warp's 32 lanes (lane i -> row i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+
 // K-major, 128-byte-swizzled UMMA shared-memory descriptor: 8-row atoms of
 // 128 B (1024 B apart), version 1, layout SWIZZLE_128B.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
@@ -154,9 +189,13 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
 
 // ------------------------------------------------------------------ kernel
 
-template <int BN, bool kBulkA>
+template <int BN, bool kBulkA, bool kSeg>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm) {
   using Cfg = TcCfg<BN>;
+  // int32 accumulators in columns [0, 2 BN); segmented kernels keep the fp32
+  // running sum of the finished segments in columns [2 BN, 4 BN)
+  constexpr uint32_t kTmemAlloc = kSeg ? 4 * BN : 2 * BN;
+  static_assert(!kSeg || BN <= 128, "segmented tiles need 4*BN <= 512 TMEM columns");
   const GemmProblem &P = prm.P;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
@@ -189,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(Cfg::kTmemCols));
+                 "r"(kTmemAlloc));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if constexpr (kBulkA) {
@@ -208,6 +247,72 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   const int lg = prm.lp_log2;
   const int Lp32 = 1 << lg;
   const int K32 = (int)P.K;
+  // pool row of reduction index d: d itself, or d's index inside its segment
+  // (segmented problems use a (k_segment, p) pool shared by every segment)
+  auto pool_row = [&](int d) -> int { return kSeg ? d % prm.kseg : d; };
+
+  // Segmented tiles: 16 columns (half `h` of 32-column chunk `cc`) of this
+  // warp's rows after segment `sd` -- rescale the int32 counts with the
+  // segment's scales and add the fp32 sum of the earlier segments (held in
+  // TMEM columns 2 BN ..).  Result in y (fp32 bits).
+  auto seg_chunk = [&](int sd, int cc, int h, int acc_j, int quarter, int64_t grow, bool row_ok,
+                       int L, int64_t slice_b, int64_t n0, uint32_t (&y)[16]) {
+    float sa = 0.f;
+    int za = 0, rsa = 0;
+    if (row_ok && L > 0) {
+      const int64_t ra = grow * prm.nseg + sd;
+      sa = P.qa.scale[ra];
+      za = P.qa.zero[ra];
+      rsa = P.qa.rowsum[ra];
+    }
+    const int64_t gn = n0 + cc * 32 + h * 16 + (lane & 15);
+    float sbl = 0.f;
+    int zbl = 0, rsbl = 0;
+    if (gn < prm.n_rows) {
+      const int64_t rb = (slice_b * P.N + gn) * prm.nseg + sd;
+      sbl = P.qb.scale[rb];
+      zbl = P.qb.zero[rb];
+      rsbl = P.qb.rowsum[rb];
+    }
+    const uint32_t col = (uint32_t)(acc_j * BN + cc * 32 + h * 16);
+    const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    uint32_t f[16];
+    tmem_ld16(lanebase + col, y);
+    if (sd > 0) tmem_ld16(lanebase + (uint32_t)(2 * BN) + col, f);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float sb = __shfl_sync(0xffffffffu, sbl, i);
+      const int zb = __shfl_sync(0xffffffffu, zbl, i);
+      const int rsb = __shfl_sync(0xffffffffu, rsbl, i);
+      const float r = (row_ok && L > 0)
+                          ? sc_rescale(P.mode, P.prec, L, (int32_t)y[i], prm.kseg, sa, za, rsa,
+                                       sb, zb, rsb)
+                          : 0.0f;
+      y[i] = __float_as_uint(sd == 0 ? r : __fadd_rn(__uint_as_float(f[i]), r));
+    }
+  };
+  auto seg_drain = [&](int sd, int64_t slice, int64_t slice_b, int64_t m0, int64_t n0) {
+    const int pw = warp - 1;
+    const int quarter = warp & 3;
+    const int acc_j = (pw >> 2) & 1;
+    const int col_half = pw >> 3;
+    const int64_t gm = m0 + acc_j * 128 + quarter * 32 + lane;
+    const bool row_ok = gm < prm.m_rows;
+    const int64_t grow = slice * P.M + gm;
+    const int L = row_ok ? row_stream_len(P, slice, grow) : -1;
+    const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+    for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t y[16];
+        seg_chunk(sd, cc, h, acc_j, quarter, grow, row_ok, L, slice_b, n0, y);
+        tmem_st16(lanebase + (uint32_t)(2 * BN + acc_j * BN + cc * 32 + h * 16), y);
+      }
+    }
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  };
 
   if (warp == 0) {
     // ================================================= MMA issuer (lane 0)
@@ -218,29 +323,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       uint32_t phase = 0;
       int64_t it = 0;
       bool ok = true;
+      int64_t g = 0;  // drain counter: one per (tile, segment)
       for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++it) {
-        if (it > 0) ok = mbar_wait(tempty_bar, (uint32_t)((it - 1) & 1), abort);
-        if (!ok) break;
-        tc_fence_after();
-        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+        for (int seg = 0; seg < prm.nseg && ok; ++seg, ++g) {
+          // the accumulators are free once the previous drain has read them
+          if (g > 0) ok = mbar_wait(tempty_bar, (uint32_t)((g - 1) & 1), abort);
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t a0 = smem0 + stage * Cfg::kStage;
-          const uint32_t b0 = a0 + Cfg::kStageA;
+          for (int64_t kb = 0; kb < prm.nkb_seg; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a0 = smem0 + stage * Cfg::kStage;
+            const uint32_t b0 = a0 + Cfg::kStageA;
 #pragma unroll
-          for (int kk = 0; kk < kKB / 32; ++kk) {
-            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+            for (int kk = 0; kk < kKB / 32; ++kk) {
+              const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
-              tc_mma_i8(tmem_base + j * BN, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              for (int j = 0; j < 2; ++j) {
+                const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+                tc_mma_i8(tmem_base + j * BN, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              }
             }
+            tc_commit(&empty_bar[stage]);
+            if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
-          tc_commit(&empty_bar[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
+          if (!ok) break;
+          tc_commit(tfull_bar);
         }
-        if (!ok) break;
-        tc_commit(tfull_bar);
       }
       // Drain: everything this thread issued has completed before TMEM is freed.
       tc_commit(drain_bar);
@@ -260,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
     int stage = 0;
     uint32_t phase = 0;
     int64_t it = 0;
+    int64_t g = 0;  // drain counter, as on the MMA side
     bool ok = true;
     const uint32_t tw0 = 0x03020100u, tw1 = 0x07060504u, tw2 = 0x0B0A0908u, tw3 = 0x0F0E0D0Cu;
     // byte offsets of this thread's chunks inside the A / B stage (row r = rsub + 64 i)
@@ -305,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
           ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
 #pragma unroll
         for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-        if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (d * T + t0_n)));
+        if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (pool_row(d) * T + t0_n)));
       }
       for (int64_t kb = 0; kb < prm.nkb; ++kb) {
         int16_t ca[kRowsA], cb[kNB];
@@ -327,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
             ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
 #pragma unroll
           for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-          rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (d * T + t0_n)))
+          rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (pool_row(d) * T + t0_n)))
                     : make_uint4(0, 0, 0, 0);
         }
         if (prm.shift_pool) {
@@ -392,6 +502,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_bar[stage]);
         if (++stage == kStages) { stage = 0; phase ^= 1; }
+        if constexpr (kSeg) {
+          if ((kb + 1) % prm.nkb_seg == 0 && kb + 1 < prm.nkb) {
+            // ---- end of a non-final segment: int32 accumulators -> rescale with
+            // this segment's scales -> add to the fp32 running sum in TMEM
+            const int sd = (int)(kb / prm.nkb_seg);
+            if (!mbar_wait(tfull_bar, (uint32_t)(g & 1), abort)) { ok = false; break; }
+            tc_fence_after();
+            seg_drain(sd, slice, slice_b, m0, n0);
+            tc_fence_before();
+            mbar_arrive(tempty_bar);
+            ++g;
+          }
+        }
       }
       if (!ok) break;
 
@@ -399,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       // The stage ring is idle now (every MMA of this tile has completed), so
       // each warp stages its 32x32 blocks there; a producer-only barrier
       // below keeps the next tile's operand writes out until all are done.
-      if (!mbar_wait(tfull_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
+      if (!mbar_wait(tfull_bar, (uint32_t)(g & 1), abort)) { ok = false; break; }
       tc_fence_after();
       {
         const int pw = warp - 1;                 // producer warp 0..15
@@ -424,25 +547,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
         }
         __syncwarp();
         const int64_t grow0 = slice * P.M + mrow0;
+        const int myL = rowp[lane].x;  // stream length of this lane's row
 #pragma unroll 1
         for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
-          uint32_t v[32];
-          const uint32_t taddr =
-              tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32);
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-                "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
-                "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
-                "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-                "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
-                "=r"(v[30]), "=r"(v[31])
-              : "r"(taddr));
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if constexpr (kSeg) {
+            // last segment: finished fp32 values (rescaled and summed in order)
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              uint32_t v[16];
+              seg_chunk(prm.nseg - 1, cc, h, acc_j, quarter, grow0 + lane,
+                        mrow0 + lane < prm.m_rows, myL, slice_b, n0, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __int_as_float((int)v[i]);
+              for (int i = 0; i < 16; ++i) stg[lane * 33 + h * 16 + i] = __uint_as_float(v[i]);
+            }
+          } else {
+            uint32_t v[32];
+            tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                          (uint32_t)(acc_j * BN + cc * 32),
+                      v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __uint_as_float(v[i]);
+          }
           __syncwarp();
           // lane = column now
           const int64_t gn = n0 + cc * 32 + lane;
@@ -463,13 +589,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
             if (!col_ok || rp.x < 0) continue;
             const int32_t a = rp.x > 0 ? __float_as_int(stg[r * 33 + lane]) : 0;
             float y = 0.0f;
-            if (rp.x > 0)
+            if constexpr (kSeg) {
+              if (rp.x > 0) y = stg[r * 33 + lane];
+            } else if (rp.x > 0) {
               y = sc_rescale(P.mode, P.prec, rp.x, a, P.K, __int_as_float(rp.y), rp.z, rp.w, sb,
                              zb, rsb);
+            }
             if (P.bias) y = __fadd_rn(y, bias);
             const int64_t o = (grow0 + r) * P.N + gn;
             P.out[o] = y;
-            if (P.acc_out) P.acc_out[o] = a;
+            if (!kSeg && P.acc_out) P.acc_out[o] = a;
           }
           __syncwarp();
         }
@@ -481,6 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       if (!mbar_wait(epi_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
       tc_fence_before();
       mbar_arrive(tempty_bar);
+      ++g;
     }
   }
   tc_fence_before();
@@ -488,19 +618,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(Cfg::kTmemCols));
+                 "r"(kTmemAlloc));
   }
   if (threadIdx.x == 0 && *abort) atomicOr(prm.error, 1u);
 }
 
-template <int BN, bool kBulkA>
+template <int BN, bool kBulkA, bool kSeg = false>
 cudaError_t launch_bn(const TcParams &prm, int sms, cudaStream_t s) {
   const size_t smem = TcCfg<BN>::kSmem;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, kBulkA>,
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, kBulkA, kSeg>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int64_t grid = prm.tiles < sms ? prm.tiles : sms;
-  gemm_tc_kernel<BN, kBulkA><<<(unsigned)grid, kThreads, smem, s>>>(prm);
+  gemm_tc_kernel<BN, kBulkA, kSeg><<<(unsigned)grid, kThreads, smem, s>>>(prm);
   return cudaGetLastError();
 }
 
@@ -534,32 +664,49 @@ const unsigned char *therm_table(cudaError_t *err) {
 
 }  // namespace
 
+namespace {
+int padded_stream_log2(const GemmProblem &P) {
+  const int T = 1 << P.prec;
+  const int Lmax = (P.row_L || P.slice_L) ? T : P.stoc_len;
+  int lg = 5;
+  while ((1 << lg) < Lmax) ++lg;
+  return lg;
+}
+}  // namespace
+
 bool tc_supported(const GemmProblem &P) {
   if (P.prec < 5 || P.prec > 8) return false;           // pool rows >= 32 bytes
-  if (P.pool_dims < P.K) return false;                  // reduction index = pool row
   if (P.K * 256 >= (int64_t)1 << 31) return false;      // 32-bit k-block index math
-  if (P.nseg != 1) return false;                        // segmented K: popc engine
   if (P.mode == SCMP_UNIPOLAR && P.prec == 8) return false;  // 8-bit thresholds
-  return true;
+  if (P.nseg == 1) return P.pool_dims >= P.K;           // reduction index = pool row
+  // segmented K: whole k-blocks per segment, pool row = index inside segment;
+  // the per-segment counts are not summed into acc_out on this engine
+  if (P.pool_dims < P.kseg || P.acc_out) return false;
+  return ((P.kseg << padded_stream_log2(P)) % kKB) == 0;
 }
 
 int tc_block_n(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
+
+int tc_tile_n(const GemmProblem &P, int64_t N) {
+  const int bn = tc_block_n(N);
+  return (P.nseg > 1 && bn > 128) ? 128 : bn;
+}
 
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
                            unsigned int *error, cudaStream_t s) {
   if (P.M == 0 || P.N == 0 || P.batch == 0 || m_rows == 0 || n_rows == 0) return cudaSuccess;
   TcParams prm{};
   prm.P = P;
-  const int T = 1 << P.prec;
-  const int Lmax = (P.row_L || P.slice_L) ? T : P.stoc_len;
-  int lg = 5;
-  while ((1 << lg) < Lmax) ++lg;
+  const int lg = padded_stream_log2(P);
   prm.lp_log2 = lg;
   prm.shift_pool = (P.mode == SCMP_BIPOLAR && P.prec == 8) ? 1 : 0;
   prm.nkb = (P.K * ((int64_t)1 << lg) + kKB - 1) / kKB;
+  prm.nseg = P.nseg;
+  prm.kseg = (int)P.kseg;
+  prm.nkb_seg = P.nseg > 1 ? ((P.kseg << lg) / kKB) : prm.nkb;
   prm.m_rows = m_rows;
   prm.n_rows = n_rows;
-  const int bn = tc_block_n(n_rows);
+  const int bn = tc_tile_n(P, n_rows);
   prm.tiles_m = (m_rows + kBM - 1) / kBM;
   prm.tiles_n = (n_rows + bn - 1) / bn;
   prm.tiles = P.batch * prm.tiles_m * prm.tiles_n;
@@ -569,13 +716,15 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   // Table path: every k-block lies inside one reduction index, and the tile is
   // narrow, so enable windows dominate the operand generation.
+  if (P.nseg > 1) {
+    if (bn == 64) return launch_bn<64, false, true>(prm, sms, s);
+    return launch_bn<128, false, true>(prm, sms, s);
+  }
   if (lg >= 7 && bn == 64) {
     cudaError_t e;
     prm.therm = therm_table(&e);
     if (!prm.therm) return e != cudaSuccess ? e : cudaErrorUnknown;
-    if (bn == 64) return launch_bn<64, true>(prm, sms, s);
-    if (bn == 128) return launch_bn<128, true>(prm, sms, s);
-    return launch_bn<256, true>(prm, sms, s);
+    return launch_bn<64, true>(prm, sms, s);
   }
   if (bn == 64) return launch_bn<64, false>(prm, sms, s);
   if (bn == 128) return launch_bn<128, false>(prm, sms, s);

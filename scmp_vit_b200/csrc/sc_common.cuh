@@ -90,6 +90,7 @@ cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, ui
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 bool tc_supported(const GemmProblem &P);
 int tc_block_n(int64_t N);
+int tc_tile_n(const GemmProblem &P, int64_t N);
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
                            unsigned int *error, cudaStream_t s);
 

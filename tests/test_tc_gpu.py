@@ -94,3 +94,29 @@ def test_tc_qkv_image(cuda_device):
     a = torch.randn(257, 1024, generator=g)
     b = torch.nn.init.trunc_normal_(torch.empty(3072, 1024), std=0.02, generator=g)
     _check(cuda_device, a, b, 7, 128, granularity="per_tensor")
+
+
+@pytest.mark.parametrize("M,N,K,kseg,p,L,mode", [
+    (256, 128, 256, 64, 8, 256, "bipolar"),    # head-aligned: 4 heads of 64, L=256
+    (300, 200, 128, 32, 7, 128, "bipolar"),    # row tail 44 (padded tile), BN=128 + column tail
+    (256, 64, 192, 64, 7, 100, "unipolar"),    # BN=64, L not a power of two
+])
+def test_tc_segments(cuda_device, M, N, K, kseg, p, L, mode):
+    """Segmented K on the tensor cores: per-segment quantisation and rescale,
+    fp32 segment sums in order (head-aligned compensation, chunk-D sum)."""
+    dev = cuda_device
+    g = torch.Generator().manual_seed(M + K + kseg)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    if mode == "unipolar":
+        a = a.abs()
+    bias = torch.randn(N, generator=g)
+    random.seed(9)
+    cfg = ch.make_sobol_simple_config(kseg, kseg, p)
+    y = sc_matmul(a.to(dev), b.to(dev), mode=mode, sc_prec=p, config=cfg, stoc_len=L,
+                  k_segment=kseg, bias=bias.to(dev), engine="tcgen05")
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    _, y_ref = sc_oracle.sc_matmul_segments_ref(a.numpy(), b.numpy(), kseg, mode=mode, sc_prec=p,
+                                                pool=cfg["table"], stoc_len=L, bias=bias.numpy())
+    np.testing.assert_allclose(y.cpu().numpy(), y_ref[0], rtol=RTOL, atol=1e-30)
