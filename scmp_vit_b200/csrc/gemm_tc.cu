@@ -122,6 +122,19 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t tmem_d, uint64_t adesc, uint6
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
@@ -240,6 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint32_t smem_s = smem_u32(smem);     // 32-bit shared-window addresses
+  const uint32_t therm_u = smem_u32(therm_s);
   const int T = 1 << P.prec;
   const int64_t Lp = (int64_t)1 << prm.lp_log2;
   // 32-bit index math in the k-block loop: K * Lp < 2^31 and pool_dims >= K
@@ -444,14 +459,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
           rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
           rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
         }
+        // byte j of (u * 0x01010101 + base_w) is 0x7F + u - R[t0+4w+j]; its top
+        // bit is [R < u] (no borrows: u, R < 128), read by the sign-replicating
+        // byte permute
+        const uint32_t rb0 = 0x7F7F7F7Fu - rr.x, rb1 = 0x7F7F7F7Fu - rr.y;
+        const uint32_t rb2 = 0x7F7F7F7Fu - rr.z, rb3 = 0x7F7F7F7Fu - rr.w;
         {
           int w_ok = 1;
           if (lane == 0) w_ok = mbar_wait(&empty_bar[stage], phase ^ 1, abort) ? 1 : 0;
           w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
           if (!w_ok) { ok = false; break; }
         }
-        unsigned char *sa = smem + stage * Cfg::kStage;
-        unsigned char *sb = sa + Cfg::kStageA;
+        const uint32_t sa_s = smem_s + (uint32_t)stage * Cfg::kStage + offA0;
+        const uint32_t sb_s = sa_s + Cfg::kStageA;
         // ---- A: enable windows, sigma * [t < k]
         if constexpr (kBulkA) {
           // one k-block = 128 stream positions of one reduction index: copy
@@ -459,42 +479,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
 #pragma unroll
           for (int i = 0; i < kRowsA; ++i) {
             const int c = ca[i];
-            const int k = ((c < 0 ? -c : c) * Lrow[i]) >> P.prec;
+            const int k = (abs(c) * Lrow[i]) >> P.prec;
             const int q = min(max(k - t0_blk, 0), 128);
-            const uint4 w = *reinterpret_cast<const uint4 *>(
-                therm_s + ((((c < 0 ? 129 : 0) + q) << 7) + (chunk << 4)));
-            *reinterpret_cast<uint4 *>(sa + offA0 + i * 8192) = w;
+            const uint4 w =
+                ld_shared_v4(therm_u + (uint32_t)((((c < 0 ? 129 : 0) + q) << 7) + (chunk << 4)));
+            st_shared_v4(sa_s + i * 8192, w.x, w.y, w.z, w.w);
           }
         }
 #pragma unroll
         for (int i = 0; i < (kBulkA ? 0 : kRowsA); ++i) {
           const int c = ca[i];
-          const int k = ((c < 0 ? -c : c) * Lrow[i]) >> P.prec;
-          const int q = min(max(k - t0, 0), 16);
-          const uint32_t rep = (uint32_t)(0x7F + q) * 0x01010101u;
-          const uint32_t sm = c < 0 ? 0xFFFFFFFFu : 0x01010101u;
-          uint4 w;
-          w.x = prmt(rep - tw0, 0u, 0xBA98u) & sm;
-          w.y = prmt(rep - tw1, 0u, 0xBA98u) & sm;
-          w.z = prmt(rep - tw2, 0u, 0xBA98u) & sm;
-          w.w = prmt(rep - tw3, 0u, 0xBA98u) & sm;
-          *reinterpret_cast<uint4 *>(sa + offA0 + i * 8192) = w;  // +64 rows = 8 atoms
+          const int k = (abs(c) * Lrow[i]) >> P.prec;
+          const uint32_t q = (uint32_t)min(max(k - t0, 0), 16);
+          const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
+          // byte j of (q * 0x01010101 + 0x7F7F7F7F - tw) is 0x7F + q - j: top bit = [j < q]
+          st_shared_v4(sa_s + i * 8192,  // +64 rows = 8 atoms
+                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw0), 0u, 0xBA98u) & sm,
+                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw1), 0u, 0xBA98u) & sm,
+                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw2), 0u, 0xBA98u) & sm,
+                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw3), 0u, 0xBA98u) & sm);
         }
         // ---- B: streams, sigma * [R[d'][t] < c_b]
 #pragma unroll
         for (int i = 0; i < kNB; ++i) {
           if (rsub + 64 * i >= BN) break;
           const int c = cb[i];
-          int u = c < 0 ? -c : c;
-          if (prm.shift_pool) u >>= 1;
-          const uint32_t rep = (uint32_t)(0x7F + u) * 0x01010101u;
-          const uint32_t sm = c < 0 ? 0xFFFFFFFFu : 0x01010101u;
-          uint4 w;
-          w.x = prmt(rep - rr.x, 0u, 0xBA98u) & sm;
-          w.y = prmt(rep - rr.y, 0u, 0xBA98u) & sm;
-          w.z = prmt(rep - rr.z, 0u, 0xBA98u) & sm;
-          w.w = prmt(rep - rr.w, 0u, 0xBA98u) & sm;
-          *reinterpret_cast<uint4 *>(sb + offA0 + i * 8192) = w;
+          const uint32_t u = (uint32_t)(abs(c) >> prm.shift_pool);
+          const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
+          st_shared_v4(sb_s + i * 8192,
+                       prmt(u * 0x01010101u + rb0, 0u, 0xBA98u) & sm,
+                       prmt(u * 0x01010101u + rb1, 0u, 0xBA98u) & sm,
+                       prmt(u * 0x01010101u + rb2, 0u, 0xBA98u) & sm,
+                       prmt(u * 0x01010101u + rb3, 0u, 0xBA98u) & sm);
         }
         // every lane publishes its writes to the async proxy, then one lane
         // per warp arrives (release covers the warp's writes via __syncwarp)
