@@ -108,6 +108,7 @@ void layout_operand(Carver &c, OperandLayout &o, int64_t K) {
 struct Plan {
   OperandLayout A, B;
   size_t table = 0;
+  size_t pool_comp = 0;
   size_t total = 0;
 };
 
@@ -162,6 +163,7 @@ Plan make_plan(const scmp_matmul_args *x) {
   const int T = 1 << x->sc_prec;
   const int WT = T >= 32 ? T / 32 : 1;
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
+  p.pool_comp = c.take((size_t)x->pool_dims * T);
   p.total = c.off;
   return p;
 }
@@ -272,6 +274,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.out = x.out;
   P.acc_out = x.acc_out;
   P.stream_table = table;
+  P.pool_comp = ws + plan.pool_comp;
   P.m_lo = 0;
   P.m_hi = x.M;
   P.n_lo = 0;
@@ -292,6 +295,13 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
     if (!err) return fail(SCMP_ECUDA, "cannot resolve the engine error word");
     m_tc = tc_rows(x.M, 256);
     n_tc = tc_rows(x.N, tc_tile_n(P, x.N));
+    if (tc_row_producers(P)) {
+      const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
+      if ((e = launch_pool_complement(x.pool, x.pool_dims, x.sc_prec, shift,
+                                      ws + plan.pool_comp, s)) != cudaSuccess)
+        return cuda_fail(e, "pool_complement launch");
+      count_launches(1);
+    }
     if ((e = launch_gemm_tc(P, m_tc, n_tc, err, s)) != cudaSuccess)
       return cuda_fail(e, "gemm_tc launch");
     count_launches(1);

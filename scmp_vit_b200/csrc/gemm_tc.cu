@@ -16,6 +16,11 @@
 // all 2*BN TMEM columns; 3-stage smem ring; warp 0 issues MMAs, warps 1..16
 // generate operands and run the epilogue (rescale + bias + store).  Every wait
 // is bounded: on timeout the kernel raises the error flag and drains.
+//
+// Two producer layouts: row producers (a thread owns one a row and one b row
+// of the tile, codes arrive 8 reduction indices per 16-byte load; K % 8 == 0
+// and Lp >= 64) and chunk producers (a thread owns one 16-byte chunk column of
+// several rows; every other supported shape).
 #include <stdint.h>
 
 #include <mutex>
@@ -41,7 +46,11 @@ struct TcCfg {
   static constexpr uint32_t kStage = kStageA + kStageB;
   static constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 128 (x2 when segmented)
   static constexpr uint32_t kTherm = 2 * 129 * 128;  // enable-window rows (table path)
-  static constexpr size_t kSmem = (size_t)kStages * kStage + kTherm + 1024 /*align*/ + 256;
+  // Dynamic shared memory; kernels without the table leave those 33 KB to L1
+  // (at most 196 KB of shared memory keeps a ~60 KB L1 for the pool rows).
+  static constexpr size_t smem_bytes(bool table) {
+    return (size_t)kStages * kStage + (table ? kTherm : 0) + 1024 /*align*/ + 256;
+  }
 };
 
 struct TcParams {
@@ -57,6 +66,10 @@ struct TcParams {
   int nseg;                    // K segments (1 = unsegmented)
   int kseg;                    // reduction indices per segment
   int64_t nkb_seg;             // k-blocks per segment (nkb = nseg * nkb_seg)
+  // Passed at run time so that byte-broadcast products and stage offsets
+  // compile to IMADs (the FMA pipe) rather than shifts and adds (the ALU pipe).
+  uint32_t rep;          // 0x01010101
+  uint32_t stage_bytes;  // TcCfg<BN>::kStage
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -121,6 +134,76 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t tmem_d, uint64_t adesc, uint6
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// ---- CTA pairs (cta_group::2): the even CTA of a 2-CTA cluster issues the
+// MMAs for both; every other wait on a peer is an mbarrier with a bound.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `addr` (a shared::cta address) in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Cluster-scope release: issued only by threads with no global loads in
+// flight (a release waits for them), never by the producers per k-block.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (arrivals from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  while (true) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    if (*abort) return false;
+    if (now_ns() - t0 > kTimeoutNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+// Both CTAs of the pair reach this point (every path to it is bounded).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tc_mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Completion of this thread's pair MMAs arrives on `bar` in both CTAs (the
+// barrier sits at the same shared-memory offset in each).
+__device__ __forceinline__ void tc_commit_pair_both(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((unsigned short)3)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair_local(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -202,61 +285,149 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
 
 // ------------------------------------------------------------------ kernel
 
-template <int BN, bool kBulkA, bool kSeg>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm) {
-  using Cfg = TcCfg<BN>;
-  // int32 accumulators in columns [0, 2 BN); segmented kernels keep the fp32
-  // running sum of the finished segments in columns [2 BN, 4 BN)
-  constexpr uint32_t kTmemAlloc = kSeg ? 4 * BN : 2 * BN;
-  static_assert(!kSeg || BN <= 128, "segmented tiles need 4*BN <= 512 TMEM columns");
+// Producer kinds.
+constexpr int kProdChunks = 0;  // thread = (row group, 16-byte chunk); windows by byte compares
+constexpr int kProdTable = 1;   // as kProdChunks, enable windows copied from a smem table
+constexpr int kProdRows = 2;    // thread = one a row and one b row (see produce_rows)
+
+// Shared-memory barriers and the abort word (carved after the stage ring).
+struct Bars {
+  uint64_t *full, *empty, *tfull, *tempty, *drain, *epi;
+  volatile int *abort;
+  // CTA pairs: the even CTA's peer-stage barriers pfull[] (arrived on by the
+  // odd CTA's forwarder thread) and tempty, as shared::cluster addresses
+  uint64_t *pfull;
+  uint32_t pfull_cl, tempty_cl;
+};
+
+// Producer-side pipeline position (per thread).
+struct ProdState {
+  int stage;
+  uint32_t phase;
+  int64_t g;  // drain counter: one per (tile, segment), as on the MMA side
+};
+
+// Every lane polls (one issue slot per poll, like a single lane, but the warp
+// never diverges); the lanes agree on the outcome.
+__device__ __forceinline__ bool acquire_stage(const Bars &b, const ProdState &st, int lane) {
+  (void)lane;
+  const bool ok = mbar_wait(&b.empty[st.stage], st.phase ^ 1, b.abort);
+  return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// Every lane publishes its writes to the async proxy, then one lane per warp
+// arrives (the release covers the warp's writes through __syncwarp).
+template <int NS = kStages>
+__device__ __forceinline__ void publish_stage(const Bars &b, ProdState &st, int lane) {
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&b.full[st.stage]);
+  if (++st.stage == NS) {
+    st.stage = 0;
+    st.phase ^= 1;
+  }
+}
+
+// Segmented tiles: 16 columns (half `h` of 32-column chunk `cc`) of this
+// warp's rows after segment `sd` -- rescale the int32 counts with the
+// segment's scales and add the fp32 sum of the earlier segments (held in
+// TMEM columns 2 BN ..).  Result in y (fp32 bits).
+template <int BN>
+__device__ __forceinline__ void seg_chunk(const TcParams &prm, uint32_t tmem_base, int lane,
+                                          int sd, int cc, int h, int acc_j, int quarter,
+                                          int64_t grow, bool row_ok, int L, int64_t slice_b,
+                                          int64_t n0, uint32_t (&y)[16]) {
   const GemmProblem &P = prm.P;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char *smem = reinterpret_cast<unsigned char *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char *therm_s = smem + kStages * Cfg::kStage;  // [sign][window 0..128][128 B]
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(therm_s + Cfg::kTherm);
-  uint64_t *empty_bar = full_bar + kStages;
-  uint64_t *tfull_bar = empty_bar + kStages;
-  uint64_t *tempty_bar = tfull_bar + 1;
-  uint64_t *drain_bar = tempty_bar + 1;
-  uint64_t *epi_bar = drain_bar + 1;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epi_bar + 1);
-  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  float sa = 0.f;
+  int za = 0, rsa = 0;
+  if (row_ok && L > 0) {
+    const int64_t ra = grow * prm.nseg + sd;
+    sa = P.qa.scale[ra];
+    za = P.qa.zero[ra];
+    rsa = P.qa.rowsum[ra];
+  }
+  const int64_t gn = n0 + cc * 32 + h * 16 + (lane & 15);
+  float sbl = 0.f;
+  int zbl = 0, rsbl = 0;
+  if (gn < prm.n_rows) {
+    const int64_t rb = (slice_b * P.N + gn) * prm.nseg + sd;
+    sbl = P.qb.scale[rb];
+    zbl = P.qb.zero[rb];
+    rsbl = P.qb.rowsum[rb];
+  }
+  const uint32_t col = (uint32_t)(acc_j * BN + cc * 32 + h * 16);
+  const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+  uint32_t f[16];
+  tmem_ld16(lanebase + col, y);
+  if (sd > 0) tmem_ld16(lanebase + (uint32_t)(2 * BN) + col, f);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float sb = __shfl_sync(0xffffffffu, sbl, i);
+    const int zb = __shfl_sync(0xffffffffu, zbl, i);
+    const int rsb = __shfl_sync(0xffffffffu, rsbl, i);
+    const float r = (row_ok && L > 0) ? sc_rescale(P.mode, P.prec, L, (int32_t)y[i], prm.kseg, sa,
+                                                   za, rsa, sb, zb, rsb)
+                                      : 0.0f;
+    y[i] = __float_as_uint(sd == 0 ? r : __fadd_rn(__uint_as_float(f[i]), r));
+  }
+}
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], kProducerWarps);
-      mbar_init(&empty_bar[s], 1);
-    }
-    mbar_init(tfull_bar, 1);
-    mbar_init(tempty_bar, kProducers);
-    mbar_init(drain_bar, 1);
-    mbar_init(epi_bar, kProducers);
-    *abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kTmemAlloc));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  if constexpr (kBulkA) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(prm.therm);
-    uint4 *dst = reinterpret_cast<uint4 *>(therm_s);
-    for (int i = threadIdx.x; i < (int)(Cfg::kTherm / 16); i += blockDim.x) dst[i] = __ldg(src + i);
-  }
-  tc_fence_before();
-  __syncthreads();
+// End of a non-final segment: wait for its MMAs, fold the int32 counts into
+// the fp32 running sums in TMEM, hand the accumulators back to the MMA warp.
+template <int BN>
+__device__ bool segment_drain(const TcParams &prm, const Bars &b, ProdState &st,
+                              uint32_t tmem_base, int warp, int lane, int sd, int64_t slice,
+                              int64_t slice_b, int64_t m0, int64_t n0) {
+  const GemmProblem &P = prm.P;
+  if (!mbar_wait(b.tfull, (uint32_t)(st.g & 1), b.abort)) return false;
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const uint32_t smem_s = smem_u32(smem);     // 32-bit shared-window addresses
-  const uint32_t therm_u = smem_u32(therm_s);
+  const int pw = warp - 1;
+  const int quarter = warp & 3;
+  const int acc_j = (pw >> 2) & 1;
+  const int col_half = pw >> 3;
+  const int64_t gm = m0 + acc_j * 128 + quarter * 32 + lane;
+  const bool row_ok = gm < prm.m_rows;
+  const int64_t grow = slice * P.M + gm;
+  const int L = row_ok ? row_stream_len(P, slice, grow) : -1;
+  const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+  for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      uint32_t y[16];
+      seg_chunk<BN>(prm, tmem_base, lane, sd, cc, h, acc_j, quarter, grow, row_ok, L, slice_b, n0,
+                    y);
+      tmem_st16(lanebase + (uint32_t)(2 * BN + acc_j * BN + cc * 32 + h * 16), y);
+    }
+  }
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  tc_fence_before();
+  mbar_arrive(b.tempty);
+  ++st.g;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Chunk producers: thread pt fills 16-byte chunk `chunk` of a-rows rsub + 64 i
+// (i < 4) and b-rows rsub + 64 i (i < BN / 64) of every k-block.  Codes and
+// pool bytes of k-block kb + 1 are loaded while k-block kb is generated.
+// Handles every supported shape (ragged K, Lp = 32).
+template <int BN, bool kBulkA, bool kSeg>
+__device__ bool produce_chunks(const TcParams &prm, const Bars &b, ProdState &st,
+                               uint32_t smem_s, uint32_t therm_u, uint32_t tmem_base, int warp,
+                               int lane, int64_t slice, int64_t slice_b, int64_t m0, int64_t n0) {
+  using Cfg = TcCfg<BN>;
+  const GemmProblem &P = prm.P;
+  constexpr int kRowsA = kBM / 64;             // 4
+  constexpr int kNB = BN >= 64 ? BN / 64 : 1;  // b rows per thread
+  const int pt = threadIdx.x - 32;             // 0 .. kProducers-1
+  const int chunk = pt & 7;
+  const int rsub = pt >> 3;  // 0 .. 63
   const int T = 1 << P.prec;
-  const int64_t Lp = (int64_t)1 << prm.lp_log2;
   // 32-bit index math in the k-block loop: K * Lp < 2^31 and pool_dims >= K
   // are guaranteed by the launcher (tc_supported / launch_gemm_tc).
   const int lg = prm.lp_log2;
@@ -265,69 +436,467 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   // pool row of reduction index d: d itself, or d's index inside its segment
   // (segmented problems use a (k_segment, p) pool shared by every segment)
   auto pool_row = [&](int d) -> int { return kSeg ? d % prm.kseg : d; };
+  const uint32_t tw0 = 0x03020100u, tw1 = 0x07060504u, tw2 = 0x0B0A0908u, tw3 = 0x0F0E0D0Cu;
+  // byte offsets of this thread's chunks inside the A / B stage (row r = rsub + 64 i)
+  const uint32_t offA0 = sw128_offset(rsub, chunk);
 
-  // Segmented tiles: 16 columns (half `h` of 32-column chunk `cc`) of this
-  // warp's rows after segment `sd` -- rescale the int32 counts with the
-  // segment's scales and add the fp32 sum of the earlier segments (held in
-  // TMEM columns 2 BN ..).  Result in y (fp32 bits).
-  auto seg_chunk = [&](int sd, int cc, int h, int acc_j, int quarter, int64_t grow, bool row_ok,
-                       int L, int64_t slice_b, int64_t n0, uint32_t (&y)[16]) {
-    float sa = 0.f;
-    int za = 0, rsa = 0;
-    if (row_ok && L > 0) {
-      const int64_t ra = grow * prm.nseg + sd;
-      sa = P.qa.scale[ra];
-      za = P.qa.zero[ra];
-      rsa = P.qa.rowsum[ra];
-    }
-    const int64_t gn = n0 + cc * 32 + h * 16 + (lane & 15);
-    float sbl = 0.f;
-    int zbl = 0, rsbl = 0;
-    if (gn < prm.n_rows) {
-      const int64_t rb = (slice_b * P.N + gn) * prm.nseg + sd;
-      sbl = P.qb.scale[rb];
-      zbl = P.qb.zero[rb];
-      rsbl = P.qb.rowsum[rb];
-    }
-    const uint32_t col = (uint32_t)(acc_j * BN + cc * 32 + h * 16);
-    const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    uint32_t f[16];
-    tmem_ld16(lanebase + col, y);
-    if (sd > 0) tmem_ld16(lanebase + (uint32_t)(2 * BN) + col, f);
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  int Lrow[kRowsA];
+  const int16_t *arow[kRowsA];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float sb = __shfl_sync(0xffffffffu, sbl, i);
-      const int zb = __shfl_sync(0xffffffffu, zbl, i);
-      const int rsb = __shfl_sync(0xffffffffu, rsbl, i);
-      const float r = (row_ok && L > 0)
-                          ? sc_rescale(P.mode, P.prec, L, (int32_t)y[i], prm.kseg, sa, za, rsa,
-                                       sb, zb, rsb)
-                          : 0.0f;
-      y[i] = __float_as_uint(sd == 0 ? r : __fadd_rn(__uint_as_float(f[i]), r));
+  for (int i = 0; i < kRowsA; ++i) {
+    const int64_t gm = m0 + rsub + 64 * i;
+    Lrow[i] = 0;
+    arow[i] = P.qa.code;  // dummy, never read when Lrow = 0 / invalid
+    if (gm < prm.m_rows) {
+      const int64_t grow = slice * P.M + gm;
+      Lrow[i] = row_stream_len(P, slice, grow);
+      arow[i] = P.qa.code + grow * P.K;
     }
-  };
-  auto seg_drain = [&](int sd, int64_t slice, int64_t slice_b, int64_t m0, int64_t n0) {
-    const int pw = warp - 1;
-    const int quarter = warp & 3;
-    const int acc_j = (pw >> 2) & 1;
-    const int col_half = pw >> 3;
-    const int64_t gm = m0 + acc_j * 128 + quarter * 32 + lane;
-    const bool row_ok = gm < prm.m_rows;
-    const int64_t grow = slice * P.M + gm;
-    const int L = row_ok ? row_stream_len(P, slice, grow) : -1;
-    const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
-#pragma unroll 1
-    for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t y[16];
-        seg_chunk(sd, cc, h, acc_j, quarter, grow, row_ok, L, slice_b, n0, y);
-        tmem_st16(lanebase + (uint32_t)(2 * BN + acc_j * BN + cc * 32 + h * 16), y);
+  }
+  bool bval[kNB];
+  const int16_t *brow[kNB];
+#pragma unroll
+  for (int i = 0; i < kNB; ++i) {
+    const int64_t gn = n0 + rsub + 64 * i;
+    bval[i] = (rsub + 64 * i < BN) && gn < prm.n_rows;
+    brow[i] = bval[i] ? P.qb.code + (slice_b * P.N + gn) * P.K : P.qb.code;
+  }
+  // ---- prefetch k-block 0
+  int16_t ca_n[kRowsA], cb_n[kNB];
+  uint4 rr_n = make_uint4(0, 0, 0, 0);
+  int t0_n = 0;
+  {
+    const int i0 = chunk * 16;
+    const int d = i0 >> lg;
+    t0_n = i0 & (Lp32 - 1);
+    const bool dv = d < K32;
+#pragma unroll
+    for (int i = 0; i < kRowsA; ++i)
+      ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
+#pragma unroll
+    for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
+    if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (pool_row(d) * T + t0_n)));
+  }
+  for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+    int16_t ca[kRowsA], cb[kNB];
+#pragma unroll
+    for (int i = 0; i < kRowsA; ++i) ca[i] = ca_n[i];
+#pragma unroll
+    for (int i = 0; i < kNB; ++i) cb[i] = cb_n[i];
+    uint4 rr = rr_n;
+    const int t0 = t0_n;
+    // k-block start inside its reduction index (table path: one d per k-block)
+    const int t0_blk = ((int)kb * kKB) & (Lp32 - 1);
+    if (kb + 1 < prm.nkb) {
+      const int i0 = ((int)kb + 1) * kKB + chunk * 16;
+      const int d = i0 >> lg;
+      t0_n = i0 & (Lp32 - 1);
+      const bool dv = d < K32;
+#pragma unroll
+      for (int i = 0; i < kRowsA; ++i)
+        ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
+#pragma unroll
+      for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
+      rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (pool_row(d) * T + t0_n)))
+                : make_uint4(0, 0, 0, 0);
+    }
+    if (prm.shift_pool) {
+      rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
+      rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
+    }
+    // byte j of (u * 0x01010101 + base_w) is 0x7F + u - R[t0+4w+j]; its top
+    // bit is [R < u] (no borrows: u, R < 128), read by the sign-replicating
+    // byte permute
+    const uint32_t rb0 = 0x7F7F7F7Fu - rr.x, rb1 = 0x7F7F7F7Fu - rr.y;
+    const uint32_t rb2 = 0x7F7F7F7Fu - rr.z, rb3 = 0x7F7F7F7Fu - rr.w;
+    if (!acquire_stage(b, st, lane)) return false;
+    const uint32_t sa_s = smem_s + (uint32_t)st.stage * Cfg::kStage + offA0;
+    const uint32_t sb_s = sa_s + Cfg::kStageA;
+    // ---- A: enable windows, sigma * [t < k]
+    if constexpr (kBulkA) {
+      // one k-block = 128 stream positions of one reduction index: copy
+      // chunk `chunk` of the window row (sign, q) from the smem table
+#pragma unroll
+      for (int i = 0; i < kRowsA; ++i) {
+        const int c = ca[i];
+        const int k = (abs(c) * Lrow[i]) >> P.prec;
+        const int q = min(max(k - t0_blk, 0), 128);
+        const uint4 w =
+            ld_shared_v4(therm_u + (uint32_t)((((c < 0 ? 129 : 0) + q) << 7) + (chunk << 4)));
+        st_shared_v4(sa_s + i * 8192, w.x, w.y, w.z, w.w);
       }
     }
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-  };
+#pragma unroll
+    for (int i = 0; i < (kBulkA ? 0 : kRowsA); ++i) {
+      const int c = ca[i];
+      const int k = (abs(c) * Lrow[i]) >> P.prec;
+      const uint32_t q = (uint32_t)min(max(k - t0, 0), 16);
+      const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
+      // byte j of (q * 0x01010101 + 0x7F7F7F7F - tw) is 0x7F + q - j: top bit = [j < q]
+      st_shared_v4(sa_s + i * 8192,  // +64 rows = 8 atoms
+                   prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw0), 0u, 0xBA98u) & sm,
+                   prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw1), 0u, 0xBA98u) & sm,
+                   prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw2), 0u, 0xBA98u) & sm,
+                   prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw3), 0u, 0xBA98u) & sm);
+    }
+    // ---- B: streams, sigma * [R[d'][t] < c_b]
+#pragma unroll
+    for (int i = 0; i < kNB; ++i) {
+      if (rsub + 64 * i >= BN) break;
+      const int c = cb[i];
+      const uint32_t u = (uint32_t)(abs(c) >> prm.shift_pool);
+      const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
+      st_shared_v4(sb_s + i * 8192,
+                   prmt(u * 0x01010101u + rb0, 0u, 0xBA98u) & sm,
+                   prmt(u * 0x01010101u + rb1, 0u, 0xBA98u) & sm,
+                   prmt(u * 0x01010101u + rb2, 0u, 0xBA98u) & sm,
+                   prmt(u * 0x01010101u + rb3, 0u, 0xBA98u) & sm);
+    }
+    publish_stage(b, st, lane);
+    if constexpr (kSeg) {
+      if ((kb + 1) % prm.nkb_seg == 0 && kb + 1 < prm.nkb) {
+        // ---- end of a non-final segment
+        if (!segment_drain<BN>(prm, b, st, tmem_base, warp, lane, (int)(kb / prm.nkb_seg), slice,
+                               slice_b, m0, n0))
+          return false;
+      }
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Row producers (K % 8 == 0, Lp >= 64).  Thread pt owns a-row pt % 256 (its
+// chunks 4 (pt / 256) .. + 3) and b-row pt % BN (its BN / 64 chunks starting
+// at (BN / 64) (pt / BN)), so a warp covers 32 consecutive rows of one
+// operand and each code is turned into a window length / threshold once per
+// k-block, not once per chunk.  Codes arrive 8 reduction indices at a time
+// (one 16-byte load per row per macro step of G = Lp / 16 k-blocks).
+//
+// Bytes are produced four at a time with one IMAD, one byte permute and one
+// AND: for a chunk starting at stream position t0,
+//   a: word j = sign(0x7F + (k - t0) - (4 j + b)) for bytes b < 4, i.e. the
+//      top bit of byte b is [t0 + 4 j + b < k] (k - t0 in [-112, 128], so no
+//      byte under- or overflows);
+//   b: word j = sign(u + PC[d'][t0 + 4 j + b]) with PC = 0x7F - (R >> shift),
+//      top bit [R >> shift < u] (u < 128).
+// sign(x) replicates each byte's top bit (prmt 0xBA98) and is ANDed with
+// 0x01010101 (sigma = +1) or 0xFFFFFFFF (sigma = -1).
+__device__ __forceinline__ uint32_t mad_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// 16 bytes of codes read once per macro step: no L1 allocation, so the pool
+// complement rows the producers re-read stay resident
+__device__ __forceinline__ uint4 ld_stream_v4(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+// code of reduction index `idx` (0..7) of a macro step: int16 lane of the
+// 16-byte code load
+__device__ __forceinline__ int code_of(const uint4 &v, int idx) {
+  const uint32_t w = word_of(v, idx >> 1);
+  return (idx & 1) ? ((int)w >> 16) : (int)(int16_t)(w & 0xFFFFu);
+}
+// code of index 2 j + e (e in {0, 1} known only at run time): sh = 16 - 16 e
+__device__ __forceinline__ int code_of_rt(const uint4 &v, int j, uint32_t sh) {
+  return (int)(word_of(v, j) << sh) >> 16;
+}
+
+// BN = b rows this CTA generates (starting at n0); CTA pairs (kPair) run NS
+// stages.
+template <int BN, int LG, bool kSeg, int NS = kStages, bool kPair = false>
+__device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, uint32_t smem_s,
+                             uint32_t tmem_base, int warp, int lane, int64_t slice,
+                             int64_t slice_b, int64_t m0, int64_t n0) {
+  static_assert(LG >= 6 && LG <= 8, "row producers need 64 <= Lp <= 256");
+  static_assert(!(kSeg && kPair), "CTA pairs run unsegmented problems");
+  using Cfg = TcCfg<BN>;
+  const GemmProblem &P = prm.P;
+  constexpr int NBC = BN / 64;          // b chunks per thread
+  constexpr int G = (1 << LG) / 16;     // k-blocks per macro step (8 reduction indices)
+  const int pt = threadIdx.x - 32;
+  const int ra = pt & 255;              // a row of the tile
+  const int hA = pt >> 8;               // a chunks 4 hA .. 4 hA + 3
+  const int rbn = pt & (BN - 1);        // b row of the tile
+  const int cB0 = NBC * (pt / BN);      // first b chunk
+  // rows (an invalid row reads the last valid row: its outputs are never
+  // stored; with CTA pairs a whole half tile can lie past the last row)
+  const int64_t gmA = m0 + ra;
+  const bool vA = gmA < prm.m_rows;
+  const int64_t growA = slice * P.M + (vA ? gmA : prm.m_rows - 1);
+  int Lg = 0;
+  if (vA) {
+    const int L = row_stream_len(P, slice, growA);
+    Lg = L > 0 ? L : 0;
+  }
+  const int64_t gnB = n0 + rbn;
+  const int64_t growB = slice_b * P.N + (gnB < prm.n_rows ? gnB : prm.n_rows - 1);
+  const uint4 *pa = reinterpret_cast<const uint4 *>(P.qa.code + growA * P.K);
+  const uint4 *pb = reinterpret_cast<const uint4 *>(P.qb.code + growB * P.K);
+  // shared-memory addresses of this thread's chunks in stage 0
+  uint32_t sA[4], sB[NBC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sA[i] = smem_s + sw128_offset(ra, 4 * hA + i);
+#pragma unroll
+  for (int i = 0; i < NBC; ++i) sB[i] = smem_s + Cfg::kStageA + sw128_offset(rbn, cB0 + i);
+  // stream position of the first a chunk inside its reduction index (or
+  // half index for Lp = 256), and of the first b chunk
+  const int t0A = LG >= 7 ? 64 * hA : 0;
+  const int t0B = LG >= 7 ? 16 * cB0 : 16 * (cB0 & 3);
+  // Lp = 64: a chunks lie in index 2 j + hA, b chunks in 2 j + (cB0 >> 2)
+  const uint32_t shA = 16u - 16u * (uint32_t)hA;
+  const uint32_t shB = 16u - 16u * (uint32_t)(cB0 >> 2);
+  const uint32_t rep = prm.rep;           // 0x01010101
+  const uint32_t stage_bytes = prm.stage_bytes;
+  const int prec = P.prec;
+  const int shift = prm.shift_pool;
+  const int nmacro = (int)(P.K >> 3);
+  const int msteps_seg = kSeg ? prm.kseg >> 3 : 0;  // macro steps per segment
+  const uint8_t *pcomp = P.pool_comp + t0B;
+  // pool rows one segment (or the whole K) spans; prefetches wrap inside it
+  const int prow_lim = kSeg ? prm.kseg : (int)P.K;
+  int pbase = 0;  // pool row of the macro step's first reduction index
+  int mseg = 0;   // macro steps done in the current segment
+  uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
+#pragma unroll 1
+  for (int mc = 0; mc < nmacro; ++mc) {
+    const uint4 ca = ca_n, cb = cb_n;
+    if (mc + 1 < nmacro) {
+      ca_n = ld_stream_v4(pa + mc + 1);
+      cb_n = ld_stream_v4(pb + mc + 1);
+    }
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      // ---- b: pool complement bytes of this k-block's b chunks; the row two
+      // k-blocks ahead is pulled into L1 now (each k-block starts a new row,
+      // and an L2 round trip per k-block would stall every producer)
+      const int dB = LG == 8 ? (j >> 1) : (LG == 7 ? j : 2 * j + (cB0 >> 2));
+      const uint8_t *pc = pcomp + ((size_t)(pbase + dB) << prec) + (LG == 8 ? 128 * (j & 1) : 0);
+      {
+        const int dB2 = LG == 8 ? ((j + 2) >> 1) : (LG == 7 ? j + 2 : 2 * (j + 2) + (cB0 >> 2));
+        int pr2 = pbase + dB2;
+        if (pr2 >= prow_lim) pr2 -= prow_lim;
+        prefetch_l1(pcomp + ((size_t)pr2 << prec) + (LG == 8 ? 128 * (j & 1) : 0));
+      }
+      uint4 pcw[NBC];
+#pragma unroll
+      for (int i = 0; i < NBC; ++i) pcw[i] = __ldg(reinterpret_cast<const uint4 *>(pc) + i);
+      // ---- a: window length of this k-block's reduction index
+      const int codeA = LG == 6 ? code_of_rt(ca, j, shA) : code_of(ca, LG == 8 ? (j >> 1) : j);
+      int k = (abs(codeA) * Lg) >> prec;
+      if (LG == 8) k = (j & 1) ? max(k - 128, 0) : min(k, 128);
+      const uint32_t kbase = (uint32_t)(k - t0A);
+      const uint32_t smA = (uint32_t)(codeA >> 31) | 0x01010101u;
+      const int codeB = LG == 6 ? code_of_rt(cb, j, shB) : code_of(cb, LG == 8 ? (j >> 1) : j);
+      const uint32_t u = (uint32_t)(abs(codeB) >> shift);
+      const uint32_t smB = (uint32_t)(codeB >> 31) | 0x01010101u;
+      if (!acquire_stage(b, st, lane)) return false;
+      const uint32_t stg = (uint32_t)st.stage;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        // chunk 4 hA + i starts at t0A + 16 i: k - t0 = kbase - 16 i
+        const uint32_t kc = kbase - 16u * (uint32_t)i;
+        st_shared_v4(mad_u32(stg, stage_bytes, sA[i]),
+                     prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x03020100u), 0u, 0xBA98u) & smA,
+                     prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x07060504u), 0u, 0xBA98u) & smA,
+                     prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x0B0A0908u), 0u, 0xBA98u) & smA,
+                     prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x0F0E0D0Cu), 0u, 0xBA98u) & smA);
+      }
+#pragma unroll
+      for (int i = 0; i < NBC; ++i) {
+        st_shared_v4(mad_u32(stg, stage_bytes, sB[i]),
+                     prmt(mad_u32(u, rep, pcw[i].x), 0u, 0xBA98u) & smB,
+                     prmt(mad_u32(u, rep, pcw[i].y), 0u, 0xBA98u) & smB,
+                     prmt(mad_u32(u, rep, pcw[i].z), 0u, 0xBA98u) & smB,
+                     prmt(mad_u32(u, rep, pcw[i].w), 0u, 0xBA98u) & smB);
+      }
+      publish_stage<NS>(b, st, lane);
+    }
+    pbase += 8;
+    if constexpr (kSeg) {
+      if (++mseg == msteps_seg) {
+        mseg = 0;
+        pbase = 0;
+        // ---- end of a segment (the last one drains in the epilogue)
+        if (mc + 1 < nmacro &&
+            !segment_drain<BN>(prm, b, st, tmem_base, warp, lane, (mc + 1) / msteps_seg - 1,
+                               slice, slice_b, m0, n0))
+          return false;
+      }
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue: TMEM -> smem transpose -> rescale -> bias -> coalesced stores.
+// The stage ring is idle (every MMA of this tile has completed), so each warp
+// stages its 32x32 blocks there; a producer-only barrier keeps the next
+// tile's operand writes out until all are done.
+template <int BN, bool kSeg, bool kPair = false>
+__device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
+                              unsigned char *smem, uint32_t tmem_base, int warp, int lane,
+                              int64_t slice, int64_t slice_b, int64_t m0, int64_t n0, int64_t it) {
+  const GemmProblem &P = prm.P;
+  if (!mbar_wait(b.tfull, (uint32_t)(st.g & 1), b.abort)) return false;
+  tc_fence_after();
+  {
+    const int pw = warp - 1;                 // producer warp 0..15
+    const int quarter = warp & 3;            // TMEM lanes this warp may access
+    const int acc_j = (pw >> 2) & 1;         // accumulator (a rows 0-127 / 128-255)
+    const int col_half = pw >> 3;            // which half of the BN columns
+    float *stg = reinterpret_cast<float *>(smem) + pw * (32 * 33);
+    int4 *rowp = reinterpret_cast<int4 *>(smem + kProducerWarps * 32 * 33 * 4) + pw * 32;
+    const int64_t mrow0 = m0 + acc_j * 128 + quarter * 32;  // first row of this warp
+    {
+      const int64_t gm = mrow0 + lane;
+      int L = -1, za = 0, rsa = 0;
+      float sa = 0.f;
+      if (gm < prm.m_rows) {
+        const int64_t grow = slice * P.M + gm;
+        L = row_stream_len(P, slice, grow);
+        sa = P.qa.scale[grow];
+        za = P.qa.zero[grow];
+        rsa = P.qa.rowsum[grow];
+      }
+      rowp[lane] = make_int4(L, __float_as_int(sa), za, rsa);
+    }
+    __syncwarp();
+    const int64_t grow0 = slice * P.M + mrow0;
+    const int myL = rowp[lane].x;  // stream length of this lane's row
+#pragma unroll 1
+    for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
+      if constexpr (kSeg) {
+        // last segment: finished fp32 values (rescaled and summed in order)
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[16];
+          seg_chunk<BN>(prm, tmem_base, lane, prm.nseg - 1, cc, h, acc_j, quarter, grow0 + lane,
+                        mrow0 + lane < prm.m_rows, myL, slice_b, n0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) stg[lane * 33 + h * 16 + i] = __uint_as_float(v[i]);
+        }
+      } else {
+        uint32_t v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32),
+                  v);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __uint_as_float(v[i]);
+      }
+      __syncwarp();
+      // lane = column now
+      const int64_t gn = n0 + cc * 32 + lane;
+      const bool col_ok = gn < prm.n_rows;
+      float sb = 0.f;
+      int32_t zb = 0, rsb = 0;
+      float bias = 0.f;
+      if (col_ok) {
+        const int64_t brw = slice_b * P.N + gn;
+        sb = P.qb.scale[brw];
+        zb = P.qb.zero[brw];
+        rsb = P.qb.rowsum[brw];
+        if (P.bias) bias = P.bias[gn];
+      }
+#pragma unroll 4
+      for (int r = 0; r < 32; ++r) {
+        const int4 rp = rowp[r];  // broadcast
+        if (!col_ok || rp.x < 0) continue;
+        const int32_t a = rp.x > 0 ? __float_as_int(stg[r * 33 + lane]) : 0;
+        float y = 0.0f;
+        if constexpr (kSeg) {
+          if (rp.x > 0) y = stg[r * 33 + lane];
+        } else if (rp.x > 0) {
+          y = sc_rescale(P.mode, P.prec, rp.x, a, P.K, __int_as_float(rp.y), rp.z, rp.w, sb, zb,
+                         rsb);
+        }
+        if (P.bias) y = __fadd_rn(y, bias);
+        const int64_t o = (grow0 + r) * P.N + gn;
+        P.out[o] = y;
+        if (!kSeg && P.acc_out) P.acc_out[o] = a;
+      }
+      __syncwarp();
+    }
+  }
+  // every producer is done with the staging area before anyone refills it
+  // (a bounded mbarrier wait, not bar.sync: an aborting thread must not
+  // leave the others blocked)
+  if constexpr (kPair) {
+    // one thread per CTA hands the accumulators back to the even CTA's MMA
+    // thread once every producer of this CTA has read them
+    tc_fence_before();
+    mbar_arrive(b.epi);
+    if (!mbar_wait(b.epi, (uint32_t)(it & 1), b.abort)) return false;
+    if (threadIdx.x == 32) mbar_arrive_cluster(b.tempty_cl);
+  } else {
+    mbar_arrive(b.epi);
+    if (!mbar_wait(b.epi, (uint32_t)(it & 1), b.abort)) return false;
+    tc_fence_before();
+    mbar_arrive(b.tempty);
+  }
+  ++st.g;
+  return true;
+}
+
+template <int BN, int kProd, int LG, bool kSeg>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm) {
+  using Cfg = TcCfg<BN>;
+  // int32 accumulators in columns [0, 2 BN); segmented kernels keep the fp32
+  // running sum of the finished segments in columns [2 BN, 4 BN)
+  constexpr uint32_t kTmemAlloc = kSeg ? 4 * BN : 2 * BN;
+  static_assert(!kSeg || BN <= 128, "segmented tiles need 4*BN <= 512 TMEM columns");
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *therm_s = smem + kStages * Cfg::kStage;  // [sign][window 0..128][128 B]
+  Bars b;
+  b.full = reinterpret_cast<uint64_t *>(therm_s + (kProd == kProdTable ? Cfg::kTherm : 0));
+  b.empty = b.full + kStages;
+  b.tfull = b.empty + kStages;
+  b.tempty = b.tfull + 1;
+  b.drain = b.tempty + 1;
+  b.epi = b.drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(b.epi + 1);
+  b.abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&b.full[s], kProducerWarps);
+      mbar_init(&b.empty[s], 1);
+    }
+    mbar_init(b.tfull, 1);
+    mbar_init(b.tempty, kProducers);
+    mbar_init(b.drain, 1);
+    mbar_init(b.epi, kProducers);
+    *b.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemAlloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if constexpr (kProd == kProdTable) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(prm.therm);
+    uint4 *dst = reinterpret_cast<uint4 *>(therm_s);
+    for (int i = threadIdx.x; i < (int)(Cfg::kTherm / 16); i += blockDim.x) dst[i] = __ldg(src + i);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ================================================= MMA issuer (lane 0)
@@ -336,17 +905,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       const uint32_t smem0 = smem_u32(smem);
       int stage = 0;
       uint32_t phase = 0;
-      int64_t it = 0;
       bool ok = true;
       int64_t g = 0;  // drain counter: one per (tile, segment)
-      for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++it) {
+      for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x) {
         for (int seg = 0; seg < prm.nseg && ok; ++seg, ++g) {
           // the accumulators are free once the previous drain has read them
-          if (g > 0) ok = mbar_wait(tempty_bar, (uint32_t)((g - 1) & 1), abort);
+          if (g > 0) ok = mbar_wait(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
           if (!ok) break;
           tc_fence_after();
           for (int64_t kb = 0; kb < prm.nkb_seg; ++kb) {
-            if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+            if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
             tc_fence_after();
             const uint32_t a0 = smem0 + stage * Cfg::kStage;
             const uint32_t b0 = a0 + Cfg::kStageA;
@@ -359,274 +927,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
                 tc_mma_i8(tmem_base + j * BN, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
               }
             }
-            tc_commit(&empty_bar[stage]);
+            tc_commit(&b.empty[stage]);
             if (++stage == kStages) { stage = 0; phase ^= 1; }
           }
           if (!ok) break;
-          tc_commit(tfull_bar);
+          tc_commit(b.tfull);
         }
       }
       // Drain: everything this thread issued has completed before TMEM is freed.
-      tc_commit(drain_bar);
-      mbar_wait(drain_bar, 0, abort);
+      tc_commit(b.drain);
+      mbar_wait(b.drain, 0, b.abort);
     }
     __syncwarp();
   } else {
     // ============================ producers + epilogue (kProducerWarps warps)
-    // Thread pt fills 16-byte chunk `chunk` of a-rows rsub + 64 i (i < 4) and
-    // b-rows rsub + 64 i (i < kNB) of every k-block.  Codes and pool bytes of
-    // k-block kb + 1 are loaded while k-block kb is generated.
-    constexpr int kRowsA = kBM / 64;                 // 4
-    constexpr int kNB = BN >= 64 ? BN / 64 : 1;      // b rows per thread
-    const int pt = threadIdx.x - 32;                 // 0 .. kProducers-1
-    const int chunk = pt & 7;
-    const int rsub = pt >> 3;                        // 0 .. 63
-    int stage = 0;
-    uint32_t phase = 0;
+    const uint32_t smem_s = smem_u32(smem);  // 32-bit shared-window addresses
+    const uint32_t therm_u = smem_u32(therm_s);
+    ProdState st{0, 0u, 0};
     int64_t it = 0;
-    int64_t g = 0;  // drain counter, as on the MMA side
-    bool ok = true;
-    const uint32_t tw0 = 0x03020100u, tw1 = 0x07060504u, tw2 = 0x0B0A0908u, tw3 = 0x0F0E0D0Cu;
-    // byte offsets of this thread's chunks inside the A / B stage (row r = rsub + 64 i)
-    const uint32_t offA0 = sw128_offset(rsub, chunk);
-    for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++it) {
+    for (int64_t tile = blockIdx.x; tile < prm.tiles; tile += gridDim.x, ++it) {
       const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
       const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
       const int64_t m0 = (rem % prm.tiles_m) * kBM;
       const int64_t n0 = (rem / prm.tiles_m) * BN;
-      const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
-      int Lrow[kRowsA];
-      const int16_t *arow[kRowsA];
-#pragma unroll
-      for (int i = 0; i < kRowsA; ++i) {
-        const int64_t gm = m0 + rsub + 64 * i;
-        Lrow[i] = 0;
-        arow[i] = P.qa.code;  // dummy, never read when Lrow = 0 / invalid
-        if (gm < prm.m_rows) {
-          const int64_t grow = slice * P.M + gm;
-          Lrow[i] = row_stream_len(P, slice, grow);
-          arow[i] = P.qa.code + grow * P.K;
-        }
-      }
-      bool bval[kNB];
-      const int16_t *brow[kNB];
-#pragma unroll
-      for (int i = 0; i < kNB; ++i) {
-        const int64_t gn = n0 + rsub + 64 * i;
-        bval[i] = (rsub + 64 * i < BN) && gn < prm.n_rows;
-        brow[i] = bval[i] ? P.qb.code + (slice_b * P.N + gn) * P.K : P.qb.code;
-      }
-      // ---- prefetch k-block 0
-      int16_t ca_n[kRowsA], cb_n[kNB];
-      uint4 rr_n = make_uint4(0, 0, 0, 0);
-      int t0_n = 0;
-      {
-        const int i0 = chunk * 16;
-        const int d = i0 >> lg;
-        t0_n = i0 & (Lp32 - 1);
-        const bool dv = d < K32;
-#pragma unroll
-        for (int i = 0; i < kRowsA; ++i)
-          ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
-#pragma unroll
-        for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-        if (dv) rr_n = __ldg(reinterpret_cast<const uint4 *>(P.pool + (pool_row(d) * T + t0_n)));
-      }
-      for (int64_t kb = 0; kb < prm.nkb; ++kb) {
-        int16_t ca[kRowsA], cb[kNB];
-#pragma unroll
-        for (int i = 0; i < kRowsA; ++i) ca[i] = ca_n[i];
-#pragma unroll
-        for (int i = 0; i < kNB; ++i) cb[i] = cb_n[i];
-        uint4 rr = rr_n;
-        const int t0 = t0_n;
-        // k-block start inside its reduction index (table path: one d per k-block)
-        const int t0_blk = ((int)kb * kKB) & (Lp32 - 1);
-        if (kb + 1 < prm.nkb) {
-          const int i0 = ((int)kb + 1) * kKB + chunk * 16;
-          const int d = i0 >> lg;
-          t0_n = i0 & (Lp32 - 1);
-          const bool dv = d < K32;
-#pragma unroll
-          for (int i = 0; i < kRowsA; ++i)
-            ca_n[i] = (dv && Lrow[i] != 0) ? __ldg(arow[i] + d) : (int16_t)0;
-#pragma unroll
-          for (int i = 0; i < kNB; ++i) cb_n[i] = (dv && bval[i]) ? __ldg(brow[i] + d) : (int16_t)0;
-          rr_n = dv ? __ldg(reinterpret_cast<const uint4 *>(P.pool + (pool_row(d) * T + t0_n)))
-                    : make_uint4(0, 0, 0, 0);
-        }
-        if (prm.shift_pool) {
-          rr.x = (rr.x >> 1) & 0x7F7F7F7Fu; rr.y = (rr.y >> 1) & 0x7F7F7F7Fu;
-          rr.z = (rr.z >> 1) & 0x7F7F7F7Fu; rr.w = (rr.w >> 1) & 0x7F7F7F7Fu;
-        }
-        // byte j of (u * 0x01010101 + base_w) is 0x7F + u - R[t0+4w+j]; its top
-        // bit is [R < u] (no borrows: u, R < 128), read by the sign-replicating
-        // byte permute
-        const uint32_t rb0 = 0x7F7F7F7Fu - rr.x, rb1 = 0x7F7F7F7Fu - rr.y;
-        const uint32_t rb2 = 0x7F7F7F7Fu - rr.z, rb3 = 0x7F7F7F7Fu - rr.w;
-        {
-          int w_ok = 1;
-          if (lane == 0) w_ok = mbar_wait(&empty_bar[stage], phase ^ 1, abort) ? 1 : 0;
-          w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-          if (!w_ok) { ok = false; break; }
-        }
-        const uint32_t sa_s = smem_s + (uint32_t)stage * Cfg::kStage + offA0;
-        const uint32_t sb_s = sa_s + Cfg::kStageA;
-        // ---- A: enable windows, sigma * [t < k]
-        if constexpr (kBulkA) {
-          // one k-block = 128 stream positions of one reduction index: copy
-          // chunk `chunk` of the window row (sign, q) from the smem table
-#pragma unroll
-          for (int i = 0; i < kRowsA; ++i) {
-            const int c = ca[i];
-            const int k = (abs(c) * Lrow[i]) >> P.prec;
-            const int q = min(max(k - t0_blk, 0), 128);
-            const uint4 w =
-                ld_shared_v4(therm_u + (uint32_t)((((c < 0 ? 129 : 0) + q) << 7) + (chunk << 4)));
-            st_shared_v4(sa_s + i * 8192, w.x, w.y, w.z, w.w);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < (kBulkA ? 0 : kRowsA); ++i) {
-          const int c = ca[i];
-          const int k = (abs(c) * Lrow[i]) >> P.prec;
-          const uint32_t q = (uint32_t)min(max(k - t0, 0), 16);
-          const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
-          // byte j of (q * 0x01010101 + 0x7F7F7F7F - tw) is 0x7F + q - j: top bit = [j < q]
-          st_shared_v4(sa_s + i * 8192,  // +64 rows = 8 atoms
-                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw0), 0u, 0xBA98u) & sm,
-                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw1), 0u, 0xBA98u) & sm,
-                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw2), 0u, 0xBA98u) & sm,
-                       prmt(q * 0x01010101u + (0x7F7F7F7Fu - tw3), 0u, 0xBA98u) & sm);
-        }
-        // ---- B: streams, sigma * [R[d'][t] < c_b]
-#pragma unroll
-        for (int i = 0; i < kNB; ++i) {
-          if (rsub + 64 * i >= BN) break;
-          const int c = cb[i];
-          const uint32_t u = (uint32_t)(abs(c) >> prm.shift_pool);
-          const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
-          st_shared_v4(sb_s + i * 8192,
-                       prmt(u * 0x01010101u + rb0, 0u, 0xBA98u) & sm,
-                       prmt(u * 0x01010101u + rb1, 0u, 0xBA98u) & sm,
-                       prmt(u * 0x01010101u + rb2, 0u, 0xBA98u) & sm,
-                       prmt(u * 0x01010101u + rb3, 0u, 0xBA98u) & sm);
-        }
-        // every lane publishes its writes to the async proxy, then one lane
-        // per warp arrives (release covers the warp's writes via __syncwarp)
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full_bar[stage]);
-        if (++stage == kStages) { stage = 0; phase ^= 1; }
-        if constexpr (kSeg) {
-          if ((kb + 1) % prm.nkb_seg == 0 && kb + 1 < prm.nkb) {
-            // ---- end of a non-final segment: int32 accumulators -> rescale with
-            // this segment's scales -> add to the fp32 running sum in TMEM
-            const int sd = (int)(kb / prm.nkb_seg);
-            if (!mbar_wait(tfull_bar, (uint32_t)(g & 1), abort)) { ok = false; break; }
-            tc_fence_after();
-            seg_drain(sd, slice, slice_b, m0, n0);
-            tc_fence_before();
-            mbar_arrive(tempty_bar);
-            ++g;
-          }
-        }
-      }
+      const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
+      bool ok;
+      if constexpr (kProd == kProdRows)
+        ok = produce_rows<BN, LG, kSeg>(prm, b, st, smem_s, tmem_base, warp, lane, slice, slice_b,
+                                        m0, n0);
+      else
+        ok = produce_chunks<BN, kProd == kProdTable, kSeg>(prm, b, st, smem_s, therm_u, tmem_base,
+                                                           warp, lane, slice, slice_b, m0, n0);
       if (!ok) break;
-
-      // ---- epilogue: TMEM -> smem transpose -> rescale -> bias -> coalesced stores.
-      // The stage ring is idle now (every MMA of this tile has completed), so
-      // each warp stages its 32x32 blocks there; a producer-only barrier
-      // below keeps the next tile's operand writes out until all are done.
-      if (!mbar_wait(tfull_bar, (uint32_t)(g & 1), abort)) { ok = false; break; }
-      tc_fence_after();
-      {
-        const int pw = warp - 1;                 // producer warp 0..15
-        const int quarter = warp & 3;            // TMEM lanes this warp may access
-        const int acc_j = (pw >> 2) & 1;         // accumulator (a rows 0-127 / 128-255)
-        const int col_half = pw >> 3;            // which half of the BN columns
-        float *stg = reinterpret_cast<float *>(smem) + pw * (32 * 33);
-        int4 *rowp = reinterpret_cast<int4 *>(smem + kProducerWarps * 32 * 33 * 4) + pw * 32;
-        const int64_t mrow0 = m0 + acc_j * 128 + quarter * 32;  // first row of this warp
-        {
-          const int64_t gm = mrow0 + lane;
-          int L = -1, za = 0, rsa = 0;
-          float sa = 0.f;
-          if (gm < prm.m_rows) {
-            const int64_t grow = slice * P.M + gm;
-            L = row_stream_len(P, slice, grow);
-            sa = P.qa.scale[grow];
-            za = P.qa.zero[grow];
-            rsa = P.qa.rowsum[grow];
-          }
-          rowp[lane] = make_int4(L, __float_as_int(sa), za, rsa);
-        }
-        __syncwarp();
-        const int64_t grow0 = slice * P.M + mrow0;
-        const int myL = rowp[lane].x;  // stream length of this lane's row
-#pragma unroll 1
-        for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
-          if constexpr (kSeg) {
-            // last segment: finished fp32 values (rescaled and summed in order)
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              uint32_t v[16];
-              seg_chunk(prm.nseg - 1, cc, h, acc_j, quarter, grow0 + lane,
-                        mrow0 + lane < prm.m_rows, myL, slice_b, n0, v);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) stg[lane * 33 + h * 16 + i] = __uint_as_float(v[i]);
-            }
-          } else {
-            uint32_t v[32];
-            tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                          (uint32_t)(acc_j * BN + cc * 32),
-                      v);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-            for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __uint_as_float(v[i]);
-          }
-          __syncwarp();
-          // lane = column now
-          const int64_t gn = n0 + cc * 32 + lane;
-          const bool col_ok = gn < prm.n_rows;
-          float sb = 0.f;
-          int32_t zb = 0, rsb = 0;
-          float bias = 0.f;
-          if (col_ok) {
-            const int64_t brw = slice_b * P.N + gn;
-            sb = P.qb.scale[brw];
-            zb = P.qb.zero[brw];
-            rsb = P.qb.rowsum[brw];
-            if (P.bias) bias = P.bias[gn];
-          }
-#pragma unroll 4
-          for (int r = 0; r < 32; ++r) {
-            const int4 rp = rowp[r];  // broadcast
-            if (!col_ok || rp.x < 0) continue;
-            const int32_t a = rp.x > 0 ? __float_as_int(stg[r * 33 + lane]) : 0;
-            float y = 0.0f;
-            if constexpr (kSeg) {
-              if (rp.x > 0) y = stg[r * 33 + lane];
-            } else if (rp.x > 0) {
-              y = sc_rescale(P.mode, P.prec, rp.x, a, P.K, __int_as_float(rp.y), rp.z, rp.w, sb,
-                             zb, rsb);
-            }
-            if (P.bias) y = __fadd_rn(y, bias);
-            const int64_t o = (grow0 + r) * P.N + gn;
-            P.out[o] = y;
-            if (!kSeg && P.acc_out) P.acc_out[o] = a;
-          }
-          __syncwarp();
-        }
-      }
-      // every producer is done with the staging area before anyone refills it
-      // (a bounded mbarrier wait, not bar.sync: an aborting thread must not
-      // leave the others blocked)
-      mbar_arrive(epi_bar);
-      if (!mbar_wait(epi_bar, (uint32_t)(it & 1), abort)) { ok = false; break; }
-      tc_fence_before();
-      mbar_arrive(tempty_bar);
-      ++g;
+      if (!tile_epilogue<BN, kSeg>(prm, b, st, smem, tmem_base, warp, lane, slice, slice_b, m0, n0,
+                                   it))
+        break;
     }
   }
   tc_fence_before();
@@ -636,18 +971,223 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kTmemAlloc));
   }
-  if (threadIdx.x == 0 && *abort) atomicOr(prm.error, 1u);
+  if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
 }
 
-template <int BN, bool kBulkA, bool kSeg = false>
-cudaError_t launch_bn(const TcParams &prm, int sms, cudaStream_t s) {
-  const size_t smem = TcCfg<BN>::kSmem;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, kBulkA, kSeg>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+// ---------------------------------------------------------------------------
+// CTA-pair kernel (cta_group::2; unsegmented row producers, N >= 129).
+// A 2-CTA cluster owns a 512 x 256 output tile: CTA q generates a rows
+// m0 + 256 q .. + 255 and b rows n0 + 128 q .. + 127 of every k-block; the
+// even CTA issues M = 256 x N = 256 MMAs that read both CTAs' shared memory,
+// and each CTA's TMEM receives its own 256 a rows x all 256 columns.  Per
+// CTA this generates 384 operand rows per k-block instead of 512 and reads
+// 64 KB of shared memory per k-block for the MMAs instead of 96 KB; a stage
+// is 48 KB, so four fit.
+constexpr int kPairStages = 4;
+constexpr uint32_t kPairStageA = kBM * kKB;          // 32 KB: 256 a rows
+constexpr uint32_t kPairStageB = 128 * kKB;          // 16 KB: this CTA's 128 b rows
+constexpr uint32_t kPairStage = kPairStageA + kPairStageB;
+constexpr size_t kPairSmem = (size_t)kPairStages * kPairStage + 1024 /*align*/ + 256;
+
+// Instruction descriptor for the pair MMA: s8 x s8 -> s32, K-major, M = 256, N = 256.
+constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                                ((uint32_t)(256 >> 4) << 24);
+
+template <int LG>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_kernel(const TcParams prm) {
+  constexpr uint32_t kTmemAlloc = 512;  // two 256-column accumulators
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars b;
+  b.full = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStage);
+  b.empty = b.full + kPairStages;
+  b.pfull = b.empty + kPairStages;
+  b.tfull = b.pfull + kPairStages;
+  b.tempty = b.tfull + 1;
+  b.drain = b.tempty + 1;
+  b.epi = b.drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(b.epi + 1);
+  b.abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&b.full[s], kProducerWarps);  // this CTA's producer warps
+      mbar_init(&b.empty[s], 1);
+      mbar_init(&b.pfull[s], 1);              // the odd CTA's stage (even CTA only)
+    }
+    mbar_init(b.tfull, 1);
+    mbar_init(b.tempty, 2);  // one arrival per CTA after its epilogue
+    mbar_init(b.drain, 1);
+    mbar_init(b.epi, kProducers);
+    *b.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemAlloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers exist before anyone arrives on them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  b.pfull_cl = mapa_shared(smem_u32(b.pfull), 0);
+  b.tempty_cl = mapa_shared(smem_u32(b.tempty), 0);
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t nclusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ====================================== MMA issuer (even CTA, lane 0)
+    if (rank == 0 && lane == 0) {
+      const uint32_t smem0 = smem_u32(smem);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t g = 0;  // tiles issued
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++g) {
+        // both CTAs have read the previous tile's accumulators
+        if (g > 0) ok = mbar_wait_cl(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
+        if (!ok) break;
+        tc_fence_after();
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          // this CTA's stage, then the odd CTA's (forwarded at cluster scope)
+          if (!mbar_wait(&b.full[stage], phase, b.abort) ||
+              !mbar_wait_cl(&b.pfull[stage], phase, b.abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem0 + stage * kPairStage;
+          const uint32_t b0 = a0 + kPairStageA;
+#pragma unroll
+          for (int kk = 0; kk < kKB / 32; ++kk) {
+            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+              tc_mma_i8_pair(tmem_base + j * 256, adesc, bdesc, kIdescPair,
+                             (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit_pair_both(&b.empty[stage]);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair_both(b.tfull);
+      }
+      // Drain: everything this thread issued has completed before TMEM is freed.
+      tc_commit_pair_local(b.drain);
+      mbar_wait_cl(b.drain, 0, b.abort);
+    } else if (rank == 1 && lane == 0) {
+      // ============ forwarder (odd CTA): each filled stage of this CTA is
+      // announced to the MMA thread with one cluster-scope release
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters) {
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
+          mbar_arrive_cluster(b.pfull_cl + 8u * (uint32_t)stage);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ============================ producers + epilogue (kProducerWarps warps)
+    const uint32_t smem_s = smem_u32(smem);
+    ProdState st{0, 0u, 0};
+    int64_t it = 0;
+    for (int64_t tile = cluster; tile < prm.tiles; tile += nclusters, ++it) {
+      const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
+      const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+      const int64_t m0 = (rem % prm.tiles_m) * (2 * kBM) + (int64_t)rank * kBM;
+      const int64_t n0 = (rem / prm.tiles_m) * 256;
+      const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
+      if (!produce_rows<128, LG, false, kPairStages, true>(prm, b, st, smem_s, tmem_base, warp,
+                                                           lane, slice, slice_b, m0,
+                                                           n0 + (int64_t)rank * 128))
+        break;
+      if (!tile_epilogue<256, false, true>(prm, b, st, smem, tmem_base, warp, lane, slice, slice_b,
+                                           m0, n0, it))
+        break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while the pair may still touch its memory
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemAlloc));
+  }
+  if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
+}
+
+template <int BN, int kProd, int LG, bool kSeg>
+cudaError_t launch_bn(TcParams prm, int sms, cudaStream_t s) {
+  const size_t smem = TcCfg<BN>::smem_bytes(kProd == kProdTable);
+  auto kern = gemm_tc_kernel<BN, kProd, LG, kSeg>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = TcCfg<BN>::kStage;
   const int64_t grid = prm.tiles < sms ? prm.tiles : sms;
-  gemm_tc_kernel<BN, kBulkA, kSeg><<<(unsigned)grid, kThreads, smem, s>>>(prm);
+  kern<<<(unsigned)grid, kThreads, smem, s>>>(prm);
   return cudaGetLastError();
+}
+
+template <int LG>
+cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
+  auto kern = gemm_tc_pair_kernel<LG>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+  if (e != cudaSuccess) return e;
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = kPairStage;
+  // pair tiles: 512 a rows x 256 b rows
+  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
+  prm.tiles_n = (prm.n_rows + 255) / 256;
+  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // one cluster per resident pair slot (persistent tiles)
+  static int max_clusters[64][3] = {};
+  int clusters = dev >= 0 && dev < 64 ? max_clusters[dev][LG - 6] : 0;
+  if (clusters <= 0) {
+    cfg.gridDim = dim3(2, 1, 1);
+    if ((e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg)) != cudaSuccess) return e;
+    if (clusters <= 0) return cudaErrorInvalidConfiguration;
+    if (dev >= 0 && dev < 64) max_clusters[dev][LG - 6] = clusters;
+  }
+  const int64_t grid = prm.tiles < clusters ? prm.tiles : clusters;
+  cfg.gridDim = dim3((unsigned)(2 * grid), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, prm);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <int BN, bool kSeg>
+cudaError_t launch_rows(const TcParams &prm, int sms, cudaStream_t s) {
+  if (prm.lp_log2 == 6) return launch_bn<BN, kProdRows, 6, kSeg>(prm, sms, s);
+  if (prm.lp_log2 == 7) return launch_bn<BN, kProdRows, 7, kSeg>(prm, sms, s);
+  return launch_bn<BN, kProdRows, 8, kSeg>(prm, sms, s);
 }
 
 // Enable-window rows for the table path: [sign 0/1][window 0..128] x 128
@@ -701,6 +1241,15 @@ bool tc_supported(const GemmProblem &P) {
   return ((P.kseg << padded_stream_log2(P)) % kKB) == 0;
 }
 
+bool tc_row_producers(const GemmProblem &P) {
+  const int lg = padded_stream_log2(P);
+  if (lg < 6 || lg > 8 || (P.K & 7) != 0) return false;
+  if (P.nseg > 1 && (P.kseg & 7) != 0) return false;  // segments end on macro steps
+  // 16-byte code loads: rows of K int16 codes from 16-byte aligned planes
+  return ((reinterpret_cast<uintptr_t>(P.qa.code) | reinterpret_cast<uintptr_t>(P.qb.code)) & 15) ==
+         0;
+}
+
 int tc_block_n(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
 
 int tc_tile_n(const GemmProblem &P, int64_t N) {
@@ -730,21 +1279,37 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (tc_row_producers(P)) {
+    // pairs pay off only with two a tiles per pair (one accumulator per CTA
+    // would generate as many rows per MAC as a single CTA)
+    if (P.nseg == 1 && bn == 256 && m_rows > kBM) {
+      if (lg == 6) return launch_pair<6>(prm, dev, s);
+      if (lg == 7) return launch_pair<7>(prm, dev, s);
+      return launch_pair<8>(prm, dev, s);
+    }
+    if (P.nseg > 1) {
+      if (bn == 64) return launch_rows<64, true>(prm, sms, s);
+      return launch_rows<128, true>(prm, sms, s);
+    }
+    if (bn == 64) return launch_rows<64, false>(prm, sms, s);
+    if (bn == 128) return launch_rows<128, false>(prm, sms, s);
+    return launch_rows<256, false>(prm, sms, s);
+  }
+  if (P.nseg > 1) {
+    if (bn == 64) return launch_bn<64, kProdChunks, 0, true>(prm, sms, s);
+    return launch_bn<128, kProdChunks, 0, true>(prm, sms, s);
+  }
   // Table path: every k-block lies inside one reduction index, and the tile is
   // narrow, so enable windows dominate the operand generation.
-  if (P.nseg > 1) {
-    if (bn == 64) return launch_bn<64, false, true>(prm, sms, s);
-    return launch_bn<128, false, true>(prm, sms, s);
-  }
   if (lg >= 7 && bn == 64) {
     cudaError_t e;
     prm.therm = therm_table(&e);
     if (!prm.therm) return e != cudaSuccess ? e : cudaErrorUnknown;
-    return launch_bn<64, true>(prm, sms, s);
+    return launch_bn<64, kProdTable, 0, false>(prm, sms, s);
   }
-  if (bn == 64) return launch_bn<64, false>(prm, sms, s);
-  if (bn == 128) return launch_bn<128, false>(prm, sms, s);
-  return launch_bn<256, false>(prm, sms, s);
+  if (bn == 64) return launch_bn<64, kProdChunks, 0, false>(prm, sms, s);
+  if (bn == 128) return launch_bn<128, kProdChunks, 0, false>(prm, sms, s);
+  return launch_bn<256, kProdChunks, 0, false>(prm, sms, s);
 }
 
 }  // namespace scmp

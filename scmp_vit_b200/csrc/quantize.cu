@@ -170,6 +170,16 @@ __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_d
   }
 }
 
+// PC[d][t] = 0x7F - (R[d][t] >> shift).  The tensor-core engine forms the
+// stream byte 0x7F + u - (R >> shift) for a threshold u < 128: its top bit is
+// [R >> shift < u], with no borrow into the neighbouring byte.
+__global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int64_t bytes, int shift,
+                                       uint8_t *__restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (uint8_t)(0x7F - (pool[i] >> shift));
+}
+
 }  // namespace
 
 cudaError_t launch_row_stats(const float *x, int64_t rows, int64_t K, int mode, float2 *stat,
@@ -203,6 +213,15 @@ cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int 
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s) {
   stream_table_kernel<<<296, 256, 0, s>>>(pool, pool_dims, prec, table);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int prec, int shift,
+                                   uint8_t *out, cudaStream_t s) {
+  const int64_t bytes = (int64_t)pool_dims << prec;
+  const int64_t blocks = (bytes + 255) / 256;
+  pool_complement_kernel<<<(unsigned)(blocks < 296 ? blocks : 296), 256, 0, s>>>(pool, bytes, shift,
+                                                                               out);
   return cudaGetLastError();
 }
 

@@ -51,6 +51,9 @@ struct GemmProblem {
   int32_t *acc_out;
   // stream table ST[pool_dims][2^p + 1][2^p / 32] (bit t of threshold v)
   const uint32_t *stream_table;
+  // pool complement PC[pool_dims][2^p] = 0x7F - (R >> shift) (tensor-core
+  // row producers; shift = 1 for bipolar p = 8, else 0)
+  const uint8_t *pool_comp;
   // window of (a row, b row) pairs per slice this launch computes
   int64_t m_lo, m_hi, n_lo, n_hi;
 };
@@ -87,10 +90,14 @@ cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int 
                             cudaStream_t s);
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
+cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int prec, int shift,
+                                   uint8_t *out, cudaStream_t s);
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 bool tc_supported(const GemmProblem &P);
 int tc_block_n(int64_t N);
 int tc_tile_n(const GemmProblem &P, int64_t N);
+// true when the row-producer kernel runs this problem (it reads P.pool_comp)
+bool tc_row_producers(const GemmProblem &P);
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
                            unsigned int *error, cudaStream_t s);
 

@@ -57,6 +57,16 @@ def test_tc_single_tile(cuda_device):
     (257, 257, 64, 7, 128),     # 257th row/column through the CUDA-core strips
     (300, 64, 257, 7, 128),     # padded row tail, BN = 64
     (256, 100, 80, 7, 100),     # BN = 128 with padded columns, L not a power of two
+    # row producers (K % 8 == 0) at every padded length and tile width
+    (256, 256, 64, 6, 64),      # Lp = 64, BN = 256: a chunks of index 2j + half
+    (256, 128, 48, 6, 50),      # Lp = 64, BN = 128, L not a power of two
+    (300, 64, 72, 6, 64),       # Lp = 64, BN = 64, padded row tail
+    (256, 64, 64, 8, 256),      # Lp = 256, BN = 64
+    (512, 128, 40, 8, 200),     # Lp = 256, BN = 128, early termination
+    (256, 256, 8, 7, 128),      # one macro step (8 reduction indices)
+    # CTA pairs (N > 128): the odd CTA's a rows / b rows partly or wholly past the end
+    (300, 300, 64, 7, 128),
+    (4096, 2560, 16, 7, 128),   # 80 pair tiles: clusters loop over several tiles
 ])
 def test_tc_shapes(cuda_device, M, N, K, p, L):
     g = torch.Generator().manual_seed(M + N + K)
@@ -77,6 +87,14 @@ def test_tc_unipolar_bias(cuda_device):
     a = torch.rand(256, 70, generator=g)
     b = torch.randn(128, 70, generator=g)
     _check(cuda_device, a, b, 7, 128, mode="unipolar", bias=torch.randn(128, generator=g))
+
+
+def test_tc_unipolar_rows(cuda_device):
+    """Unipolar through the row producers (K % 8 == 0): zero points and row sums."""
+    g = torch.Generator().manual_seed(4)
+    a = torch.rand(256, 72, generator=g)
+    b = torch.randn(192, 72, generator=g)
+    _check(cuda_device, a, b, 7, 128, mode="unipolar", bias=torch.randn(192, generator=g))
 
 
 def test_tc_row_stream_lengths(cuda_device):
