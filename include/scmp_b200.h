@@ -54,6 +54,12 @@ enum scmp_status {
 
 enum scmp_granularity { SCMP_PER_ROW = 0, SCMP_PER_HEAD = 1, SCMP_PER_TENSOR = 2 };
 enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
+/* Element types of a, b and out (scmp_matmul_args.io_flags; 0 = all fp32). */
+enum scmp_io_flags {
+  SCMP_IO_A_BF16 = 1,   /* a is bf16: widened exactly to fp32 before quantisation */
+  SCMP_IO_B_BF16 = 2,   /* b is bf16 */
+  SCMP_IO_OUT_BF16 = 4  /* out is bf16: the fp32 result (bias included) rounded to nearest even */
+};
 enum scmp_engine {
   SCMP_ENGINE_AUTO = 0,
   SCMP_ENGINE_POPC = 1,    /* CUDA-core LOP3 + POPC over bit-packed streams */
@@ -63,10 +69,11 @@ enum scmp_engine {
 typedef struct scmp_matmul_args {
   int32_t abi_version;      /* must be SCMP_ABI_VERSION */
   int32_t engine;           /* enum scmp_engine */
-  /* a: [batch, M, K] fp32 contiguous; b: [batch_b, N, K] with batch_b in
-   * {1, batch} (1 = b shared by every slice, e.g. a weight). */
-  const float *a;
-  const float *b;
+  /* a: [batch, M, K] contiguous; b: [batch_b, N, K] with batch_b in
+   * {1, batch} (1 = b shared by every slice, e.g. a weight).  fp32, or bf16
+   * per io_flags. */
+  const void *a;
+  const void *b;
   int64_t batch, batch_b, M, N, K;
   int32_t granularity;      /* enum scmp_granularity */
   int32_t mode;             /* enum scmp_mode */
@@ -82,7 +89,7 @@ typedef struct scmp_matmul_args {
   int64_t k_segment;
   const uint8_t *pool;      /* stream pool R [pool_dims, 2^p] (uint8) */
   int32_t pool_dims;        /* reduction index d reads pool row d % pool_dims */
-  int32_t reserved0;
+  int32_t io_flags;         /* enum scmp_io_flags bits; 0 = fp32 a, b, out */
   /* Optional per-a-row stream length [batch * M]: > 0 computes the row with
    * that L, 0 writes the pruned row (zeros + bias), < 0 leaves the output row
    * untouched (it belongs to another call).  NULL = every row uses stoc_len. */
@@ -90,7 +97,7 @@ typedef struct scmp_matmul_args {
   /* Optional per-slice stream length [batch] (same meaning, per slice). */
   const int32_t *slice_stoc_len;
   const float *bias;        /* nullable [N], added after the rescale */
-  float *out;               /* [batch, M, N] fp32 */
+  void *out;                /* [batch, M, N] fp32, or bf16 per io_flags */
   int32_t *acc_out;         /* nullable [batch, M, N] signed popcount sums */
   void *workspace;          /* device scratch, see scmp_sc_matmul_workspace_size */
   size_t workspace_bytes;

@@ -22,6 +22,7 @@ STATUS_NAMES = {
 GRANULARITY = {"per_row": 0, "per_head": 1, "per_tensor": 2}
 MODE = {"bipolar": 0, "unipolar": 1}
 ENGINE = {"auto": 0, "popc": 1, "tcgen05": 2}
+IO_A_BF16, IO_B_BF16, IO_OUT_BF16 = 1, 2, 4  # scmp_matmul_args.io_flags bits
 
 EXPORTED_SYMBOLS = (
     "scmp_sc_matmul_workspace_size",
@@ -56,7 +57,7 @@ class MatmulArgs(ctypes.Structure):
         ("k_segment", ctypes.c_int64),
         ("pool", ctypes.c_void_p),
         ("pool_dims", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("io_flags", ctypes.c_int32),
         ("row_stoc_len", ctypes.c_void_p),
         ("slice_stoc_len", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),

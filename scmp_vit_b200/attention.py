@@ -146,18 +146,24 @@ def _av_rows_by_prec(a_flat, b_flat, row_L: torch.Tensor, levels, counts, *, mod
 
 
 def sc_qk(q: torch.Tensor, k: torch.Tensor, sc_prec: int, *, mp_cfg=None,
-          cfg_for: Optional[CfgFor] = None) -> torch.Tensor:
-    """SC ``q @ k^T`` for q, k ``[B, H, N, D]`` -> ``[B, H, N, N]`` fp32, unscaled."""
+          cfg_for: Optional[CfgFor] = None,
+          out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """SC ``q @ k^T`` for q, k ``[B, H, N, D]`` -> ``[B, H, N, N]`` fp32, unscaled.
+
+    ``out_dtype=torch.bfloat16`` lets the uniform path write the scores in
+    bf16 directly (the fp32 result rounded to nearest even); bf16 q, k are
+    read without an fp32 copy (widening is exact)."""
     cfg_for = cfg_for or _scl._get_config
     B, H, N, D = q.shape
-    qf = q.float().reshape(B * H, N, D)
-    kf = k.float().reshape(B * H, N, D)
     if mp_cfg is None:
         if _scl.USE_NOISE_MODEL:
             return _noisy_matmul_core(q.float(), k.float(), L=2 ** sc_prec, mode="bipolar")
-        out = sc_matmul(qf, kf, granularity="per_head", sc_prec=sc_prec,
-                        config=cfg_for(D, sc_prec), stoc_len=2 ** sc_prec)
+        out = sc_matmul(q.reshape(B * H, N, D), k.reshape(B * H, N, D), granularity="per_head",
+                        sc_prec=sc_prec, config=cfg_for(D, sc_prec), stoc_len=2 ** sc_prec,
+                        out_dtype=out_dtype)
         return out.reshape(B, H, N, N)
+    qf = q.float().reshape(B * H, N, D)
+    kf = k.float().reshape(B * H, N, D)
     metric = q.float().abs().amax(dim=(0, 2, 3))  # per head
     if isinstance(mp_cfg, AdaptiveMPConfig):
         t, T = _scl.get_vit_timestep()
@@ -193,19 +199,22 @@ def sc_qk(q: torch.Tensor, k: torch.Tensor, sc_prec: int, *, mp_cfg=None,
 
 
 def sc_av(attn: torch.Tensor, v: torch.Tensor, sc_prec: int, *, mode: str = "bipolar",
-          mp_cfg=None, cfg_for: Optional[CfgFor] = None) -> torch.Tensor:
+          mp_cfg=None, cfg_for: Optional[CfgFor] = None,
+          out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
     """SC ``attn @ v`` for attn ``[B, H, N, N]``, v ``[B, H, N, D]`` ->
-    ``[B, H, N, D]`` fp32; per-row scales for attn rows and v columns."""
+    ``[B, H, N, D]`` fp32; per-row scales for attn rows and v columns.
+    ``out_dtype`` and bf16 inputs as in ``sc_qk`` (uniform path)."""
     cfg_for = cfg_for or _scl._get_config
     B, H, N, D = v.shape
+    if mp_cfg is None and not _scl.USE_NOISE_MODEL:
+        out = sc_matmul(attn.reshape(B * H, N, N), v.transpose(-1, -2).reshape(B * H, D, N),
+                        granularity="per_row", group_a=1, group_b=1, mode=mode,
+                        sc_prec=sc_prec, config=cfg_for(N, sc_prec), out_dtype=out_dtype)
+        return out.reshape(B, H, N, D)
     a_flat = attn.float().reshape(B * H, N, N)
     b_flat = v.float().transpose(-1, -2).reshape(B * H, D, N)
     if mp_cfg is None:
-        if _scl.USE_NOISE_MODEL:
-            out = _noisy_matmul_core(a_flat, b_flat, L=2 ** sc_prec, mode=mode, per_row_scale=True)
-        else:
-            out = sc_matmul(a_flat, b_flat, granularity="per_row", group_a=1, group_b=1,
-                            mode=mode, sc_prec=sc_prec, config=cfg_for(N, sc_prec))
+        out = _noisy_matmul_core(a_flat, b_flat, L=2 ** sc_prec, mode=mode, per_row_scale=True)
         return out.reshape(B, H, N, D)
     score = av_row_score(a_flat)  # [BH, N]
     if isinstance(mp_cfg, AdaptiveMPConfig):
@@ -244,6 +253,12 @@ def sc_av(attn: torch.Tensor, v: torch.Tensor, sc_prec: int, *, mode: str = "bip
     return out.reshape(B, H, N, D)
 
 
+def _glue_dtype(x: torch.Tensor) -> Optional[torch.dtype]:
+    """bf16 models take SC results in bf16 straight from the engine (the same
+    values ``.to(torch.bfloat16)`` gives); otherwise fp32."""
+    return torch.bfloat16 if x.dtype == torch.bfloat16 else None
+
+
 def make_sc_attention_forward(sc_prec: int, sc_av: bool, sc_qk: bool = True,
                               qk_mp_cfg: MPConfig | None = None,
                               av_mp_cfg: MPConfig | None = None, *,
@@ -261,14 +276,15 @@ def make_sc_attention_forward(sc_prec: int, sc_av: bool, sc_qk: bool = True,
         q, k, v = torch.unbind(qkv, 2)
         q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if sc_qk:
-            attn = sc_qk_fn(q, k, sc_prec, mp_cfg=qk_mp_cfg, cfg_for=cfg_for)
+            attn = sc_qk_fn(q, k, sc_prec, mp_cfg=qk_mp_cfg, cfg_for=cfg_for,
+                            out_dtype=_glue_dtype(x))
             attn = attn.to(x.dtype) * self.scale
         else:
             attn = (q @ k.transpose(-2, -1)) * self.scale
         attn = attn.softmax(dim=-1)
         if do_av:
             out = sc_av_fn(attn, v, sc_prec, mode=av_mode, mp_cfg=av_mp_cfg,
-                           cfg_for=cfg_for).to(x.dtype)
+                           cfg_for=cfg_for, out_dtype=_glue_dtype(x)).to(x.dtype)
         else:
             out = attn @ v
         out = out.transpose(1, 2).reshape(B, N, C)

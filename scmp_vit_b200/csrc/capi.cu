@@ -35,10 +35,13 @@ unsigned int *engine_error_ptr() {
 }
 
 // Rows of the tail that the CUDA-core engine takes instead of padding a
-// tensor-core tile (e.g. the 257th token).
+// tensor-core tile (e.g. the 257th token).  Up to 8 rows run on the
+// warp-per-output kernel at full occupancy; a longer tail costs less as a
+// padded tensor-core tile (the tensor cores do ~5x the bit-products per
+// second of the CUDA-core engine).
 int64_t tc_rows(int64_t rows, int64_t tile) {
   const int64_t tail = rows % tile;
-  if (tail != 0 && tail <= tile / 8 && rows > tile) return rows - tail;
+  if (tail != 0 && tail <= 8 && rows > tile) return rows - tail;
   return rows;
 }
 
@@ -62,6 +65,7 @@ inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct OperandLayout {
   GroupShape g;
+  int64_t ldc;  // code row stride
   size_t stat, gscale, ginv, gzero, code, rscale, rzero, rsum;  // offsets
 };
 
@@ -93,13 +97,14 @@ GroupShape make_groups(int gran, int64_t slices, int64_t rows_per_slice, int64_t
   return g;
 }
 
-void layout_operand(Carver &c, OperandLayout &o, int64_t K) {
+void layout_operand(Carver &c, OperandLayout &o, int64_t K, int64_t ldc) {
+  o.ldc = ldc;
   const int64_t rows = o.g.rows, ng = o.g.ngroups;
   o.stat = c.take(sizeof(float2) * rows);
   o.gscale = c.take(sizeof(float) * ng);
   o.ginv = c.take(sizeof(float) * ng);
   o.gzero = c.take(sizeof(int32_t) * ng);
-  o.code = c.take(sizeof(int16_t) * rows * K);
+  o.code = c.take(sizeof(int16_t) * rows * ldc);
   o.rscale = c.take(sizeof(float) * rows);
   o.rzero = c.take(sizeof(int32_t) * rows);
   o.rsum = c.take(sizeof(int32_t) * rows);
@@ -109,6 +114,8 @@ struct Plan {
   OperandLayout A, B;
   size_t table = 0;
   size_t pool_comp = 0;
+  int64_t pool_comp_rows = 0;
+  int64_t ldk = 0;
   size_t total = 0;
 };
 
@@ -143,6 +150,8 @@ int validate(const scmp_matmul_args *x) {
         (x->granularity != SCMP_PER_ROW || x->group_a != 1 || x->group_b != 1))
       return fail(SCMP_EINVAL, "k_segment needs granularity per_row with group_a=group_b=1");
   }
+  if (x->io_flags & ~(SCMP_IO_A_BF16 | SCMP_IO_B_BF16 | SCMP_IO_OUT_BF16))
+    return fail(SCMP_EINVAL, "unknown io_flags bits 0x%x", (unsigned)x->io_flags);
   if (x->engine != SCMP_ENGINE_AUTO && x->engine != SCMP_ENGINE_POPC &&
       x->engine != SCMP_ENGINE_TCGEN05)
     return fail(SCMP_EINVAL, "unknown engine %d", x->engine);
@@ -158,28 +167,32 @@ Plan make_plan(const scmp_matmul_args *x) {
   const int64_t kseg = seg_len(x), nseg = x->K / kseg;
   p.A.g = make_groups(x->granularity, x->batch, x->M * nseg, nseg > 1 ? 1 : x->group_a);
   p.B.g = make_groups(x->granularity, x->batch_b, x->N * nseg, nseg > 1 ? 1 : x->group_b);
-  layout_operand(c, p.A, kseg);
-  layout_operand(c, p.B, kseg);
+  // unsegmented code rows are padded to a multiple of 8 (16-byte rows)
+  const int64_t ldc = nseg > 1 ? kseg : (kseg + 7) / 8 * 8;
+  p.ldk = nseg > 1 ? x->K : ldc;
+  layout_operand(c, p.A, kseg, ldc);
+  layout_operand(c, p.B, kseg, ldc);
   const int T = 1 << x->sc_prec;
   const int WT = T >= 32 ? T / 32 : 1;
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
-  p.pool_comp = c.take((size_t)x->pool_dims * T);
+  p.pool_comp_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
+  p.pool_comp = c.take((size_t)p.pool_comp_rows * T);
   p.total = c.off;
   return p;
 }
 
-int quantize_operand(const float *x, const OperandLayout &o, int64_t K, int mode, int prec,
-                     unsigned char *ws, cudaStream_t s) {
+int quantize_operand(const void *x, bool x_bf16, const OperandLayout &o, int64_t K, int mode,
+                     int prec, unsigned char *ws, cudaStream_t s) {
   cudaError_t e;
   auto *stat = reinterpret_cast<float2 *>(ws + o.stat);
   auto *gscale = reinterpret_cast<float *>(ws + o.gscale);
   auto *ginv = reinterpret_cast<float *>(ws + o.ginv);
   auto *gzero = reinterpret_cast<int32_t *>(ws + o.gzero);
-  if ((e = launch_row_stats(x, o.g.rows, K, mode, stat, s)) != cudaSuccess)
+  if ((e = launch_row_stats(x, x_bf16, o.g.rows, K, mode, stat, s)) != cudaSuccess)
     return cuda_fail(e, "row_stats launch");
   if ((e = launch_group_stats(stat, o.g, mode, prec, gscale, ginv, gzero, s)) != cudaSuccess)
     return cuda_fail(e, "group_stats launch");
-  if ((e = launch_quantize(x, o.g, K, mode, prec, gscale, ginv, gzero,
+  if ((e = launch_quantize(x, x_bf16, o.g, K, o.ldc, mode, prec, gscale, ginv, gzero,
                            reinterpret_cast<int16_t *>(ws + o.code),
                            reinterpret_cast<float *>(ws + o.rscale),
                            reinterpret_cast<int32_t *>(ws + o.rzero),
@@ -248,8 +261,12 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   auto s = static_cast<cudaStream_t>(stream);
 
   const int64_t kseg = seg_len(&x);
-  if ((rc = quantize_operand(x.a, plan.A, kseg, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
-  if ((rc = quantize_operand(x.b, plan.B, kseg, x.mode, x.sc_prec, ws, s)) != SCMP_OK) return rc;
+  if ((rc = quantize_operand(x.a, (x.io_flags & SCMP_IO_A_BF16) != 0, plan.A, kseg, x.mode,
+                             x.sc_prec, ws, s)) != SCMP_OK)
+    return rc;
+  if ((rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, plan.B, kseg, x.mode,
+                             x.sc_prec, ws, s)) != SCMP_OK)
+    return rc;
   auto *table = reinterpret_cast<uint32_t *>(ws + plan.table);
   cudaError_t e;
 
@@ -261,6 +278,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.M = x.M;
   P.N = x.N;
   P.K = x.K;
+  P.ldk = plan.ldk;
   P.kseg = kseg;
   P.nseg = (int)(x.K / kseg);
   P.mode = x.mode;
@@ -272,6 +290,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.slice_L = x.slice_stoc_len;
   P.bias = x.bias;
   P.out = x.out;
+  P.out_bf16 = (x.io_flags & SCMP_IO_OUT_BF16) != 0;
   P.acc_out = x.acc_out;
   P.stream_table = table;
   P.pool_comp = ws + plan.pool_comp;
@@ -297,7 +316,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
     n_tc = tc_rows(x.N, tc_tile_n(P, x.N));
     if (tc_row_producers(P)) {
       const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
-      if ((e = launch_pool_complement(x.pool, x.pool_dims, x.sc_prec, shift,
+      if ((e = launch_pool_complement(x.pool, x.pool_dims, plan.pool_comp_rows, x.sc_prec, shift,
                                       ws + plan.pool_comp, s)) != cudaSuccess)
         return cuda_fail(e, "pool_complement launch");
       count_launches(1);

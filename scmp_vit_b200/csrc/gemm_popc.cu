@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
       if (gm < P.m_hi && d < P.K) {
         const int64_t grow = slice * P.M + gm;
         const int L = row_stream_len(P, slice, grow);
-        const int c = P.qa.code[grow * P.K + d];
+        const int c = P.qa.code[grow * P.ldk + d];
         s = c < 0 ? -1 : 1;
         if (L > 0) k = ((c < 0 ? -c : c) * L) >> P.prec;
       }
@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
       uint32_t *dst = sB + (dd * BN + n) * LW;
       int s = 1;
       if (gn < P.n_hi && d < P.K) {
-        const int c = P.qb.code[(slice_b * P.N + gn) * P.K + d];
+        const int c = P.qb.code[(slice_b * P.N + gn) * P.ldk + d];
         s = c < 0 ? -1 : 1;
         const int v = c < 0 ? -c : c;
         const uint32_t *st =
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kThreads) gemm_popc_kernel(GemmProblem P) {
       float v = L > 0 ? y[i][j] : 0.0f;
       if (P.bias) v = __fadd_rn(v, P.bias[gn]);
       const int64_t o = grow * P.N + gn;
-      P.out[o] = v;
+      store_out(P, o, v);
       if (P.acc_out) P.acc_out[o] = L > 0 ? acc_sum[i][j] : 0;
     }
   }
@@ -183,12 +183,16 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
     if (L < 0) continue;  // warp-uniform
     int acc = 0;
     if (L > 0) {
-      const int16_t *ca = P.qa.code + grow * P.K;
-      const int16_t *cb = P.qb.code + brow * P.K;
-      for (int64_t d = lane; d < P.K; d += 32) {
+      const int16_t *ca = P.qa.code + grow * P.ldk;
+      const int16_t *cb = P.qb.code + brow * P.ldk;
+      const int pd = P.pool_dims;
+      int dm = lane % pd;  // pool row d mod pool_dims, advanced without a division
+      for (int d = lane; d < (int)P.K; d += 32) {
         const int a = ca[d], b = cb[d];
         const int k = ((a < 0 ? -a : a) * L) >> P.prec;
-        const uint32_t *st = P.stream_table + ((d % P.pool_dims) * (T + 1) + (b < 0 ? -b : b)) * WT;
+        const uint32_t *st = P.stream_table + ((int64_t)dm * (T + 1) + (b < 0 ? -b : b)) * WT;
+        dm += 32;
+        while (dm >= pd) dm -= pd;
         int cnt = 0;
 #pragma unroll
         for (int w = 0; w < LW; ++w) {
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
         y = sc_rescale(P.mode, P.prec, L, acc, P.K, P.qa.scale[grow], P.qa.zero[grow],
                        P.qa.rowsum[grow], P.qb.scale[brow], P.qb.zero[brow], P.qb.rowsum[brow]);
       if (P.bias) y = __fadd_rn(y, P.bias[gn]);
-      P.out[grow * P.N + gn] = y;
+      store_out(P, grow * P.N + gn, y);
       if (P.acc_out) P.acc_out[grow * P.N + gn] = L > 0 ? acc : 0;
     }
   }

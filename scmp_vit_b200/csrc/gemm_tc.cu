@@ -450,7 +450,7 @@ __device__ bool produce_chunks(const TcParams &prm, const Bars &b, ProdState &st
     if (gm < prm.m_rows) {
       const int64_t grow = slice * P.M + gm;
       Lrow[i] = row_stream_len(P, slice, grow);
-      arow[i] = P.qa.code + grow * P.K;
+      arow[i] = P.qa.code + grow * P.ldk;
     }
   }
   bool bval[kNB];
@@ -459,7 +459,7 @@ __device__ bool produce_chunks(const TcParams &prm, const Bars &b, ProdState &st
   for (int i = 0; i < kNB; ++i) {
     const int64_t gn = n0 + rsub + 64 * i;
     bval[i] = (rsub + 64 * i < BN) && gn < prm.n_rows;
-    brow[i] = bval[i] ? P.qb.code + (slice_b * P.N + gn) * P.K : P.qb.code;
+    brow[i] = bval[i] ? P.qb.code + (slice_b * P.N + gn) * P.ldk : P.qb.code;
   }
   // ---- prefetch k-block 0
   int16_t ca_n[kRowsA], cb_n[kNB];
@@ -639,8 +639,8 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
   }
   const int64_t gnB = n0 + rbn;
   const int64_t growB = slice_b * P.N + (gnB < prm.n_rows ? gnB : prm.n_rows - 1);
-  const uint4 *pa = reinterpret_cast<const uint4 *>(P.qa.code + growA * P.K);
-  const uint4 *pb = reinterpret_cast<const uint4 *>(P.qb.code + growB * P.K);
+  const uint4 *pa = reinterpret_cast<const uint4 *>(P.qa.code + growA * P.ldk);
+  const uint4 *pb = reinterpret_cast<const uint4 *>(P.qb.code + growB * P.ldk);
   // shared-memory addresses of this thread's chunks in stage 0
   uint32_t sA[4], sB[NBC];
 #pragma unroll
@@ -658,11 +658,11 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
   const uint32_t stage_bytes = prm.stage_bytes;
   const int prec = P.prec;
   const int shift = prm.shift_pool;
-  const int nmacro = (int)(P.K >> 3);
+  const int nmacro = (int)(P.ldk >> 3);  // zero-padded indices past K add nothing
   const int msteps_seg = kSeg ? prm.kseg >> 3 : 0;  // macro steps per segment
   const uint8_t *pcomp = P.pool_comp + t0B;
   // pool rows one segment (or the whole K) spans; prefetches wrap inside it
-  const int prow_lim = kSeg ? prm.kseg : (int)P.K;
+  const int prow_lim = kSeg ? prm.kseg : (int)P.ldk;
   int pbase = 0;  // pool row of the macro step's first reduction index
   int mseg = 0;   // macro steps done in the current segment
   uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
@@ -820,7 +820,7 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         }
         if (P.bias) y = __fadd_rn(y, bias);
         const int64_t o = (grow0 + r) * P.N + gn;
-        P.out[o] = y;
+        store_out(P, o, y);
         if (!kSeg && P.acc_out) P.acc_out[o] = a;
       }
       __syncwarp();
@@ -1232,7 +1232,7 @@ int padded_stream_log2(const GemmProblem &P) {
 
 bool tc_supported(const GemmProblem &P) {
   if (P.prec < 5 || P.prec > 8) return false;           // pool rows >= 32 bytes
-  if (P.K * 256 >= (int64_t)1 << 31) return false;      // 32-bit k-block index math
+  if (P.ldk * 256 >= (int64_t)1 << 31) return false;    // 32-bit k-block index math
   if (P.mode == SCMP_UNIPOLAR && P.prec == 8) return false;  // 8-bit thresholds
   if (P.nseg == 1) return P.pool_dims >= P.K;           // reduction index = pool row
   // segmented K: whole k-blocks per segment, pool row = index inside segment;
@@ -1243,9 +1243,10 @@ bool tc_supported(const GemmProblem &P) {
 
 bool tc_row_producers(const GemmProblem &P) {
   const int lg = padded_stream_log2(P);
-  if (lg < 6 || lg > 8 || (P.K & 7) != 0) return false;
+  if (lg < 6 || lg > 8 || (P.ldk & 7) != 0) return false;
   if (P.nseg > 1 && (P.kseg & 7) != 0) return false;  // segments end on macro steps
-  // 16-byte code loads: rows of K int16 codes from 16-byte aligned planes
+  // 16-byte code loads: rows of ldk int16 codes from 16-byte aligned planes
+  // (pool complement rows cover the padded indices)
   return ((reinterpret_cast<uintptr_t>(P.qa.code) | reinterpret_cast<uintptr_t>(P.qb.code)) & 15) ==
          0;
 }
@@ -1265,7 +1266,9 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   const int lg = padded_stream_log2(P);
   prm.lp_log2 = lg;
   prm.shift_pool = (P.mode == SCMP_BIPOLAR && P.prec == 8) ? 1 : 0;
-  prm.nkb = (P.K * ((int64_t)1 << lg) + kKB - 1) / kKB;
+  // row producers run every padded index (ldk); chunk producers stop at K
+  const int64_t krun = tc_row_producers(P) ? P.ldk : P.K;
+  prm.nkb = (krun * ((int64_t)1 << lg) + kKB - 1) / kKB;
   prm.nseg = P.nseg;
   prm.kseg = (int)P.kseg;
   prm.nkb_seg = P.nseg > 1 ? ((P.kseg << lg) / kKB) : prm.nkb;

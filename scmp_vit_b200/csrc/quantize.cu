@@ -3,6 +3,8 @@
 // Bit-exact restatement of sco_quantize in oracle/sc_oracle.c: IEEE fp32
 // divide/multiply (no contraction), round-half-even, 1e-6 floor on the range
 // (reference sc_integration/sc_linear.py:95-111).
+#include <type_traits>
+
 #include "sc_common.cuh"
 
 namespace scmp {
@@ -18,6 +20,17 @@ __device__ __forceinline__ float warp_min(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+template <typename T>
+__device__ __forceinline__ float ldx(const T *p);
+template <>
+__device__ __forceinline__ float ldx<float>(const float *p) {
+  return __ldg(p);
+}
+template <>
+__device__ __forceinline__ float ldx<__nv_bfloat16>(const __nv_bfloat16 *p) {
+  return __bfloat162float(__ldg(p));
+}
+
 __device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -25,14 +38,25 @@ __device__ __forceinline__ int warp_sum(int v) {
 }
 
 // One warp per row: (max|x|, -) for bipolar, (min x, max x) for unipolar.
-__global__ void row_stats_kernel(const float *__restrict__ x, int64_t rows, int64_t K, int mode,
+template <typename T>
+__global__ void row_stats_kernel(const T *__restrict__ x, int64_t rows, int64_t K, int mode,
                                  float2 *__restrict__ stat) {
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
-  const float *xr = x + warp * K;
+  const T *xr = x + warp * K;
   float lo = INFINITY, hi = -INFINITY;
-  if ((K & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
+  if constexpr (!std::is_same<T, float>::value) {
+    for (int64_t i = lane; i < K; i += 32) {
+      const float v = ldx(xr + i);
+      if (mode == SCMP_BIPOLAR) {
+        hi = fmaxf(hi, fabsf(v));
+      } else {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+      }
+    }
+  } else if ((K & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
     const float4 *x4 = reinterpret_cast<const float4 *>(xr);
     for (int64_t i = lane; i < (K >> 2); i += 32) {
       float4 v = __ldg(x4 + i);
@@ -59,8 +83,52 @@ __global__ void row_stats_kernel(const float *__restrict__ x, int64_t rows, int6
   if (lane == 0) stat[warp] = make_float2(lo, hi);
 }
 
-// One block per scale group.
-__global__ void group_stats_kernel(const float2 *__restrict__ stat, GroupShape g, int mode,
+// Scale of one group from its min / max (shared by both group kernels).
+__device__ __forceinline__ void write_group_scale(int64_t grp, float lo, float hi, int mode,
+                                                  int prec, float *__restrict__ gscale,
+                                                  float *__restrict__ ginv,
+                                                  int32_t *__restrict__ gzero) {
+  if (mode == SCMP_BIPOLAR) {
+    const float qmax = (float)((1 << (prec - 1)) - 1);
+    const float amax = hi > 1e-6f ? hi : 1e-6f;
+    gscale[grp] = __fdiv_rn(amax, qmax);
+    ginv[grp] = __fdiv_rn(qmax, amax);
+    gzero[grp] = 0;
+  } else {
+    const float qmax = (float)((1 << prec) - 1);
+    float rng = __fsub_rn(hi, lo);
+    if (!(rng > 1e-6f)) rng = 1e-6f;
+    const float inv = __fdiv_rn(qmax, rng);
+    gscale[grp] = __fdiv_rn(rng, qmax);
+    ginv[grp] = inv;
+    gzero[grp] = __float2int_rn(__fmul_rn(-lo, inv));
+  }
+}
+
+// Small groups (per-row scaling, a few rows per group): one thread per group.
+__global__ void group_stats_small_kernel(const float2 *__restrict__ stat, GroupShape g, int mode,
+                                         int prec, float *__restrict__ gscale,
+                                         float *__restrict__ ginv, int32_t *__restrict__ gzero) {
+  for (int64_t grp = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; grp < g.ngroups;
+       grp += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t slice = grp / g.groups_per_slice;
+    const int64_t j = grp % g.groups_per_slice;
+    const int64_t r0 = slice * g.slice_rows + j * g.group_rows;
+    int64_t r1 = r0 + g.group_rows;
+    const int64_t slice_end = (slice + 1) * g.slice_rows;
+    if (r1 > slice_end) r1 = slice_end;
+    float lo = INFINITY, hi = -INFINITY;
+    for (int64_t r = r0; r < r1; ++r) {
+      const float2 s = stat[r];
+      lo = fminf(lo, s.x);
+      hi = fmaxf(hi, s.y);
+    }
+    write_group_scale(grp, lo, hi, mode, prec, gscale, ginv, gzero);
+  }
+}
+
+// Large groups: one block per scale group.
+__global__ void __launch_bounds__(1024) group_stats_kernel(const float2 *__restrict__ stat, GroupShape g, int mode,
                                    int prec, float *__restrict__ gscale,
                                    float *__restrict__ ginv, int32_t *__restrict__ gzero) {
   const int64_t grp = blockIdx.x;
@@ -72,6 +140,7 @@ __global__ void group_stats_kernel(const float2 *__restrict__ stat, GroupShape g
   const int64_t slice_end = (slice + 1) * g.slice_rows;
   if (r1 > slice_end) r1 = slice_end;
   float lo = INFINITY, hi = -INFINITY;
+#pragma unroll 4
   for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
     float2 s = stat[r];
     lo = fminf(lo, s.x);
@@ -89,29 +158,16 @@ __global__ void group_stats_kernel(const float2 *__restrict__ stat, GroupShape g
     hi = lane < nw ? shi[lane] : -INFINITY;
     lo = warp_min(lo);
     hi = warp_max(hi);
-    if (lane == 0) {
-      if (mode == SCMP_BIPOLAR) {
-        const float qmax = (float)((1 << (prec - 1)) - 1);
-        const float amax = hi > 1e-6f ? hi : 1e-6f;
-        gscale[grp] = __fdiv_rn(amax, qmax);
-        ginv[grp] = __fdiv_rn(qmax, amax);
-        gzero[grp] = 0;
-      } else {
-        const float qmax = (float)((1 << prec) - 1);
-        float rng = __fsub_rn(hi, lo);
-        if (!(rng > 1e-6f)) rng = 1e-6f;
-        const float inv = __fdiv_rn(qmax, rng);
-        gscale[grp] = __fdiv_rn(rng, qmax);
-        ginv[grp] = inv;
-        gzero[grp] = __float2int_rn(__fmul_rn(-lo, inv));
-      }
-    }
+    if (lane == 0) write_group_scale(grp, lo, hi, mode, prec, gscale, ginv, gzero);
   }
 }
 
 // One warp per row: signed codes, per-row scale/zero, magnitude row sum.
-__global__ void quantize_kernel(const float *__restrict__ x, GroupShape g, int64_t K, int mode,
-                                int prec, const float *__restrict__ gscale,
+// Codes are written with row stride ldc >= K; indices K .. ldc-1 get code 0,
+// which contributes nothing to any count (zero window, zero threshold).
+template <typename T>
+__global__ void quantize_kernel(const T *__restrict__ x, GroupShape g, int64_t K, int64_t ldc,
+                                int mode, int prec, const float *__restrict__ gscale,
                                 const float *__restrict__ ginv, const int32_t *__restrict__ gzero,
                                 int16_t *__restrict__ code, float *__restrict__ rscale,
                                 int32_t *__restrict__ rzero, int32_t *__restrict__ rsum) {
@@ -121,13 +177,14 @@ __global__ void quantize_kernel(const float *__restrict__ x, GroupShape g, int64
   const int64_t grp = group_of_row(g, row);
   const float inv = ginv[grp];
   const int32_t z = gzero[grp];
-  const float *xr = x + row * K;
-  int16_t *cr = code + row * K;
+  const T *xr = x + row * K;
+  int16_t *cr = code + row * ldc;
+  for (int64_t i = K + lane; i < ldc; i += 32) cr[i] = 0;
   int acc = 0;
   if (mode == SCMP_BIPOLAR) {
     const int iq = (1 << (prec - 1)) - 1;
     for (int64_t i = lane; i < K; i += 32) {
-      int q = __float2int_rn(__fmul_rn(__ldg(xr + i), inv));
+      int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv));
       q = max(-iq, min(iq, q));
       cr[i] = (int16_t)(2 * q);
       acc += 2 * abs(q);
@@ -135,7 +192,7 @@ __global__ void quantize_kernel(const float *__restrict__ x, GroupShape g, int64
   } else {
     const int iq = (1 << prec) - 1;
     for (int64_t i = lane; i < K; i += 32) {
-      int q = __float2int_rn(__fmul_rn(__ldg(xr + i), inv)) + z;
+      int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv)) + z;
       q = max(0, min(iq, q));
       cr[i] = (int16_t)q;
       acc += q;
@@ -173,40 +230,64 @@ __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_d
 // PC[d][t] = 0x7F - (R[d][t] >> shift).  The tensor-core engine forms the
 // stream byte 0x7F + u - (R >> shift) for a threshold u < 128: its top bit is
 // [R >> shift < u], with no borrow into the neighbouring byte.
-__global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int64_t bytes, int shift,
-                                       uint8_t *__restrict__ out) {
+// Rows past the pool (reduction indices of zero padding) hold 0x7F: with a
+// zero threshold they produce no stream bits.
+__global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int64_t pool_bytes,
+                                       int64_t bytes, int shift, uint8_t *__restrict__ out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes;
        i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = (uint8_t)(0x7F - (pool[i] >> shift));
+    out[i] = i < pool_bytes ? (uint8_t)(0x7F - (pool[i] >> shift)) : (uint8_t)0x7F;
 }
 
 }  // namespace
 
-cudaError_t launch_row_stats(const float *x, int64_t rows, int64_t K, int mode, float2 *stat,
-                             cudaStream_t s) {
+cudaError_t launch_row_stats(const void *x, bool x_bf16, int64_t rows, int64_t K, int mode,
+                             float2 *stat, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
-  row_stats_kernel<<<(unsigned)blocks, threads, 0, s>>>(x, rows, K, mode, stat);
+  if (x_bf16)
+    row_stats_kernel<<<(unsigned)blocks, threads, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(x), rows, K, mode, stat);
+  else
+    row_stats_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const float *>(x), rows, K,
+                                                          mode, stat);
   return cudaGetLastError();
 }
 
 cudaError_t launch_group_stats(const float2 *stat, const GroupShape &g, int mode, int prec,
                                float *gscale, float *ginv, int32_t *gzero, cudaStream_t s) {
   if (g.ngroups == 0) return cudaSuccess;
-  group_stats_kernel<<<(unsigned)g.ngroups, 256, 0, s>>>(stat, g, mode, prec, gscale, ginv, gzero);
+  if (g.group_rows <= 64) {
+    const int64_t blocks = (g.ngroups + 255) / 256;
+    group_stats_small_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(
+        stat, g, mode, prec, gscale, ginv, gzero);
+    return cudaGetLastError();
+  }
+  // few large groups (per-tensor / per-head over a whole batch): one wide
+  // block per group keeps many row-stat loads in flight
+  const int threads = g.ngroups < 296 ? 1024 : 256;
+  group_stats_kernel<<<(unsigned)g.ngroups, threads, 0, s>>>(stat, g, mode, prec, gscale, ginv,
+                                                             gzero);
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int mode, int prec,
+cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int64_t K,
+                            int64_t ldc, int mode, int prec,
                             const float *gscale, const float *ginv, const int32_t *gzero,
                             int16_t *code, float *rscale, int32_t *rzero, int32_t *rsum,
                             cudaStream_t s) {
   if (g.rows == 0) return cudaSuccess;
   const int threads = 256;
   const int64_t blocks = (g.rows * 32 + threads - 1) / threads;
-  quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(x, g, K, mode, prec, gscale, ginv, gzero,
-                                                        code, rscale, rzero, rsum);
+  if (x_bf16)
+    quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), g,
+                                                          K, ldc, mode, prec, gscale, ginv, gzero,
+                                                          code, rscale, rzero, rsum);
+  else
+    quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const float *>(x), g, K, ldc,
+                                                          mode, prec, gscale, ginv, gzero, code,
+                                                          rscale, rzero, rsum);
   return cudaGetLastError();
 }
 
@@ -216,12 +297,13 @@ cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, ui
   return cudaGetLastError();
 }
 
-cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int prec, int shift,
-                                   uint8_t *out, cudaStream_t s) {
-  const int64_t bytes = (int64_t)pool_dims << prec;
+cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t rows, int prec,
+                                   int shift, uint8_t *out, cudaStream_t s) {
+  const int64_t pool_bytes = (int64_t)pool_dims << prec;
+  const int64_t bytes = (rows > pool_dims ? rows : (int64_t)pool_dims) << prec;
   const int64_t blocks = (bytes + 255) / 256;
-  pool_complement_kernel<<<(unsigned)(blocks < 296 ? blocks : 296), 256, 0, s>>>(pool, bytes, shift,
-                                                                               out);
+  pool_complement_kernel<<<(unsigned)(blocks < 296 ? blocks : 296), 256, 0, s>>>(
+      pool, pool_bytes, bytes, shift, out);
   return cudaGetLastError();
 }
 

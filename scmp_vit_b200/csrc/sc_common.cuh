@@ -2,6 +2,7 @@
 // include/scmp_b200.h).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -40,6 +41,9 @@ struct GemmProblem {
   QuantPlane qa, qb;
   int64_t batch, batch_b, M, N, K;
   int64_t kseg;  // segment length (K when unsegmented); per-(row, segment) scales
+  // code row stride: K rounded up to 8 (zero codes) when unsegmented, else K
+  // (segment rows of kseg codes back to back)
+  int64_t ldk;
   int nseg;      // K / kseg
   int mode, prec, stoc_len;
   const uint8_t *pool;  // [pool_dims, 2^prec]
@@ -47,7 +51,8 @@ struct GemmProblem {
   const int32_t *row_L;    // nullable [batch*M]
   const int32_t *slice_L;  // nullable [batch]
   const float *bias;
-  float *out;
+  void *out;     // fp32, or bf16 when out_bf16
+  int out_bf16;
   int32_t *acc_out;
   // stream table ST[pool_dims][2^p + 1][2^p / 32] (bit t of threshold v)
   const uint32_t *stream_table;
@@ -65,6 +70,14 @@ __device__ __forceinline__ int row_stream_len(const GemmProblem &P, int64_t slic
   return P.stoc_len;
 }
 
+// Store of one output element (fp32, or bf16 rounded to nearest even).
+__device__ __forceinline__ void store_out(const GemmProblem &P, int64_t o, float y) {
+  if (P.out_bf16)
+    static_cast<__nv_bfloat16 *>(P.out)[o] = __float2bfloat16_rn(y);
+  else
+    static_cast<float *>(P.out)[o] = y;
+}
+
 // Rescale of one accumulator (bit-exact restatement of oracle/sc_oracle.c).
 __device__ __forceinline__ float sc_rescale(int mode, int prec, int L, int32_t acc, int64_t K,
                                             float sa, int32_t za, int32_t rsa, float sb,
@@ -80,18 +93,21 @@ __device__ __forceinline__ float sc_rescale(int mode, int prec, int L, int32_t a
 }
 
 // Launchers (return cudaError_t of the launch).
-cudaError_t launch_row_stats(const float *x, int64_t rows, int64_t K, int mode, float2 *stat,
-                             cudaStream_t s);
+// x is fp32, or bf16 when x_bf16 (widened exactly on load).
+cudaError_t launch_row_stats(const void *x, bool x_bf16, int64_t rows, int64_t K, int mode,
+                             float2 *stat, cudaStream_t s);
 cudaError_t launch_group_stats(const float2 *stat, const GroupShape &g, int mode, int prec,
                                float *gscale, float *ginv, int32_t *gzero, cudaStream_t s);
-cudaError_t launch_quantize(const float *x, const GroupShape &g, int64_t K, int mode, int prec,
+cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int64_t K,
+                            int64_t ldc, int mode, int prec,
                             const float *gscale, const float *ginv, const int32_t *gzero,
                             int16_t *code, float *rscale, int32_t *rzero, int32_t *rsum,
                             cudaStream_t s);
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
-cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int prec, int shift,
-                                   uint8_t *out, cudaStream_t s);
+// PC over max(pool_dims, rows) rows (rows past the pool hold 0x7F)
+cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t rows, int prec,
+                                   int shift, uint8_t *out, cudaStream_t s);
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 bool tc_supported(const GemmProblem &P);
 int tc_block_n(int64_t N);

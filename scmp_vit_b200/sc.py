@@ -84,7 +84,8 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
               out: Optional[torch.Tensor] = None,
               acc_out: Optional[torch.Tensor] = None,
               k_segment: int = 0,
-              engine: Optional[str] = None) -> torch.Tensor:
+              engine: Optional[str] = None,
+              out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
     """SC estimate of ``a @ b^T`` (see module docstring).
 
     Extra keyword arguments beyond the reference signature:
@@ -93,7 +94,11 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     row untouched), ``slice_stoc_len`` (int32 per slice), ``out``,
     ``acc_out`` (int32 signed popcount sums, for parity checks),
     ``k_segment`` (split K into equal segments, each quantised and rescaled
-    on its own, fp32 results summed in order), ``engine``.
+    on its own, fp32 results summed in order), ``engine``, ``out_dtype``
+    (``torch.float32``, the default, or ``torch.bfloat16``: the fp32 result
+    with bias rounded to nearest even, as ``.to(torch.bfloat16)`` would).
+    bf16 operands are read as they are (widening to fp32 is exact); other
+    dtypes are converted to fp32.
 
     ``chunk_d > 0`` (bipolar, ``K > chunk_d``) runs the chunked form of the
     reference's chunk-D summation (``sc_integration/sc_attention.py:337-376``):
@@ -133,8 +138,12 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
         raise ValueError(f"config sc_prec={config['sc_prec']} != sc_prec={p}")
     dims = int(config["dims"])
     dev = a.device
-    a3 = a3.float().contiguous()
-    b3 = b3.float().contiguous()
+    def _operand(t):
+        if t.dtype not in (torch.float32, torch.bfloat16):
+            t = t.float()
+        return t.contiguous()
+    a3 = _operand(a3)
+    b3 = _operand(b3)
     if chunk_d and 0 < int(chunk_d) < K and mode == "bipolar":
         chunk_d = int(chunk_d)
         if dims < chunk_d:
@@ -159,11 +168,14 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
             raise ValueError(f"config has {dims} stream dims < K={K}; pass chunk_d")
         pool_dims = K
     if out is None:
-        out = torch.empty(BH, M, N, dtype=torch.float32, device=dev)
+        odt = torch.float32 if out_dtype is None else out_dtype
+        if odt not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"out_dtype must be float32 or bfloat16, got {odt}")
+        out = torch.empty(BH, M, N, dtype=odt, device=dev)
     else:
         out = out.view(BH, M, N)
-        if out.dtype != torch.float32 or not out.is_contiguous():
-            raise ValueError("out must be a contiguous float32 tensor")
+        if out.dtype not in (torch.float32, torch.bfloat16) or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 or bfloat16 tensor")
     if acc_out is not None:
         if acc_out.dtype != torch.int32 or acc_out.numel() != BH * M * N or not acc_out.is_contiguous():
             raise ValueError("acc_out must be a contiguous int32 tensor of BH*M*N elements")
@@ -201,6 +213,9 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     args.bias = _ptr(bias)
     args.out = out.data_ptr()
     args.acc_out = _ptr(acc_out)
+    args.io_flags = ((_lib.IO_A_BF16 if a3.dtype == torch.bfloat16 else 0)
+                     | (_lib.IO_B_BF16 if b3.dtype == torch.bfloat16 else 0)
+                     | (_lib.IO_OUT_BF16 if out.dtype == torch.bfloat16 else 0))
     lib = _lib.load()
     nbytes = lib.scmp_sc_matmul_workspace_size(ctypes.byref(args))
     if nbytes == 0:

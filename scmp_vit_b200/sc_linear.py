@@ -84,8 +84,13 @@ def _sc_linear(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int,
     rows.  Bias is added in the engine's epilogue (same fp32 add)."""
     orig_shape = x.shape
     D_in = orig_shape[-1]
-    x2 = x.reshape(-1, D_in).float()
-    w = weight.float()
+    # bf16 operands go to the engine as they are (widening is exact) and the
+    # engine writes bf16: fp32 result + fp32 bias, rounded to nearest even --
+    # the values of the fp32 path followed by .to(bfloat16)
+    bf16 = x.dtype == torch.bfloat16 and not USE_NOISE_MODEL
+    x2 = x.reshape(-1, D_in) if bf16 else x.reshape(-1, D_in).float()
+    w = weight if bf16 and weight.dtype == torch.bfloat16 else weight.float()
+    odt = torch.bfloat16 if bf16 else None
     if USE_NOISE_MODEL:
         y = noise_matmul.noisy_sc_matmul_grouped(x2, w, group_a=1, group_b=1, mode=mode,
                                                  sc_prec=sc_prec, stoc_len=stoc_len)
@@ -94,11 +99,11 @@ def _sc_linear(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int,
     elif chunk_d > 0 and mode == "bipolar" and D_in > chunk_d and cfg_override is None:
         y = sc_matmul(x2, w, granularity="per_row", mode=mode, sc_prec=sc_prec,
                       config=_get_config(chunk_d, sc_prec), group_a=1, group_b=1,
-                      chunk_d=chunk_d, stoc_len=stoc_len, bias=bias)
+                      chunk_d=chunk_d, stoc_len=stoc_len, bias=bias, out_dtype=odt)
     else:
         cfg = cfg_override if cfg_override is not None else _get_config(D_in, sc_prec)
         y = sc_matmul(x2, w, granularity="per_row", group_a=1, group_b=1, mode=mode,
-                      sc_prec=sc_prec, config=cfg, stoc_len=stoc_len, bias=bias)
+                      sc_prec=sc_prec, config=cfg, stoc_len=stoc_len, bias=bias, out_dtype=odt)
     return y.to(x.dtype).reshape(*orig_shape[:-1], w.shape[0])
 
 

@@ -67,6 +67,8 @@ def test_tc_single_tile(cuda_device):
     # CTA pairs (N > 128): the odd CTA's a rows / b rows partly or wholly past the end
     (300, 300, 64, 7, 128),
     (4096, 2560, 16, 7, 128),   # 80 pair tiles: clusters loop over several tiles
+    (280, 264, 64, 7, 128),     # 24-row tail in a padded tile, 8-column tail on the CUDA cores
+    (256, 128, 257, 7, 128),    # K = 257: codes padded to 264 for the row producers
 ])
 def test_tc_shapes(cuda_device, M, N, K, p, L):
     g = torch.Generator().manual_seed(M + N + K)
