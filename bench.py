@@ -179,13 +179,33 @@ def int8_tensor_peak(dev) -> float:
     return 2.0 * n ** 3 / best
 
 
-def roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops) -> dict:
+# DRAM bytes (read + write) of one qkv_proj pair-kernel launch per image, from
+# the ncu capture of 64 images (profiles/gemm_tc_pair_vit_l14_qkv_b64.md:
+# 292.2 MB + 145.9 MB); traffic grows with the a rows, i.e. per image.
+QKV_DRAM_BYTES_PER_IMAGE = (292.2e6 + 145.9e6) / 64
+
+
+def _tensor_peak_alt() -> dict:
+    """int8 denominator from the driver's measured bf16 GEMM rate (x2: the
+    tensor cores run int8 at twice the bf16 rate), or the recipe's fallback."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            bf16 = float(json.load(f)["bf16_tflops"])
+        return {"value": 2 * bf16, "source": "of measured: MEASURED_PEAKS.json bf16_tflops x2"}
+    except (OSError, KeyError, ValueError, TypeError):
+        return {"value": 2 * 1590.0, "source": "of fallback: 1.59 PFLOP/s bf16 x2"}
+
+
+def roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops, images=None) -> dict:
     """Roofline of the dominant kernel (the qkv_proj SC matmul).  One SC
     bit-product = one int8 multiply-add on the tensor-core engine (2 ops) and
     one counted AND bit on the CUDA-core engine."""
     base = {"kernel": "sc_matmul qkv_proj", "per_launch_ms": qkv_ms,
             "algorithmic_per_launch": qkv_bitops, "algorithmic_unit": "bit-products",
-            "traffic": None,
+            "traffic": (QKV_DRAM_BYTES_PER_IMAGE * images) if (images and on_tc) else None,
+            "traffic_source": "ncu dram__bytes_read+write of the pair kernel at 64 images, "
+                              "scaled per image",
             "int_pipe_peak_tbitops": peak_popc / 1e12,
             "x_int_pipe_roofline": (achieved / peak_popc) if achieved else None}
     if on_tc:
@@ -194,6 +214,10 @@ def roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops) -> dict:
                      "peak": peak_i8 / 1e12, "unit": "TOP/s (int8)",
                      "frac": (2 * achieved / peak_i8) if achieved else None,
                      "peak_source": "measured cuBLAS int8 GEMM 8192^3 (torch._int_mm), best of 10"})
+        alt = _tensor_peak_alt()
+        if achieved:
+            alt["frac"] = 2 * achieved / 1e12 / alt["value"]
+        base["peak_alt_tops"] = alt
     else:
         base.update({"bound": "int", "engine": "CUDA-core LOP3+POPC",
                      "achieved": achieved / 1e12 if achieved else None,
@@ -444,7 +468,8 @@ def main():
                              "activations per step)"},
             "e2e": e2e,
             "gpu_launches": int(launches),
-            "roofline": roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops),
+            "roofline": roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops,
+                                 images=bl),
             "ms_per_step_split": split,
             "cpu_baseline": cpu,
             "clocks": clk,
