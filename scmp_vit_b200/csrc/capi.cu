@@ -316,8 +316,9 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
     n_tc = tc_rows(x.N, tc_tile_n(P, x.N));
     if (tc_row_producers(P)) {
       const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
-      if ((e = launch_pool_complement(x.pool, x.pool_dims, plan.pool_comp_rows, x.sc_prec, shift,
-                                      ws + plan.pool_comp, s)) != cudaSuccess)
+      if ((e = launch_pool_complement(x.pool, x.pool_dims, plan.pool_comp_rows, x.sc_prec,
+                                      tc_stream_log2(P), shift, ws + plan.pool_comp, s)) !=
+          cudaSuccess)
         return cuda_fail(e, "pool_complement launch");
       count_launches(1);
     }

@@ -46,10 +46,12 @@ struct TcCfg {
   static constexpr uint32_t kStage = kStageA + kStageB;
   static constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 128 (x2 when segmented)
   static constexpr uint32_t kTherm = 2 * 129 * 128;  // enable-window rows (table path)
+  // ring depth: 3 x 64 KB for BN = 256, 4 stages for the narrower tiles
+  static constexpr int kNS = BN == 256 ? kStages : 4;
   // Dynamic shared memory; kernels without the table leave those 33 KB to L1
   // (at most 196 KB of shared memory keeps a ~60 KB L1 for the pool rows).
   static constexpr size_t smem_bytes(bool table) {
-    return (size_t)kStages * kStage + (table ? kTherm : 0) + 1024 /*align*/ + 256;
+    return (size_t)kNS * kStage + (table ? kTherm : 0) + 1024 /*align*/ + 256;
   }
 };
 
@@ -314,6 +316,17 @@ __device__ __forceinline__ bool acquire_stage(const Bars &b, const ProdState &st
   const bool ok = mbar_wait(&b.empty[st.stage], st.phase ^ 1, b.abort);
   return __all_sync(0xffffffffu, ok);
 }
+// Stage s known at compile time (row producers whose macro step is a whole
+// number of ring turns).
+__device__ __forceinline__ bool acquire_at(const Bars &b, int s, uint32_t phase) {
+  const bool ok = mbar_wait(&b.empty[s], phase ^ 1, b.abort);
+  return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ void publish_at(const Bars &b, int s, int lane) {
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&b.full[s]);
+}
 __device__ __forceinline__ void prefetch_l1(const void *p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
@@ -552,7 +565,7 @@ __device__ bool produce_chunks(const TcParams &prm, const Bars &b, ProdState &st
                    prmt(u * 0x01010101u + rb2, 0u, 0xBA98u) & sm,
                    prmt(u * 0x01010101u + rb3, 0u, 0xBA98u) & sm);
     }
-    publish_stage(b, st, lane);
+    publish_stage<Cfg::kNS>(b, st, lane);
     if constexpr (kSeg) {
       if ((kb + 1) % prm.nkb_seg == 0 && kb + 1 < prm.nkb) {
         // ---- end of a non-final segment
@@ -612,7 +625,7 @@ __device__ __forceinline__ int code_of_rt(const uint4 &v, int j, uint32_t sh) {
 
 // BN = b rows this CTA generates (starting at n0); CTA pairs (kPair) run NS
 // stages.
-template <int BN, int LG, bool kSeg, int NS = kStages, bool kPair = false>
+template <int BN, int LG, bool kSeg, int NS, bool kPair = false>
 __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, uint32_t smem_s,
                              uint32_t tmem_base, int warp, int lane, int64_t slice,
                              int64_t slice_b, int64_t m0, int64_t n0) {
@@ -622,6 +635,11 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
   const GemmProblem &P = prm.P;
   constexpr int NBC = BN / 64;          // b chunks per thread
   constexpr int G = (1 << LG) / 16;     // k-blocks per macro step (8 reduction indices)
+  constexpr int LPB = 1 << LG;          // pool complement row stride (bytes)
+  // a macro step that is a whole number of ring turns starts at stage 0:
+  // stage and phase of each k-block are then known at compile time
+  constexpr bool kStatic = (G % NS) == 0;
+  constexpr uint32_t kStageBytes = Cfg::kStage;
   const int pt = threadIdx.x - 32;
   const int ra = pt & 255;              // a row of the tile
   const int hA = pt >> 8;               // a chunks 4 hA .. 4 hA + 3
@@ -660,12 +678,22 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
   const int shift = prm.shift_pool;
   const int nmacro = (int)(P.ldk >> 3);  // zero-padded indices past K add nothing
   const int msteps_seg = kSeg ? prm.kseg >> 3 : 0;  // macro steps per segment
-  const uint8_t *pcomp = P.pool_comp + t0B;
-  // pool rows one segment (or the whole K) spans; prefetches wrap inside it
+  // Pool complement rows are LPB bytes apart (the table is laid out with the
+  // padded stream length as row stride), so k-block j of a macro step reads
+  // its b chunks at pcm + 128 j for every Lp: Lp = 128 one row per k-block,
+  // Lp = 256 half a row, Lp = 64 the row 2 j + (cB0 >> 2).
+  const uint8_t *pc_thr = P.pool_comp + t0B + (LG == 6 ? 64 * (cB0 >> 2) : 0);
+  // pool rows one segment (or the whole K) spans
   const int prow_lim = kSeg ? prm.kseg : (int)P.ldk;
+  // the 8 rows (G lines of 128 B) of a macro step are pulled into L1 one
+  // macro step ahead, one line per lane
+  auto prefetch_macro = [&](int prow) {
+    if (lane < G && prow < prow_lim) prefetch_l1(P.pool_comp + (size_t)prow * LPB + 128 * lane);
+  };
   int pbase = 0;  // pool row of the macro step's first reduction index
   int mseg = 0;   // macro steps done in the current segment
   uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
+  prefetch_macro(0);
 #pragma unroll 1
   for (int mc = 0; mc < nmacro; ++mc) {
     const uint4 ca = ca_n, cb = cb_n;
@@ -673,19 +701,12 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
       ca_n = ld_stream_v4(pa + mc + 1);
       cb_n = ld_stream_v4(pb + mc + 1);
     }
+    prefetch_macro((kSeg && mseg + 1 == msteps_seg) ? 0 : pbase + 8);
+    const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
-      // ---- b: pool complement bytes of this k-block's b chunks; the row two
-      // k-blocks ahead is pulled into L1 now (each k-block starts a new row,
-      // and an L2 round trip per k-block would stall every producer)
-      const int dB = LG == 8 ? (j >> 1) : (LG == 7 ? j : 2 * j + (cB0 >> 2));
-      const uint8_t *pc = pcomp + ((size_t)(pbase + dB) << prec) + (LG == 8 ? 128 * (j & 1) : 0);
-      {
-        const int dB2 = LG == 8 ? ((j + 2) >> 1) : (LG == 7 ? j + 2 : 2 * (j + 2) + (cB0 >> 2));
-        int pr2 = pbase + dB2;
-        if (pr2 >= prow_lim) pr2 -= prow_lim;
-        prefetch_l1(pcomp + ((size_t)pr2 << prec) + (LG == 8 ? 128 * (j & 1) : 0));
-      }
+      // ---- b: pool complement bytes of this k-block's b chunks
+      const uint8_t *pc = pcm + 128 * j;
       uint4 pcw[NBC];
 #pragma unroll
       for (int i = 0; i < NBC; ++i) pcw[i] = __ldg(reinterpret_cast<const uint4 *>(pc) + i);
@@ -698,13 +719,19 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
       const int codeB = LG == 6 ? code_of_rt(cb, j, shB) : code_of(cb, LG == 8 ? (j >> 1) : j);
       const uint32_t u = (uint32_t)(abs(codeB) >> shift);
       const uint32_t smB = (uint32_t)(codeB >> 31) | 0x01010101u;
-      if (!acquire_stage(b, st, lane)) return false;
-      const uint32_t stg = (uint32_t)st.stage;
+      uint32_t soff;  // byte offset of this k-block's stage
+      if constexpr (kStatic) {
+        if (!acquire_at(b, j % NS, st.phase ^ (uint32_t)((j / NS) & 1))) return false;
+        soff = (uint32_t)(j % NS) * kStageBytes;
+      } else {
+        if (!acquire_stage(b, st, lane)) return false;
+        soff = mad_u32((uint32_t)st.stage, stage_bytes, 0u);
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         // chunk 4 hA + i starts at t0A + 16 i: k - t0 = kbase - 16 i
         const uint32_t kc = kbase - 16u * (uint32_t)i;
-        st_shared_v4(mad_u32(stg, stage_bytes, sA[i]),
+        st_shared_v4(sA[i] + soff,
                      prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x03020100u), 0u, 0xBA98u) & smA,
                      prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x07060504u), 0u, 0xBA98u) & smA,
                      prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x0B0A0908u), 0u, 0xBA98u) & smA,
@@ -712,13 +739,19 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
       }
 #pragma unroll
       for (int i = 0; i < NBC; ++i) {
-        st_shared_v4(mad_u32(stg, stage_bytes, sB[i]),
+        st_shared_v4(sB[i] + soff,
                      prmt(mad_u32(u, rep, pcw[i].x), 0u, 0xBA98u) & smB,
                      prmt(mad_u32(u, rep, pcw[i].y), 0u, 0xBA98u) & smB,
                      prmt(mad_u32(u, rep, pcw[i].z), 0u, 0xBA98u) & smB,
                      prmt(mad_u32(u, rep, pcw[i].w), 0u, 0xBA98u) & smB);
       }
-      publish_stage<NS>(b, st, lane);
+      if constexpr (kStatic)
+        publish_at(b, j % NS, lane);
+      else
+        publish_stage<NS>(b, st, lane);
+    }
+    if constexpr (kStatic) {
+      if ((G / NS) & 1) st.phase ^= 1u;  // st.stage stays 0
     }
     pbase += 8;
     if constexpr (kSeg) {
@@ -856,11 +889,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char *therm_s = smem + kStages * Cfg::kStage;  // [sign][window 0..128][128 B]
+  unsigned char *therm_s = smem + Cfg::kNS * Cfg::kStage;  // [sign][window 0..128][128 B]
   Bars b;
   b.full = reinterpret_cast<uint64_t *>(therm_s + (kProd == kProdTable ? Cfg::kTherm : 0));
-  b.empty = b.full + kStages;
-  b.tfull = b.empty + kStages;
+  b.empty = b.full + Cfg::kNS;
+  b.tfull = b.empty + Cfg::kNS;
   b.tempty = b.tfull + 1;
   b.drain = b.tempty + 1;
   b.epi = b.drain + 1;
@@ -871,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < Cfg::kNS; ++s) {
       mbar_init(&b.full[s], kProducerWarps);
       mbar_init(&b.empty[s], 1);
     }
@@ -928,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
               }
             }
             tc_commit(&b.empty[stage]);
-            if (++stage == kStages) { stage = 0; phase ^= 1; }
+            if (++stage == Cfg::kNS) { stage = 0; phase ^= 1; }
           }
           if (!ok) break;
           tc_commit(b.tfull);
@@ -953,7 +986,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
       bool ok;
       if constexpr (kProd == kProdRows)
-        ok = produce_rows<BN, LG, kSeg>(prm, b, st, smem_s, tmem_base, warp, lane, slice, slice_b,
+        ok = produce_rows<BN, LG, kSeg, Cfg::kNS>(prm, b, st, smem_s, tmem_base, warp, lane, slice,
+                                                  slice_b,
                                         m0, n0);
       else
         ok = produce_chunks<BN, kProd == kProdTable, kSeg>(prm, b, st, smem_s, therm_u, tmem_base,
@@ -987,6 +1021,7 @@ constexpr int kPairStages = 4;
 constexpr uint32_t kPairStageA = kBM * kKB;          // 32 KB: 256 a rows
 constexpr uint32_t kPairStageB = 128 * kKB;          // 16 KB: this CTA's 128 b rows
 constexpr uint32_t kPairStage = kPairStageA + kPairStageB;
+static_assert(kPairStage == TcCfg<128>::kStage, "pair producers use the BN = 128 stage layout");
 constexpr size_t kPairSmem = (size_t)kPairStages * kPairStage + 1024 /*align*/ + 256;
 
 // Instruction descriptor for the pair MMA: s8 x s8 -> s32, K-major, M = 256, N = 256.
@@ -1240,6 +1275,8 @@ bool tc_supported(const GemmProblem &P) {
   if (P.pool_dims < P.kseg || P.acc_out) return false;
   return ((P.kseg << padded_stream_log2(P)) % kKB) == 0;
 }
+
+int tc_stream_log2(const GemmProblem &P) { return padded_stream_log2(P); }
 
 bool tc_row_producers(const GemmProblem &P) {
   const int lg = padded_stream_log2(P);

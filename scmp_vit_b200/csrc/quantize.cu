@@ -230,13 +230,20 @@ __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_d
 // PC[d][t] = 0x7F - (R[d][t] >> shift).  The tensor-core engine forms the
 // stream byte 0x7F + u - (R >> shift) for a threshold u < 128: its top bit is
 // [R >> shift < u], with no borrow into the neighbouring byte.
-// Rows past the pool (reduction indices of zero padding) hold 0x7F: with a
-// zero threshold they produce no stream bits.
-__global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int64_t pool_bytes,
-                                       int64_t bytes, int shift, uint8_t *__restrict__ out) {
+// Written with row stride Lp = 2^lp_log2 <= 2^prec (the padded stream
+// length; positions t >= Lp are never read).  Rows past the pool (reduction
+// indices of zero padding) hold 0x7F: with a zero threshold they produce no
+// stream bits.
+__global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int pool_dims,
+                                       int64_t rows, int prec, int lp_log2, int shift,
+                                       uint8_t *__restrict__ out) {
+  const int64_t bytes = rows << lp_log2;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes;
-       i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = i < pool_bytes ? (uint8_t)(0x7F - (pool[i] >> shift)) : (uint8_t)0x7F;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t d = i >> lp_log2;
+    const int64_t t = i & ((1 << lp_log2) - 1);
+    out[i] = d < pool_dims ? (uint8_t)(0x7F - (pool[(d << prec) + t] >> shift)) : (uint8_t)0x7F;
+  }
 }
 
 }  // namespace
@@ -298,12 +305,12 @@ cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, ui
 }
 
 cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t rows, int prec,
-                                   int shift, uint8_t *out, cudaStream_t s) {
-  const int64_t pool_bytes = (int64_t)pool_dims << prec;
-  const int64_t bytes = (rows > pool_dims ? rows : (int64_t)pool_dims) << prec;
+                                   int lp_log2, int shift, uint8_t *out, cudaStream_t s) {
+  if (rows < pool_dims) rows = pool_dims;
+  const int64_t bytes = rows << lp_log2;
   const int64_t blocks = (bytes + 255) / 256;
   pool_complement_kernel<<<(unsigned)(blocks < 296 ? blocks : 296), 256, 0, s>>>(
-      pool, pool_bytes, bytes, shift, out);
+      pool, pool_dims, rows, prec, lp_log2, shift, out);
   return cudaGetLastError();
 }
 

@@ -105,15 +105,18 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
                             cudaStream_t s);
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
-// PC over max(pool_dims, rows) rows (rows past the pool hold 0x7F)
+// PC over max(pool_dims, rows) rows of 2^lp_log2 bytes (rows past the pool
+// hold 0x7F)
 cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t rows, int prec,
-                                   int shift, uint8_t *out, cudaStream_t s);
+                                   int lp_log2, int shift, uint8_t *out, cudaStream_t s);
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 bool tc_supported(const GemmProblem &P);
 int tc_block_n(int64_t N);
 int tc_tile_n(const GemmProblem &P, int64_t N);
 // true when the row-producer kernel runs this problem (it reads P.pool_comp)
 bool tc_row_producers(const GemmProblem &P);
+// log2 of the padded stream length Lp the tensor-core engine uses
+int tc_stream_log2(const GemmProblem &P);
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
                            unsigned int *error, cudaStream_t s);
 
