@@ -217,8 +217,69 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
   }
 }
 
+// Thin windows with a short reduction (K <= 512, e.g. the 257th row / column
+// of Q@K^T and Attn@V): one thread per output walks all K indices, so no
+// lanes idle on a short K and the rescale runs on every lane.  Consecutive
+// threads take consecutive columns of a row (the a codes are shared).
+template <int LW>
+__global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P) {
+  const int64_t wm = P.m_hi - P.m_lo, wn = P.n_hi - P.n_lo;
+  const int64_t total = P.batch * wm * wn;
+  const int T = 1 << P.prec;
+  const int WT = T >= 32 ? T / 32 : 1;
+  const int pd = P.pool_dims;
+  const int K = (int)P.K;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t slice = o / (wm * wn);
+    const int64_t r = o % (wm * wn);
+    const int64_t gm = P.m_lo + r / wn, gn = P.n_lo + r % wn;
+    const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
+    const int64_t grow = slice * P.M + gm, brow = slice_b * P.N + gn;
+    const int L = row_stream_len(P, slice, grow);
+    if (L < 0) continue;
+    int acc = 0;
+    if (L > 0) {
+      const int16_t *ca = P.qa.code + grow * P.ldk;
+      const int16_t *cb = P.qb.code + brow * P.ldk;
+      int dm = 0;  // d mod pool_dims
+      for (int d = 0; d < K; ++d) {
+        const int a = ca[d], b = cb[d];
+        const int k = ((a < 0 ? -a : a) * L) >> P.prec;
+        const uint32_t *st = P.stream_table + ((int64_t)dm * (T + 1) + (b < 0 ? -b : b)) * WT;
+        if (++dm == pd) dm = 0;
+        int cnt = 0;
+#pragma unroll
+        for (int w = 0; w < LW; ++w) {
+          const int lo = 32 * w;
+          const uint32_t win = k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
+          cnt += __popc(win & __ldg(st + w));
+        }
+        acc += ((a < 0) != (b < 0) ? -cnt : cnt);
+      }
+    }
+    float y = 0.0f;
+    if (L > 0)
+      y = sc_rescale(P.mode, P.prec, L, acc, P.K, P.qa.scale[grow], P.qa.zero[grow],
+                     P.qa.rowsum[grow], P.qb.scale[brow], P.qb.zero[brow], P.qb.rowsum[brow]);
+    if (P.bias) y = __fadd_rn(y, P.bias[gn]);
+    store_out(P, grow * P.N + gn, y);
+    if (P.acc_out) P.acc_out[grow * P.N + gn] = L > 0 ? acc : 0;
+  }
+}
+
+template <int LW>
+cudaError_t launch_thin_lane(const GemmProblem &P, cudaStream_t s) {
+  const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  gemm_popc_thin_lane_kernel<LW><<<(unsigned)blocks, 256, 0, s>>>(P);
+  return cudaGetLastError();
+}
+
 template <int LW>
 cudaError_t launch_thin(const GemmProblem &P, cudaStream_t s) {
+  if (P.K <= 512) return launch_thin_lane<LW>(P, s);
   const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
   int64_t blocks = (total + 7) / 8;  // 8 warps per block, one output per warp
   if (blocks > 148 * 32) blocks = 148 * 32;

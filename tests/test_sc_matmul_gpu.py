@@ -177,12 +177,13 @@ def test_slice_stream_lengths(cuda_device):
         np.testing.assert_allclose(y[s].cpu().numpy(), y_ref[0], rtol=RTOL, atol=1e-30)
 
 
-@pytest.mark.parametrize("M,N", [(257, 16), (16, 300), (3, 257)])
-def test_thin_windows_on_cuda_cores(cuda_device, M, N):
+@pytest.mark.parametrize("M,N,K", [(257, 16, 96), (16, 300, 96), (3, 257, 96),
+                                   (5, 40, 600)])  # K > 512: one warp per output
+def test_thin_windows_on_cuda_cores(cuda_device, M, N, K):
     g = torch.Generator().manual_seed(M + N)
-    a = torch.randn(2, M, 96, generator=g)
-    b = torch.randn(2, N, 96, generator=g)
-    _run(cuda_device, a, b, _cfg("sobol", 96, 7), sc_prec=7, stoc_len=128, engine="popc")
+    a = torch.randn(2, M, K, generator=g)
+    b = torch.randn(2, N, K, generator=g)
+    _run(cuda_device, a, b, _cfg("sobol", K, 7), sc_prec=7, stoc_len=128, engine="popc")
 
 
 def test_qkv_shape_full_size(cuda_device):
