@@ -308,6 +308,10 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        # stdout carries exactly one JSON line: keep NCCL's version banner off it
+        # unless verbose NCCL logging was asked for
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
 
     from scmp_vit_b200 import _lib
