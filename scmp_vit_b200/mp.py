@@ -398,3 +398,12 @@ class MetricProfiler:
     @classmethod
     def reset(cls) -> None:
         cls._data.clear()
+
+
+def __getattr__(name):
+    # ``from scmp_kernels.mp import RidgeFitter`` (sc_integration/mp_search.py:49):
+    # the ridge solve lives with the QwT compensation code
+    if name == "RidgeFitter":
+        from .qwt import RidgeFitter
+        return RidgeFitter
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
