@@ -58,7 +58,8 @@ enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
 enum scmp_io_flags {
   SCMP_IO_A_BF16 = 1,   /* a is bf16: widened exactly to fp32 before quantisation */
   SCMP_IO_B_BF16 = 2,   /* b is bf16 */
-  SCMP_IO_OUT_BF16 = 4  /* out is bf16: the fp32 result (bias included) rounded to nearest even */
+  SCMP_IO_OUT_BF16 = 4, /* out is bf16: the fp32 result (bias included) rounded to nearest even */
+  SCMP_IO_B_PACKED = 8  /* b is a buffer written by scmp_prepack_b for the same b arguments */
 };
 enum scmp_engine {
   SCMP_ENGINE_AUTO = 0,
@@ -130,6 +131,23 @@ SCMP_API int scmp_sc_matmul(const scmp_matmul_args *args, void *stream);
  * first call on each device looks up the array's address with that device
  * current; make it before any stream capture begins. */
 SCMP_API int scmp_sc_matmul_noalloc(const scmp_matmul_args *args, void *stream);
+
+/* Prepacked weights (no reference counterpart: the reference regenerates a
+ * weight's stochastic streams in every call).  A weight b that stays fixed
+ * across calls (batch_b = 1, no k_segment, 5 <= sc_prec <= 8, not unipolar
+ * p = 8, pool_dims >= K) can be quantised and expanded into its tensor-core
+ * operand bytes once; later calls pass the packed buffer as `b` with
+ * SCMP_IO_B_PACKED and identical N, K, mode, granularity, group_b, sc_prec
+ * and pool, and the engine loads those bytes with TMA instead of generating
+ * them.  Results are bit-identical to passing b itself.  The buffer holds the
+ * int16 codes, per-row scales and the bytes [N][ceil8(K) * 2^p] (about
+ * N * K * 2^p bytes: 403 MB for a 3072 x 1024 weight at p = 7).
+ * scmp_prepack_b_size returns its size (0 on invalid arguments; a, M and
+ * the stream lengths are ignored); scmp_prepack_b writes it asynchronously on
+ * `stream` (b fp32 or bf16 per io_flags). */
+SCMP_API size_t scmp_prepack_b_size(const scmp_matmul_args *args);
+SCMP_API int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_bytes,
+                            void *stream);
 
 /* Message of the last failure on this thread ("" if none). */
 SCMP_API const char *scmp_last_error(void);

@@ -22,7 +22,7 @@ STATUS_NAMES = {
 GRANULARITY = {"per_row": 0, "per_head": 1, "per_tensor": 2}
 MODE = {"bipolar": 0, "unipolar": 1}
 ENGINE = {"auto": 0, "popc": 1, "tcgen05": 2}
-IO_A_BF16, IO_B_BF16, IO_OUT_BF16 = 1, 2, 4  # scmp_matmul_args.io_flags bits
+IO_A_BF16, IO_B_BF16, IO_OUT_BF16, IO_B_PACKED = 1, 2, 4, 8  # scmp_matmul_args.io_flags bits
 
 EXPORTED_SYMBOLS = (
     "scmp_sc_matmul_workspace_size",
@@ -100,6 +100,11 @@ def load() -> ctypes.CDLL:
         lib.scmp_sc_matmul.restype = ctypes.c_int
         lib.scmp_sc_matmul_noalloc.argtypes = [ctypes.POINTER(MatmulArgs), ctypes.c_void_p]
         lib.scmp_sc_matmul_noalloc.restype = ctypes.c_int
+        lib.scmp_prepack_b_size.argtypes = [ctypes.POINTER(MatmulArgs)]
+        lib.scmp_prepack_b_size.restype = ctypes.c_size_t
+        lib.scmp_prepack_b.argtypes = [ctypes.POINTER(MatmulArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                       ctypes.c_void_p]
+        lib.scmp_prepack_b.restype = ctypes.c_int
         lib.scmp_last_error.argtypes = []
         lib.scmp_last_error.restype = ctypes.c_char_p
         lib.scmp_abi_version.argtypes = []

@@ -150,7 +150,7 @@ int validate(const scmp_matmul_args *x) {
         (x->granularity != SCMP_PER_ROW || x->group_a != 1 || x->group_b != 1))
       return fail(SCMP_EINVAL, "k_segment needs granularity per_row with group_a=group_b=1");
   }
-  if (x->io_flags & ~(SCMP_IO_A_BF16 | SCMP_IO_B_BF16 | SCMP_IO_OUT_BF16))
+  if (x->io_flags & ~(SCMP_IO_A_BF16 | SCMP_IO_B_BF16 | SCMP_IO_OUT_BF16 | SCMP_IO_B_PACKED))
     return fail(SCMP_EINVAL, "unknown io_flags bits 0x%x", (unsigned)x->io_flags);
   if (x->engine != SCMP_ENGINE_AUTO && x->engine != SCMP_ENGINE_POPC &&
       x->engine != SCMP_ENGINE_TCGEN05)
@@ -159,6 +159,44 @@ int validate(const scmp_matmul_args *x) {
 }
 
 int64_t seg_len(const scmp_matmul_args *x) { return x->k_segment > 0 ? x->k_segment : x->K; }
+
+// A weight that can be prepacked: one b slice, one K segment, a pool row per
+// reduction index, and 8-bit thresholds that fit the byte compare.
+int check_packable(const scmp_matmul_args *x) {
+  if (x->batch_b != 1) return fail(SCMP_EINVAL, "prepacked b needs batch_b = 1");
+  if (x->k_segment != 0 && x->k_segment != x->K)
+    return fail(SCMP_EINVAL, "prepacked b needs k_segment = 0");
+  if (x->sc_prec < 5 || (x->mode == SCMP_UNIPOLAR && x->sc_prec == 8))
+    return fail(SCMP_EUNSUPPORTED, "prepacked b needs 5 <= sc_prec <= 8 (not unipolar p = 8)");
+  if (x->pool_dims < x->K) return fail(SCMP_EINVAL, "prepacked b needs pool_dims >= K");
+  const int64_t ldk = (x->K + 7) / 8 * 8;
+  if ((ldk << x->sc_prec) >= ((int64_t)1 << 31))
+    return fail(SCMP_EUNSUPPORTED, "prepacked b rows of %lld bytes are too long",
+                (long long)(ldk << x->sc_prec));
+  return SCMP_OK;
+}
+
+// Layout of a prepacked b buffer (offsets from its base): the b operand
+// (group stats, int16 codes [N][ldk], per-row scale / zero / row sum), the
+// pool complement at row stride 2^p, and the operand bytes [N][ldk * 2^p].
+struct PackPlan {
+  OperandLayout B;
+  size_t pool_comp = 0, streams = 0, total = 0;
+  int64_t ldk = 0, pool_rows = 0;
+};
+
+PackPlan make_pack_plan(const scmp_matmul_args *x) {
+  PackPlan p;
+  Carver c;
+  p.ldk = (x->K + 7) / 8 * 8;
+  p.B.g = make_groups(x->granularity, 1, x->N, x->group_b);
+  layout_operand(c, p.B, x->K, p.ldk);
+  p.pool_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
+  p.pool_comp = c.take((size_t)p.pool_rows << x->sc_prec);
+  p.streams = c.take((size_t)x->N * (size_t)(p.ldk << x->sc_prec));
+  p.total = c.off;
+  return p;
+}
 
 Plan make_plan(const scmp_matmul_args *x) {
   Plan p;
@@ -239,6 +277,46 @@ int scmp_engine_status(int reset, unsigned int *flags) {
   return SCMP_OK;
 }
 
+size_t scmp_prepack_b_size(const scmp_matmul_args *args) {
+  if (validate(args) != SCMP_OK || check_packable(args) != SCMP_OK) return 0;
+  if (args->N == 0) return kAlign;
+  return make_pack_plan(args).total;
+}
+
+int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_bytes,
+                   void *stream) {
+  g_last_error.clear();
+  int rc = validate(args);
+  if (rc != SCMP_OK) return rc;
+  if ((rc = check_packable(args)) != SCMP_OK) return rc;
+  const scmp_matmul_args &x = *args;
+  if (x.io_flags & SCMP_IO_B_PACKED) return fail(SCMP_EINVAL, "b is already packed");
+  if (x.N == 0) return SCMP_OK;
+  if (!x.b || !x.pool || !packed) return fail(SCMP_EINVAL, "b, pool and packed must be non-NULL");
+  const PackPlan pk = make_pack_plan(&x);
+  if (packed_bytes < pk.total)
+    return fail(SCMP_EWORKSPACE, "packed buffer needs %zu bytes, got %zu", pk.total,
+                packed_bytes);
+  if ((reinterpret_cast<uintptr_t>(packed) & (kAlign - 1)) != 0)
+    return fail(SCMP_EINVAL, "packed buffer must be %zu-byte aligned", kAlign);
+  auto *pb = static_cast<unsigned char *>(packed);
+  auto s = static_cast<cudaStream_t>(stream);
+  if ((rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, pk.B, x.K, x.mode,
+                             x.sc_prec, pb, s)) != SCMP_OK)
+    return rc;
+  const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
+  cudaError_t e;
+  if ((e = launch_pool_complement(x.pool, x.pool_dims, pk.pool_rows, x.sc_prec, x.sc_prec, shift,
+                                  pb + pk.pool_comp, s)) != cudaSuccess)
+    return cuda_fail(e, "pool_complement launch");
+  if ((e = launch_pack_b_streams(reinterpret_cast<const int16_t *>(pb + pk.B.code), x.N, pk.ldk,
+                                 x.sc_prec, shift, pb + pk.pool_comp, pb + pk.streams, s)) !=
+      cudaSuccess)
+    return cuda_fail(e, "pack_b_streams launch");
+  count_launches(2);
+  return SCMP_OK;
+}
+
 size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args) {
   if (validate(args) != SCMP_OK) return 0;
   if (args->batch == 0 || args->M == 0 || args->N == 0) return kAlign;
@@ -261,18 +339,28 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   auto s = static_cast<cudaStream_t>(stream);
 
   const int64_t kseg = seg_len(&x);
+  const bool packed = (x.io_flags & SCMP_IO_B_PACKED) != 0;
+  if (packed && (rc = check_packable(&x)) != SCMP_OK) return rc;
   if ((rc = quantize_operand(x.a, (x.io_flags & SCMP_IO_A_BF16) != 0, plan.A, kseg, x.mode,
                              x.sc_prec, ws, s)) != SCMP_OK)
     return rc;
-  if ((rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, plan.B, kseg, x.mode,
-                             x.sc_prec, ws, s)) != SCMP_OK)
+  if (!packed && (rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, plan.B, kseg,
+                                        x.mode, x.sc_prec, ws, s)) != SCMP_OK)
     return rc;
   auto *table = reinterpret_cast<uint32_t *>(ws + plan.table);
   cudaError_t e;
 
   GemmProblem P{};
   P.qa = plane_of(plan.A, ws);
-  P.qb = plane_of(plan.B, ws);
+  if (packed) {
+    // b's codes, scales and operand bytes were written by scmp_prepack_b
+    const PackPlan pk = make_pack_plan(&x);
+    auto *pb = static_cast<unsigned char *>(const_cast<void *>(x.b));
+    P.qb = plane_of(pk.B, pb);
+    P.b_streams = pb + pk.streams;
+  } else {
+    P.qb = plane_of(plan.B, ws);
+  }
   P.batch = x.batch;
   P.batch_b = x.batch_b;
   P.M = x.M;

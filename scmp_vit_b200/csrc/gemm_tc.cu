@@ -21,8 +21,11 @@
 // of the tile, codes arrive 8 reduction indices per 16-byte load; K % 8 == 0
 // and Lp >= 64) and chunk producers (a thread owns one 16-byte chunk column of
 // several rows; every other supported shape).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -206,6 +209,21 @@ __device__ __forceinline__ void tc_commit_pair_local(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
                : "memory");
+}
+// ---- TMA (prepacked b): a plain 2-D tiled load into this CTA's shared
+// memory, completing bytes on an mbarrier (no multicast).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -625,7 +643,12 @@ __device__ __forceinline__ int code_of_rt(const uint4 &v, int j, uint32_t sh) {
 
 // BN = b rows this CTA generates (starting at n0); CTA pairs (kPair) run NS
 // stages.
-template <int BN, int LG, bool kSeg, int NS, bool kPair = false>
+// kNoB: b arrives by TMA from a prepacked buffer; only the a rows are generated.
+// kSparseA: a warp stores zeros without arithmetic for a chunk that lies past
+// every window of its 32 rows (short windows dominate in Attn@V, whose a rows
+// are softmax probabilities); exact, since such bytes are zero anyway.
+template <int BN, int LG, bool kSeg, int NS, bool kPair = false, bool kNoB = false,
+          bool kSparseA = false>
 __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, uint32_t smem_s,
                              uint32_t tmem_base, int warp, int lane, int64_t slice,
                              int64_t slice_b, int64_t m0, int64_t n0) {
@@ -692,16 +715,19 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
   };
   int pbase = 0;  // pool row of the macro step's first reduction index
   int mseg = 0;   // macro steps done in the current segment
-  uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
-  prefetch_macro(0);
+  uint4 ca_n = ld_stream_v4(pa), cb_n = make_uint4(0, 0, 0, 0);
+  if constexpr (!kNoB) {
+    cb_n = ld_stream_v4(pb);
+    prefetch_macro(0);
+  }
 #pragma unroll 1
   for (int mc = 0; mc < nmacro; ++mc) {
     const uint4 ca = ca_n, cb = cb_n;
     if (mc + 1 < nmacro) {
       ca_n = ld_stream_v4(pa + mc + 1);
-      cb_n = ld_stream_v4(pb + mc + 1);
+      if constexpr (!kNoB) cb_n = ld_stream_v4(pb + mc + 1);
     }
-    prefetch_macro((kSeg && mseg + 1 == msteps_seg) ? 0 : pbase + 8);
+    if constexpr (!kNoB) prefetch_macro((kSeg && mseg + 1 == msteps_seg) ? 0 : pbase + 8);
     const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
@@ -709,7 +735,8 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
       const uint8_t *pc = pcm + 128 * j;
       uint4 pcw[NBC];
 #pragma unroll
-      for (int i = 0; i < NBC; ++i) pcw[i] = __ldg(reinterpret_cast<const uint4 *>(pc) + i);
+      for (int i = 0; i < NBC; ++i)
+        pcw[i] = kNoB ? make_uint4(0, 0, 0, 0) : __ldg(reinterpret_cast<const uint4 *>(pc) + i);
       // ---- a: window length of this k-block's reduction index
       const int codeA = LG == 6 ? code_of_rt(ca, j, shA) : code_of(ca, LG == 8 ? (j >> 1) : j);
       int k = (abs(codeA) * Lg) >> prec;
@@ -727,10 +754,16 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
         if (!acquire_stage(b, st, lane)) return false;
         soff = mad_u32((uint32_t)st.stage, stage_bytes, 0u);
       }
+      // largest k - t0A over the warp's rows (the warp shares hA, so t0A)
+      const int kbmax = kSparseA ? __reduce_max_sync(0xffffffffu, (int)kbase) : 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         // chunk 4 hA + i starts at t0A + 16 i: k - t0 = kbase - 16 i
         const uint32_t kc = kbase - 16u * (uint32_t)i;
+        if (kSparseA && kbmax <= 16 * i) {  // warp-uniform: no window reaches this chunk
+          st_shared_v4(sA[i] + soff, 0u, 0u, 0u, 0u);
+          continue;
+        }
         st_shared_v4(sA[i] + soff,
                      prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x03020100u), 0u, 0xBA98u) & smA,
                      prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x07060504u), 0u, 0xBA98u) & smA,
@@ -738,7 +771,7 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
                      prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x0F0E0D0Cu), 0u, 0xBA98u) & smA);
       }
 #pragma unroll
-      for (int i = 0; i < NBC; ++i) {
+      for (int i = 0; i < (kNoB ? 0 : NBC); ++i) {
         st_shared_v4(sB[i] + soff,
                      prmt(mad_u32(u, rep, pcw[i].x), 0u, 0xBA98u) & smB,
                      prmt(mad_u32(u, rep, pcw[i].y), 0u, 0xBA98u) & smB,
@@ -986,8 +1019,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
       bool ok;
       if constexpr (kProd == kProdRows)
-        ok = produce_rows<BN, LG, kSeg, Cfg::kNS>(prm, b, st, smem_s, tmem_base, warp, lane, slice,
-                                                  slice_b,
+        ok = produce_rows<BN, LG, kSeg, Cfg::kNS, false, false, BN == 64>(
+            prm, b, st, smem_s, tmem_base, warp, lane, slice, slice_b,
                                         m0, n0);
       else
         ok = produce_chunks<BN, kProd == kProdTable, kSeg>(prm, b, st, smem_s, therm_u, tmem_base,
@@ -1028,8 +1061,14 @@ constexpr size_t kPairSmem = (size_t)kPairStages * kPairStage + 1024 /*align*/ +
 constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
                                 ((uint32_t)(256 >> 4) << 24);
 
-template <int LG>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_kernel(const TcParams prm) {
+// With kPackedB the b halves come from a prepacked buffer by TMA: warp
+// kTmaWarp (an 18th warp) loads this CTA's 128 b rows of each k-block and the
+// producers generate only the a rows.
+constexpr int kTmaWarp = 1 + kProducerWarps;
+
+template <int LG, bool kPackedB>
+__global__ void __launch_bounds__(kThreads + 32, 1)
+    gemm_tc_pair_kernel(const TcParams prm, const __grid_constant__ CUtensorMap tmap) {
   constexpr uint32_t kTmemAlloc = 512;  // two 256-column accumulators
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
@@ -1051,7 +1090,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_kernel(const TcParam
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&b.full[s], kProducerWarps);  // this CTA's producer warps
+      // this CTA's producer warps (+ the TMA thread's expect_tx arrival)
+      mbar_init(&b.full[s], kProducerWarps + (kPackedB ? 1 : 0));
       mbar_init(&b.empty[s], 1);
       mbar_init(&b.pfull[s], 1);              // the odd CTA's stage (even CTA only)
     }
@@ -1135,6 +1175,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_kernel(const TcParam
       }
     }
     __syncwarp();
+  } else if (kPackedB && warp == kTmaWarp) {
+    // ========================== b loader (lane 0): prepacked rows by TMA
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      const uint32_t smem0 = smem_u32(smem);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t it = 0;
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++it) {
+        const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+        const int nb0 = (int)((rem / prm.tiles_m) * 256 + (int64_t)rank * 128);
+        // the previous tile's epilogue stages its transpose in the ring
+        if (it > 0 && !mbar_wait(b.epi, (uint32_t)((it - 1) & 1), b.abort)) break;
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.empty[stage], phase ^ 1, b.abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&b.full[stage], kPairStageB);
+          tma_load_2d(smem0 + stage * kPairStage + kPairStageA, &tmap, (int)(kb * kKB), nb0,
+                      &b.full[stage]);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
   } else {
     // ============================ producers + epilogue (kProducerWarps warps)
     const uint32_t smem_s = smem_u32(smem);
@@ -1146,9 +1210,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_kernel(const TcParam
       const int64_t m0 = (rem % prm.tiles_m) * (2 * kBM) + (int64_t)rank * kBM;
       const int64_t n0 = (rem / prm.tiles_m) * 256;
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
-      if (!produce_rows<128, LG, false, kPairStages, true>(prm, b, st, smem_s, tmem_base, warp,
-                                                           lane, slice, slice_b, m0,
-                                                           n0 + (int64_t)rank * 128))
+      if (!produce_rows<128, LG, false, kPairStages, true, kPackedB>(
+              prm, b, st, smem_s, tmem_base, warp, lane, slice, slice_b, m0,
+              n0 + (int64_t)rank * 128))
         break;
       if (!tile_epilogue<256, false, true>(prm, b, st, smem, tmem_base, warp, lane, slice, slice_b,
                                            m0, n0, it))
@@ -1179,43 +1243,83 @@ cudaError_t launch_bn(TcParams prm, int sms, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <int LG>
-cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
-  auto kern = gemm_tc_pair_kernel<LG>;
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+template <int LG, bool kPackedB>
+cudaError_t launch_pair_v(TcParams prm, int dev, const CUtensorMap &tmap, cudaStream_t s) {
+  auto kern = gemm_tc_pair_kernel<LG, kPackedB>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
   if (e != cudaSuccess) return e;
-  prm.rep = 0x01010101u;
-  prm.stage_bytes = kPairStage;
-  // pair tiles: 512 a rows x 256 b rows
-  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
-  prm.tiles_n = (prm.n_rows + 255) / 256;
-  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kThreads + (kPackedB ? 32 : 0), 1, 1);
   cfg.dynamicSmemBytes = kPairSmem;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // one cluster per resident pair slot (persistent tiles)
-  static int max_clusters[64][3] = {};
-  int clusters = dev >= 0 && dev < 64 ? max_clusters[dev][LG - 6] : 0;
+  static int max_clusters[64] = {};
+  int clusters = dev >= 0 && dev < 64 ? max_clusters[dev] : 0;
   if (clusters <= 0) {
     cfg.gridDim = dim3(2, 1, 1);
     if ((e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg)) != cudaSuccess) return e;
     if (clusters <= 0) return cudaErrorInvalidConfiguration;
-    if (dev >= 0 && dev < 64) max_clusters[dev][LG - 6] = clusters;
+    if (dev >= 0 && dev < 64) max_clusters[dev] = clusters;
   }
   const int64_t grid = prm.tiles < clusters ? prm.tiles : clusters;
   cfg.gridDim = dim3((unsigned)(2 * grid), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, prm);
+  e = cudaLaunchKernelEx(&cfg, kern, prm, tmap);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+template <int LG>
+cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = kPairStage;
+  // pair tiles: 512 a rows x 256 b rows
+  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
+  prm.tiles_n = (prm.n_rows + 255) / 256;
+  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
+  CUtensorMap tmap;
+  memset(&tmap, 0, sizeof(tmap));
+  // prepacked b (bytes laid out at Lp = 2^prec) serves calls whose padded
+  // stream length is the full 2^prec
+  const GemmProblem &P = prm.P;
+  if (P.b_streams && P.batch_b == 1 && LG == P.prec) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc) {
+      const cuuint64_t row_bytes = (cuuint64_t)(P.ldk << LG);
+      cuuint64_t gdim[2] = {row_bytes, (cuuint64_t)P.N};
+      cuuint64_t gstride[1] = {row_bytes};
+      cuuint32_t box[2] = {(cuuint32_t)kKB, 128u};
+      cuuint32_t estride[2] = {1u, 1u};
+      const CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                             const_cast<uint8_t *>(P.b_streams), gdim, gstride, box, estride,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r == CUDA_SUCCESS) return launch_pair_v<LG, true>(prm, dev, tmap, s);
+    }
+    // no encoder or a rejected map: generate b from the packed codes instead
+  }
+  return launch_pair_v<LG, false>(prm, dev, tmap, s);
 }
 
 template <int BN, bool kSeg>

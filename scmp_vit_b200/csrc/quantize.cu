@@ -246,7 +246,56 @@ __global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int poo
   }
 }
 
+__device__ __forceinline__ uint32_t prmt_sign(uint32_t a) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(r) : "r"(a));
+  return r;
+}
+
+// Prepacked b operand bytes at Lp = 2^prec, one thread per 16-byte chunk:
+// byte t of reduction index d of row n is sigma * [R[d][t] >> shift < u]
+// with u = |c| >> shift, formed exactly as the tensor-core row producers
+// form it (u * 0x01010101 + PC, sign-replicating byte permute, AND with
+// 0x01010101 or 0xFFFFFFFF).  pool_comp rows are 2^prec bytes apart.
+__global__ void pack_b_streams_kernel(const int16_t *__restrict__ code, int64_t N, int64_t ldk,
+                                      int prec, int shift, const uint8_t *__restrict__ pool_comp,
+                                      uint8_t *__restrict__ out) {
+  const int64_t row_bytes = ldk << prec;
+  const int64_t per_row = row_bytes >> 4;
+  const int64_t total = N * per_row;
+  const int64_t tmask = (1 << prec) - 1;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / per_row;
+    const int64_t pos = (i % per_row) << 4;
+    const int64_t d = pos >> prec;
+    const int c = code[n * ldk + d];
+    const uint32_t u = (uint32_t)(abs(c) >> shift);
+    const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
+    const uint4 pc =
+        *reinterpret_cast<const uint4 *>(pool_comp + (d << prec) + (pos & tmask));
+    uint4 w;
+    w.x = prmt_sign(u * 0x01010101u + pc.x) & sm;
+    w.y = prmt_sign(u * 0x01010101u + pc.y) & sm;
+    w.z = prmt_sign(u * 0x01010101u + pc.z) & sm;
+    w.w = prmt_sign(u * 0x01010101u + pc.w) & sm;
+    *reinterpret_cast<uint4 *>(out + n * row_bytes + pos) = w;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, int prec,
+                                  int shift, const uint8_t *pool_comp, uint8_t *out,
+                                  cudaStream_t s) {
+  const int64_t total = N * ((ldk << prec) >> 4);
+  if (total == 0) return cudaSuccess;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift, pool_comp,
+                                                         out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_row_stats(const void *x, bool x_bf16, int64_t rows, int64_t K, int mode,
                              float2 *stat, cudaStream_t s) {

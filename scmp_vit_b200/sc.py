@@ -29,7 +29,8 @@ import torch
 from . import _lib
 from .config_helpers import make_sobol_simple_config, pool_table
 
-__all__ = ["sc_matmul", "device_pool", "default_config", "set_default_engine"]
+__all__ = ["sc_matmul", "device_pool", "default_config", "set_default_engine", "prepack_b",
+           "PackedWeight"]
 
 _DEFAULT_ENGINE = "auto"
 
@@ -74,6 +75,85 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+class PackedWeight:
+    """A weight ``b`` ([N, K]) quantised and expanded into its tensor-core
+    operand bytes once (``scmp_prepack_b``); pass it as ``b`` to
+    ``sc_matmul`` with the same granularity, mode, sc_prec, config and
+    group_b.  Results are bit-identical to passing the weight itself; the
+    engine loads the bytes with TMA instead of generating them in every call.
+    Holds about ``N * K * 2**sc_prec`` bytes of device memory."""
+
+    def __init__(self, buf: torch.Tensor, N: int, K: int, granularity: str, mode: str,
+                 sc_prec: int, config: dict, group_b: int):
+        self.buf = buf
+        self.N, self.K = N, K
+        self.granularity, self.mode, self.sc_prec = granularity, mode, sc_prec
+        self.config = config
+        self.group_b = group_b
+        self.device = buf.device
+
+    @property
+    def shape(self):
+        return (self.N, self.K)
+
+    def matches(self, *, granularity: str, mode: str, sc_prec: int, config: dict,
+                group_b: int) -> bool:
+        return (granularity == self.granularity and mode == self.mode and
+                sc_prec == self.sc_prec and config["uid"] == self.config["uid"] and
+                (granularity != "per_row" or max(int(group_b), 1) == self.group_b))
+
+
+def _base_args(engine: str, granularity: str, mode: str, p: int, L: int, group_a: int,
+               group_b: int) -> "_lib.MatmulArgs":
+    args = _lib.MatmulArgs()
+    args.abi_version = _lib.ABI_VERSION
+    args.engine = _lib.ENGINE[engine]
+    args.granularity = _lib.GRANULARITY[granularity]
+    args.mode = _lib.MODE[mode]
+    args.sc_prec = p
+    args.stoc_len = L
+    args.group_a = max(int(group_a), 1)
+    args.group_b = max(int(group_b), 1)
+    return args
+
+
+@torch.no_grad()
+def prepack_b(b: torch.Tensor, *, granularity: str = "per_row", mode: str = "bipolar",
+              sc_prec: int = 8, config: Optional[dict] = None,
+              group_b: int = 1) -> PackedWeight:
+    """Quantise the weight ``b`` ([N, K], fp32 or bf16, CUDA) and expand its
+    SC operand bytes once (see ``PackedWeight``)."""
+    if granularity not in _lib.GRANULARITY or mode not in _lib.MODE:
+        raise ValueError(f"unknown granularity / mode {granularity!r} / {mode!r}")
+    if b.dim() != 2 or not b.is_cuda:
+        raise ValueError("prepack_b needs a 2-D CUDA weight [N, K]")
+    N, K = b.shape
+    p = int(sc_prec)
+    if config is None:
+        config = default_config(K, p)
+    if int(config["sc_prec"]) != p or int(config["dims"]) < K:
+        raise ValueError("config must be (>= K dims, sc_prec) for prepacking")
+    bt = b.contiguous() if b.dtype in (torch.float32, torch.bfloat16) else b.float().contiguous()
+    dev = b.device
+    pool = device_pool(config, dev)
+    args = _base_args("auto", granularity, mode, p, 1 << p, 1, group_b)
+    args.b = bt.data_ptr()
+    args.batch, args.batch_b, args.M, args.N, args.K = 1, 1, 1, N, K
+    args.pool = pool.data_ptr()
+    args.pool_dims = K
+    args.io_flags = _lib.IO_B_BF16 if bt.dtype == torch.bfloat16 else 0
+    lib = _lib.load()
+    nbytes = lib.scmp_prepack_b_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(lib.scmp_prepack_b(ctypes.byref(args), None, 0, None))  # raises the reason
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(lib.scmp_prepack_b(ctypes.byref(args), ctypes.c_void_p(buf.data_ptr()),
+                                      nbytes, ctypes.c_void_p(stream)))
+    return PackedWeight(buf, N, K, granularity, mode, p, config, max(int(group_b), 1))
+
+
 @torch.no_grad()
 def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
               mode: str = "bipolar", sc_prec: int = 8, config: Optional[dict] = None,
@@ -113,19 +193,24 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     engine = _DEFAULT_ENGINE if engine is None else engine
     if engine not in _lib.ENGINE:
         raise ValueError(f"unknown engine {engine!r}")
-    if a.dim() not in (2, 3) or b.dim() not in (2, 3):
+    packed = b if isinstance(b, PackedWeight) else None
+    if a.dim() not in (2, 3) or (packed is None and b.dim() not in (2, 3)):
         raise ValueError(f"sc_matmul expects 2-D or 3-D operands, got {tuple(a.shape)} "
                          f"and {tuple(b.shape)}")
-    if not a.is_cuda or not b.is_cuda:
+    if not a.is_cuda or (packed is None and not b.is_cuda):
         raise RuntimeError("sc_matmul runs on the CUDA engine only (no CPU path); "
                            f"got devices {a.device} and {b.device}")
     if a.device != b.device:
         raise ValueError(f"operands on different devices: {a.device} vs {b.device}")
     batched = a.dim() == 3
     a3 = a if batched else a.unsqueeze(0)
-    b3 = b if b.dim() == 3 else b.unsqueeze(0)
     BH, M, K = a3.shape
-    BHb, N, Kb = b3.shape
+    if packed is not None:
+        BHb, N, Kb = 1, packed.N, packed.K
+        b3 = None
+    else:
+        b3 = b if b.dim() == 3 else b.unsqueeze(0)
+        BHb, N, Kb = b3.shape
     if Kb != K:
         raise ValueError(f"inner-dim mismatch: a K={K}, b K={Kb}")
     if BHb not in (1, BH):
@@ -143,7 +228,15 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
             t = t.float()
         return t.contiguous()
     a3 = _operand(a3)
-    b3 = _operand(b3)
+    if packed is not None:
+        if chunk_d or k_segment:
+            raise ValueError("a prepacked b runs without chunk_d / k_segment")
+        if not packed.matches(granularity=granularity, mode=mode, sc_prec=p, config=config,
+                              group_b=group_b):
+            raise ValueError("prepacked b was built with other granularity / mode / sc_prec / "
+                             "config / group_b")
+    else:
+        b3 = _operand(b3)
     if chunk_d and 0 < int(chunk_d) < K and mode == "bipolar":
         chunk_d = int(chunk_d)
         if dims < chunk_d:
@@ -197,7 +290,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     args.abi_version = _lib.ABI_VERSION
     args.engine = _lib.ENGINE[engine]
     args.a = a3.data_ptr()
-    args.b = b3.data_ptr()
+    args.b = packed.buf.data_ptr() if packed is not None else b3.data_ptr()
     args.batch, args.batch_b, args.M, args.N, args.K = BH, BHb, M, N, K
     args.granularity = _lib.GRANULARITY[granularity]
     args.mode = _lib.MODE[mode]
@@ -214,7 +307,8 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     args.out = out.data_ptr()
     args.acc_out = _ptr(acc_out)
     args.io_flags = ((_lib.IO_A_BF16 if a3.dtype == torch.bfloat16 else 0)
-                     | (_lib.IO_B_BF16 if b3.dtype == torch.bfloat16 else 0)
+                     | (_lib.IO_B_BF16 if b3 is not None and b3.dtype == torch.bfloat16 else 0)
+                     | (_lib.IO_B_PACKED if packed is not None else 0)
                      | (_lib.IO_OUT_BF16 if out.dtype == torch.bfloat16 else 0))
     lib = _lib.load()
     nbytes = lib.scmp_sc_matmul_workspace_size(ctypes.byref(args))

@@ -79,7 +79,7 @@ def _get_config(D, sc_prec):
 
 def _sc_linear(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int,
                mode: str = "bipolar", cfg_override: dict = None,
-               stoc_len: int | None = None, chunk_d: int = 0):
+               stoc_len: int | None = None, chunk_d: int = 0, packed=None):
     """``y = x @ weight^T + bias`` via SC; per-row scales for x and weight
     rows.  Bias is added in the engine's epilogue (same fp32 add)."""
     orig_shape = x.shape
@@ -102,8 +102,9 @@ def _sc_linear(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int,
                       chunk_d=chunk_d, stoc_len=stoc_len, bias=bias, out_dtype=odt)
     else:
         cfg = cfg_override if cfg_override is not None else _get_config(D_in, sc_prec)
-        y = sc_matmul(x2, w, granularity="per_row", group_a=1, group_b=1, mode=mode,
-                      sc_prec=sc_prec, config=cfg, stoc_len=stoc_len, bias=bias, out_dtype=odt)
+        y = sc_matmul(x2, packed if packed is not None else w, granularity="per_row", group_a=1,
+                      group_b=1, mode=mode, sc_prec=sc_prec, config=cfg, stoc_len=stoc_len,
+                      bias=bias, out_dtype=odt)
     return y.to(x.dtype).reshape(*orig_shape[:-1], w.shape[0])
 
 
@@ -262,6 +263,28 @@ def _sc_linear_mp(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int, mod
     return result.to(x.dtype).reshape(*orig_shape[:-1], D_out)
 
 
+_PREPACK = False
+
+
+def set_weight_prepack(enabled: bool) -> None:
+    """Whether ``SCLinear`` keeps its weight's SC operand bytes expanded once
+    (``sc.prepack_b``) instead of regenerating them in every call.  Results
+    are bit-identical either way; prepacking costs about ``N * K * 2**p``
+    bytes of device memory per layer and is redone when the weight changes.
+    Off by default: on B200 the large-N kernel is bound by shared-memory
+    traffic (operand stores + MMA reads), which a TMA-fed b does not reduce,
+    so the packed path measures the same speed (qkv_proj 16.36 vs 16.34 ms)."""
+    global _PREPACK
+    _PREPACK = bool(enabled)
+
+
+def _prepack_applies(weight: torch.Tensor, sc_prec: int, mode: str, stoc_len, chunk_d: int) -> bool:
+    from . import sc as _sc
+    return (_PREPACK and not USE_NOISE_MODEL and weight.is_cuda and chunk_d == 0
+            and 5 <= sc_prec <= 8 and not (mode == "unipolar" and sc_prec == 8)
+            and stoc_len in (None, 1 << sc_prec) and _sc._DEFAULT_ENGINE != "popc")
+
+
 class SCLinear(nn.Module):
     """Drop-in ``nn.Linear`` replacement running the matmul through SC
     (reference ``sc_linear.py:291-354``, same constructor)."""
@@ -290,12 +313,33 @@ class SCLinear(nn.Module):
                                                       group_size=range_mp_group_size)
         else:
             self.range_entries = None
+        self._packed = None
+        self._packed_key = None
+
+    def _packed_weight(self, D_in: int):
+        """The weight's prepacked SC operand (cached; rebuilt when the weight's
+        storage, version counter or the SC settings change)."""
+        from .sc import prepack_b
+        cfg = self.cfg_override if self.cfg_override is not None else _get_config(D_in, self.sc_prec)
+        w = self.weight
+        key = (w.data_ptr(), w._version, w.dtype, str(w.device), self.sc_prec, self.mode,
+               cfg["uid"])
+        if key != self._packed_key:
+            self._packed = None  # free the old buffer before building the new one
+            self._packed = prepack_b(w.detach(), granularity="per_row", mode=self.mode,
+                                     sc_prec=self.sc_prec, config=cfg, group_b=1)
+            self._packed_key = key
+        return self._packed
 
     def forward(self, x):
         if self.range_entries is None and self.mp_cfg is None and self.adaptive_mp_cfg is None:
+            packed = None
+            if _prepack_applies(self.weight, self.sc_prec, self.mode, self.stoc_len,
+                                self.chunk_d):
+                packed = self._packed_weight(x.shape[-1])
             return _sc_linear(x, self.weight, self.bias, self.sc_prec, mode=self.mode,
                               cfg_override=self.cfg_override, stoc_len=self.stoc_len,
-                              chunk_d=self.chunk_d)
+                              chunk_d=self.chunk_d, packed=packed)
         return _sc_linear_mp(x, self.weight, self.bias, self.sc_prec, self.mode,
                              range_entries=self.range_entries, mp_cfg=self.mp_cfg,
                              adaptive_mp_cfg=self.adaptive_mp_cfg, operator=self.operator,

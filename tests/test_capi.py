@@ -60,7 +60,7 @@ def _args(**kw):
     (dict(group_a=0), "group"),
     (dict(pool_dims=0), "pool_dims"),
     (dict(engine=5), "engine"),
-    (dict(io_flags=8), "io_flags"),
+    (dict(io_flags=16), "io_flags"),
 ])
 def test_invalid_arguments_are_rejected(kw, msg):
     lib = _lib.load()

@@ -1,0 +1,104 @@
+"""Prepacked weights (scmp_prepack_b / sc.prepack_b) on the engine (B200).
+
+A prepacked b must give exactly what the weight itself gives: the same
+popcount sums and the same outputs, on the CTA-pair kernel that loads the
+packed bytes with TMA (including b tiles past the last weight row), on the
+single-CTA and CUDA-core paths that read the packed codes, and through
+SCLinear's cache (rebuilt when the weight changes in place).
+"""
+import random
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from oracle import sc_oracle
+from scmp_vit_b200 import _lib
+from scmp_vit_b200 import config_helpers as ch
+from scmp_vit_b200 import sc_linear as scl
+from scmp_vit_b200.sc import prepack_b, sc_matmul
+
+pytestmark = pytest.mark.gpu
+
+
+def _same(dev, a, w, p, L=None, mode="bipolar", granularity="per_row", bias=None):
+    random.seed(p + a.shape[0])
+    K = a.shape[-1]
+    cfg = ch.make_sobol_simple_config(K, K, p)
+    M, N = a.shape[-2], w.shape[0]
+    BH = a.shape[0] if a.dim() == 3 else 1
+    acc1 = torch.empty(BH * M * N, dtype=torch.int32, device=dev)
+    acc2 = torch.empty_like(acc1)
+    kw = dict(granularity=granularity, mode=mode, sc_prec=p, config=cfg, stoc_len=L, bias=bias)
+    y1 = sc_matmul(a, w, acc_out=acc1, **kw)
+    pk = prepack_b(w, granularity=granularity, mode=mode, sc_prec=p, config=cfg)
+    y2 = sc_matmul(a, pk, acc_out=acc2, **kw)
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    assert torch.equal(acc1, acc2)
+    assert torch.equal(y1, y2)
+    return cfg, acc2, y2
+
+
+@pytest.mark.parametrize("M,N,K,p,L", [
+    (600, 384, 256, 7, None),    # CTA pairs + TMA b, odd CTA of the last pair part-filled
+    (513, 300, 64, 7, None),     # b tile past the last row (zero-filled box) + 1-row strip
+    (1024, 256, 40, 8, None),    # Lp = 256, K padded to 40
+    (700, 260, 72, 6, None),     # Lp = 64
+    (600, 384, 256, 7, 64),      # shorter stream: Lp 64 != 2^p, codes path
+    (200, 384, 128, 7, None),    # one a tile: single-CTA kernel on the packed codes
+])
+def test_prepacked_equals_weight(cuda_device, M, N, K, p, L):
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g).to(cuda_device)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(cuda_device)
+    _same(cuda_device, a, w, p, L)
+
+
+def test_prepacked_matches_oracle_and_bias(cuda_device):
+    g = torch.Generator().manual_seed(9)
+    a = torch.randn(520, 96, generator=g)
+    w = torch.randn(300, 96, generator=g) * 0.05
+    bias = torch.randn(300, generator=g)
+    cfg, acc, y = _same(cuda_device, a.to(cuda_device), w.to(cuda_device), 7,
+                        bias=bias.to(cuda_device))
+    acc_ref, y_ref = sc_oracle.sc_matmul_ref(a.numpy(), w.numpy(), granularity="per_row",
+                                             mode="bipolar", sc_prec=7, pool=cfg["table"],
+                                             stoc_len=128, bias=bias.numpy())
+    np.testing.assert_array_equal(acc.view(1, 520, 300).cpu().numpy(), acc_ref)
+    np.testing.assert_allclose(y.view(1, 520, 300).cpu().numpy(), y_ref, rtol=1e-5, atol=1e-30)
+
+
+def test_prepacked_unipolar_bf16_and_batched_a(cuda_device):
+    dev = cuda_device
+    g = torch.Generator().manual_seed(4)
+    a = torch.rand(2, 400, 128, generator=g).to(dev, torch.bfloat16)
+    w = torch.randn(320, 128, generator=g).to(dev, torch.bfloat16)
+    _same(dev, a, w, 7, mode="unipolar")
+    _same(dev, a, w, 7, granularity="per_tensor")
+
+
+def test_sclinear_cache_follows_the_weight(cuda_device):
+    dev = cuda_device
+    g = torch.Generator().manual_seed(5)
+    lin = nn.Linear(256, 384).to(dev)
+    x = torch.randn(600, 256, generator=g).to(dev)
+    random.seed(0)
+    m = scl.SCLinear(lin, 7)
+    try:
+        scl.set_weight_prepack(False)
+        y_plain = m(x)
+        scl.set_weight_prepack(True)
+        y_packed = m(x)
+        assert m._packed is not None
+        torch.testing.assert_close(y_packed, y_plain, rtol=0, atol=0)
+        with torch.no_grad():
+            lin.weight.mul_(-0.5)  # in place: bumps the version counter
+        y2 = m(x)
+        scl.set_weight_prepack(False)
+        torch.testing.assert_close(y2, m(x), rtol=0, atol=0)
+    finally:
+        scl.set_weight_prepack(False)
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0

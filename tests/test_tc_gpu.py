@@ -99,6 +99,15 @@ def test_tc_unipolar_rows(cuda_device):
     _check(cuda_device, a, b, 7, 128, mode="unipolar", bias=torch.randn(192, generator=g))
 
 
+def test_tc_sparse_windows_attn_v(cuda_device):
+    """Attn@V-shaped: peaked softmax rows give mostly short enable windows, so
+    the narrow-tile producers skip whole all-zero chunks; counts stay exact."""
+    g = torch.Generator().manual_seed(6)
+    a = torch.softmax(torch.randn(300, 264, generator=g) * 3.0, dim=-1)
+    b = torch.randn(64, 264, generator=g)
+    _check(cuda_device, a, b, 7, 128)
+
+
 def test_tc_row_stream_lengths(cuda_device):
     g = torch.Generator().manual_seed(3)
     a = torch.randn(256, 64, generator=g)
