@@ -243,20 +243,49 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
       const int16_t *ca = P.qa.code + grow * P.ldk;
       const int16_t *cb = P.qb.code + brow * P.ldk;
       int dm = 0;  // d mod pool_dims
-      for (int d = 0; d < K; ++d) {
-        const int a = ca[d], b = cb[d];
+      // one reduction index: window of a, stream word(s) of b from the table
+      auto step = [&](int a, int b) {
         const int k = ((a < 0 ? -a : a) * L) >> P.prec;
         const uint32_t *st = P.stream_table + ((int64_t)dm * (T + 1) + (b < 0 ? -b : b)) * WT;
         if (++dm == pd) dm = 0;
         int cnt = 0;
+        if (LW == 4 && WT == 4) {  // the four words of a 128-position stream in one load
+          const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(st));
+          const uint32_t sw[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int w = 0; w < LW; ++w) {
-          const int lo = 32 * w;
-          const uint32_t win = k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
-          cnt += __popc(win & __ldg(st + w));
+          for (int w = 0; w < 4; ++w) {
+            const int lo = 32 * w;
+            const uint32_t win =
+                k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
+            cnt += __popc(win & sw[w]);
+          }
+        } else {
+#pragma unroll
+          for (int w = 0; w < LW; ++w) {
+            const int lo = 32 * w;
+            const uint32_t win =
+                k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
+            cnt += __popc(win & __ldg(st + w));
+          }
         }
         acc += ((a < 0) != (b < 0) ? -cnt : cnt);
+      };
+      int d = 0;
+      if ((P.ldk & 7) == 0) {
+        // codes 8 at a time: rows of ldk int16 codes start on 16 bytes
+        const uint4 *ca4 = reinterpret_cast<const uint4 *>(ca);
+        const uint4 *cb4 = reinterpret_cast<const uint4 *>(cb);
+        for (; d + 8 <= K; d += 8) {
+          const uint4 va = __ldg(ca4 + (d >> 3)), vb = __ldg(cb4 + (d >> 3));
+          const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            step((int)(int16_t)(wa[j] & 0xFFFFu), (int)(int16_t)(wb[j] & 0xFFFFu));
+            step((int)wa[j] >> 16, (int)wb[j] >> 16);
+          }
+        }
       }
+      for (; d < K; ++d) step(ca[d], cb[d]);
     }
     float y = 0.0f;
     if (L > 0)

@@ -36,18 +36,39 @@ __device__ __forceinline__ int warp_sum(int v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// Reductions over the LPR lanes that share a row (aligned groups of a warp).
+template <int LPR>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <int LPR>
+__device__ __forceinline__ float group_min(float v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <int LPR>
+__device__ __forceinline__ int group_sum(int v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
-// One warp per row: (max|x|, -) for bipolar, (min x, max x) for unipolar.
-template <typename T>
+// LPR lanes per row (32, or 8 for short rows): (max|x|, -) for bipolar,
+// (min x, max x) for unipolar.
+template <typename T, int LPR>
 __global__ void row_stats_kernel(const T *__restrict__ x, int64_t rows, int64_t K, int mode,
                                  float2 *__restrict__ stat) {
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  const T *xr = x + warp * K;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LPR;
+  const int lane = threadIdx.x % LPR;
+  const bool active = row < rows;  // inactive lanes still take part in the shuffles
+  const T *xr = x + (active ? row : 0) * K;
+  const int64_t kk = active ? K : 0;
   float lo = INFINITY, hi = -INFINITY;
-  if constexpr (!std::is_same<T, float>::value) {
-    for (int64_t i = lane; i < K; i += 32) {
+  if constexpr (!std::is_same<T, float>::value || LPR != 32) {
+    for (int64_t i = lane; i < kk; i += LPR) {
       const float v = ldx(xr + i);
       if (mode == SCMP_BIPOLAR) {
         hi = fmaxf(hi, fabsf(v));
@@ -58,7 +79,7 @@ __global__ void row_stats_kernel(const T *__restrict__ x, int64_t rows, int64_t 
     }
   } else if ((K & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
     const float4 *x4 = reinterpret_cast<const float4 *>(xr);
-    for (int64_t i = lane; i < (K >> 2); i += 32) {
+    for (int64_t i = lane; i < (kk >> 2); i += 32) {
       float4 v = __ldg(x4 + i);
       if (mode == SCMP_BIPOLAR) {
         hi = fmaxf(hi, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
@@ -68,7 +89,7 @@ __global__ void row_stats_kernel(const T *__restrict__ x, int64_t rows, int64_t 
       }
     }
   } else {
-    for (int64_t i = lane; i < K; i += 32) {
+    for (int64_t i = lane; i < kk; i += 32) {
       float v = __ldg(xr + i);
       if (mode == SCMP_BIPOLAR) {
         hi = fmaxf(hi, fabsf(v));
@@ -78,9 +99,9 @@ __global__ void row_stats_kernel(const T *__restrict__ x, int64_t rows, int64_t 
       }
     }
   }
-  hi = warp_max(hi);
-  lo = warp_min(lo);
-  if (lane == 0) stat[warp] = make_float2(lo, hi);
+  hi = group_max<LPR>(hi);
+  lo = group_min<LPR>(lo);
+  if (active && lane == 0) stat[row] = make_float2(lo, hi);
 }
 
 // Scale of one group from its min / max (shared by both group kernels).
@@ -162,28 +183,31 @@ __global__ void __launch_bounds__(1024) group_stats_kernel(const float2 *__restr
   }
 }
 
-// One warp per row: signed codes, per-row scale/zero, magnitude row sum.
+// LPR lanes per row: signed codes, per-row scale/zero, magnitude row sum.
 // Codes are written with row stride ldc >= K; indices K .. ldc-1 get code 0,
 // which contributes nothing to any count (zero window, zero threshold).
-template <typename T>
+template <typename T, int LPR>
 __global__ void quantize_kernel(const T *__restrict__ x, GroupShape g, int64_t K, int64_t ldc,
                                 int mode, int prec, const float *__restrict__ gscale,
                                 const float *__restrict__ ginv, const int32_t *__restrict__ gzero,
                                 int16_t *__restrict__ code, float *__restrict__ rscale,
                                 int32_t *__restrict__ rzero, int32_t *__restrict__ rsum) {
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= g.rows) return;
-  const int64_t grp = group_of_row(g, row);
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LPR;
+  const int lane = threadIdx.x % LPR;
+  const bool active = row < g.rows;  // inactive lanes still take part in the shuffles
+  const int64_t r = active ? row : 0;
+  const int64_t grp = group_of_row(g, r);
   const float inv = ginv[grp];
   const int32_t z = gzero[grp];
-  const T *xr = x + row * K;
-  int16_t *cr = code + row * ldc;
-  for (int64_t i = K + lane; i < ldc; i += 32) cr[i] = 0;
+  const T *xr = x + r * K;
+  int16_t *cr = code + r * ldc;
+  const int64_t kk = active ? K : 0;
+  if (active)
+    for (int64_t i = K + lane; i < ldc; i += LPR) cr[i] = 0;
   int acc = 0;
   if (mode == SCMP_BIPOLAR) {
     const int iq = (1 << (prec - 1)) - 1;
-    for (int64_t i = lane; i < K; i += 32) {
+    for (int64_t i = lane; i < kk; i += LPR) {
       int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv));
       q = max(-iq, min(iq, q));
       cr[i] = (int16_t)(2 * q);
@@ -191,15 +215,15 @@ __global__ void quantize_kernel(const T *__restrict__ x, GroupShape g, int64_t K
     }
   } else {
     const int iq = (1 << prec) - 1;
-    for (int64_t i = lane; i < K; i += 32) {
+    for (int64_t i = lane; i < kk; i += LPR) {
       int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv)) + z;
       q = max(0, min(iq, q));
       cr[i] = (int16_t)q;
       acc += q;
     }
   }
-  acc = warp_sum(acc);
-  if (lane == 0) {
+  acc = group_sum<LPR>(acc);
+  if (active && lane == 0) {
     rscale[row] = gscale[grp];
     rzero[row] = z;
     rsum[row] = acc;
@@ -301,13 +325,20 @@ cudaError_t launch_row_stats(const void *x, bool x_bf16, int64_t rows, int64_t K
                              float2 *stat, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   const int threads = 256;
-  const int64_t blocks = (rows * 32 + threads - 1) / threads;
-  if (x_bf16)
-    row_stats_kernel<<<(unsigned)blocks, threads, 0, s>>>(
-        static_cast<const __nv_bfloat16 *>(x), rows, K, mode, stat);
+  // short rows (K <= 128): 8 lanes per row, 4 rows per warp
+  const int lpr = K <= 128 ? 8 : 32;
+  const int64_t blocks = (rows * lpr + threads - 1) / threads;
+  const auto *xb = static_cast<const __nv_bfloat16 *>(x);
+  const auto *xf = static_cast<const float *>(x);
+  if (x_bf16 && lpr == 8)
+    row_stats_kernel<__nv_bfloat16, 8><<<(unsigned)blocks, threads, 0, s>>>(xb, rows, K, mode, stat);
+  else if (x_bf16)
+    row_stats_kernel<__nv_bfloat16, 32><<<(unsigned)blocks, threads, 0, s>>>(xb, rows, K, mode,
+                                                                             stat);
+  else if (lpr == 8)
+    row_stats_kernel<float, 8><<<(unsigned)blocks, threads, 0, s>>>(xf, rows, K, mode, stat);
   else
-    row_stats_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const float *>(x), rows, K,
-                                                          mode, stat);
+    row_stats_kernel<float, 32><<<(unsigned)blocks, threads, 0, s>>>(xf, rows, K, mode, stat);
   return cudaGetLastError();
 }
 
@@ -335,15 +366,23 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
                             cudaStream_t s) {
   if (g.rows == 0) return cudaSuccess;
   const int threads = 256;
-  const int64_t blocks = (g.rows * 32 + threads - 1) / threads;
-  if (x_bf16)
-    quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), g,
-                                                          K, ldc, mode, prec, gscale, ginv, gzero,
-                                                          code, rscale, rzero, rsum);
+  const int lpr = ldc <= 128 ? 8 : 32;  // short rows: 8 lanes per row
+  const int64_t blocks = (g.rows * lpr + threads - 1) / threads;
+  const auto *xb = static_cast<const __nv_bfloat16 *>(x);
+  const auto *xf = static_cast<const float *>(x);
+#define SCMP_QUANTIZE(T, LPR, X)                                                              \
+  quantize_kernel<T, LPR><<<(unsigned)blocks, threads, 0, s>>>(X, g, K, ldc, mode, prec, gscale, \
+                                                               ginv, gzero, code, rscale, rzero,  \
+                                                               rsum)
+  if (x_bf16 && lpr == 8)
+    SCMP_QUANTIZE(__nv_bfloat16, 8, xb);
+  else if (x_bf16)
+    SCMP_QUANTIZE(__nv_bfloat16, 32, xb);
+  else if (lpr == 8)
+    SCMP_QUANTIZE(float, 8, xf);
   else
-    quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const float *>(x), g, K, ldc,
-                                                          mode, prec, gscale, ginv, gzero, code,
-                                                          rscale, rzero, rsum);
+    SCMP_QUANTIZE(float, 32, xf);
+#undef SCMP_QUANTIZE
   return cudaGetLastError();
 }
 
