@@ -307,7 +307,7 @@ int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_byt
   const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
   cudaError_t e;
   if ((e = launch_pool_complement(x.pool, x.pool_dims, pk.pool_rows, x.sc_prec, x.sc_prec, shift,
-                                  pb + pk.pool_comp, s)) != cudaSuccess)
+                                  false, pb + pk.pool_comp, s)) != cudaSuccess)
     return cuda_fail(e, "pool_complement launch");
   if ((e = launch_pack_b_streams(reinterpret_cast<const int16_t *>(pb + pk.B.code), x.N, pk.ldk,
                                  x.sc_prec, shift, pb + pk.pool_comp, pb + pk.streams, s)) !=
@@ -405,7 +405,8 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
     if (tc_row_producers(P)) {
       const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
       if ((e = launch_pool_complement(x.pool, x.pool_dims, plan.pool_comp_rows, x.sc_prec,
-                                      tc_stream_log2(P), shift, ws + plan.pool_comp, s)) !=
+                                      tc_stream_log2(P), shift, tc_nibble_pairs(P, m_tc, n_tc),
+                                      ws + plan.pool_comp, s)) !=
           cudaSuccess)
         return cuda_fail(e, "pool_complement launch");
       count_launches(1);

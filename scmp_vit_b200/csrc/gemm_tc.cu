@@ -75,6 +75,7 @@ struct TcParams {
   // compile to IMADs (the FMA pipe) rather than shifts and adds (the ALU pipe).
   uint32_t rep;          // 0x01010101
   uint32_t stage_bytes;  // TcCfg<BN>::kStage
+  int ncols;             // e2m1 CTA pairs: b rows (accumulator columns) per tile
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -803,15 +804,312 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
 }
 
 // ---------------------------------------------------------------------------
+// Narrow tiles with the window operand in tensor memory (tcgen05.mma reading
+// A from TMEM).  With BN <= 128 the 256 a rows are most of the operand bytes;
+// in shared memory they cost a 32 KB store plus a 32 KB MMA read per k-block,
+// the bandwidth that bounds those tiles.  Here each producer thread writes its
+// 64 bytes of an a row straight into its TMEM lane (one tcgen05.st of 16
+// columns); only the BN b rows go through shared memory.
+//
+// TMEM columns: [0, 2 BN) the two int32 accumulators (a rows 0-127 / 128-255),
+// then kTsStages stages of 64 columns: half h (a rows 128 h .. + 127, one per
+// lane) at +32 h, its 128 bytes of k-block as 32 columns of 4 int8 each.
+constexpr int kTsStages = 4;
+constexpr uint32_t kEpiStagingBytes =
+    kProducerWarps * 32 * 33 * 4 + kProducerWarps * 32 * 16;  // tile_epilogue's transpose + rows
+
+template <int BN>
+struct TsCfg {
+  static constexpr uint32_t kStageB = BN * kKB;
+  // the ring doubles as the epilogue's staging area
+  static constexpr uint32_t kRing =
+      ((kTsStages * kStageB > kEpiStagingBytes ? kTsStages * kStageB : kEpiStagingBytes) + 1023) &
+      ~1023u;
+  static constexpr uint32_t kAcol = 2 * BN;   // first window-operand column
+  static constexpr uint32_t kAStageCols = 64;  // 256 rows x 128 bytes over 128 lanes
+  static_assert(kAcol + kTsStages * kAStageCols <= 512, "accumulators + window stages fit TMEM");
+  static constexpr size_t smem_bytes = (size_t)kRing + 1024 /*align*/ + 256;
+};
+
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Row producers for the TMEM window operand.  TMEM lane quarters follow the
+// warp (warp w reaches lanes 32 (w % 4) ..), so producer warp pw = w - 1
+// generates a rows 128 h + 32 (w % 4) + lane, h = (pw / 4) % 2, and the half
+// 64 e .. 64 e + 63 of their k-block bytes, e = pw / 8.  The b rows and the
+// code / pool-complement streaming are those of produce_rows.  A chunk that
+// lies past every window of the warp's 32 rows is zero and one that lies
+// inside all of them is sigma in every byte; neither needs arithmetic.
+template <int BN, int LG>
+__device__ bool produce_rows_ts(const TcParams &prm, const Bars &b, ProdState &st, uint32_t smem_s,
+                                uint32_t tmem_base, int warp, int lane, int64_t slice,
+                                int64_t slice_b, int64_t m0, int64_t n0) {
+  static_assert(LG >= 6 && LG <= 8, "row producers need 64 <= Lp <= 256");
+  using Cfg = TsCfg<BN>;
+  constexpr int NS = kTsStages;
+  const GemmProblem &P = prm.P;
+  constexpr int NBC = BN / 64;       // b chunks per thread
+  constexpr int G = (1 << LG) / 16;  // k-blocks per macro step (8 reduction indices)
+  constexpr int LPB = 1 << LG;       // pool complement row stride (bytes)
+  static_assert(G % NS == 0, "a macro step is a whole number of ring turns");
+  const int pt = threadIdx.x - 32;
+  const int pw = warp - 1;
+  const int quarter = warp & 3;
+  const int hA = pw >> 3;                                  // a bytes 64 hA .. + 63
+  const int ra = ((pw >> 2) & 1) * 128 + quarter * 32 + lane;  // a row of the tile
+  const int rbn = pt & (BN - 1);
+  const int cB0 = NBC * (pt / BN);
+  const int64_t gmA = m0 + ra;
+  const bool vA = gmA < prm.m_rows;
+  const int64_t growA = slice * P.M + (vA ? gmA : prm.m_rows - 1);
+  int Lg = 0;
+  if (vA) {
+    const int L = row_stream_len(P, slice, growA);
+    Lg = L > 0 ? L : 0;
+  }
+  const int64_t gnB = n0 + rbn;
+  const int64_t growB = slice_b * P.N + (gnB < prm.n_rows ? gnB : prm.n_rows - 1);
+  const uint4 *pa = reinterpret_cast<const uint4 *>(P.qa.code + growA * P.ldk);
+  const uint4 *pb = reinterpret_cast<const uint4 *>(P.qb.code + growB * P.ldk);
+  // this warp's 16 columns of stage 0 (lane field = the quarter's first lane)
+  const uint32_t tA = tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kAcol +
+                      (uint32_t)(((pw >> 2) & 1) * 32 + hA * 16);
+  uint32_t sB[NBC];
+#pragma unroll
+  for (int i = 0; i < NBC; ++i) sB[i] = smem_s + sw128_offset(rbn, cB0 + i);
+  const int t0A = LG >= 7 ? 64 * hA : 0;
+  const int t0B = LG >= 7 ? 16 * cB0 : 16 * (cB0 & 3);
+  const uint32_t shA = 16u - 16u * (uint32_t)hA;
+  const uint32_t shB = 16u - 16u * (uint32_t)(cB0 >> 2);
+  const uint32_t rep = prm.rep;  // 0x01010101
+  const int prec = P.prec;
+  const int shift = prm.shift_pool;
+  const int nmacro = (int)(P.ldk >> 3);
+  const uint8_t *pc_thr = P.pool_comp + t0B + (LG == 6 ? 64 * (cB0 >> 2) : 0);
+  const int prow_lim = (int)P.ldk;
+  auto prefetch_macro = [&](int prow) {
+    if (lane < G && prow < prow_lim) prefetch_l1(P.pool_comp + (size_t)prow * LPB + 128 * lane);
+  };
+  int pbase = 0;
+  uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
+  prefetch_macro(0);
+#pragma unroll 1
+  for (int mc = 0; mc < nmacro; ++mc) {
+    const uint4 ca = ca_n, cb = cb_n;
+    if (mc + 1 < nmacro) {
+      ca_n = ld_stream_v4(pa + mc + 1);
+      cb_n = ld_stream_v4(pb + mc + 1);
+    }
+    prefetch_macro(pbase + 8);
+    const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int s = j % NS;
+      const uint8_t *pc = pcm + 128 * j;
+      uint4 pcw[NBC];
+#pragma unroll
+      for (int i = 0; i < NBC; ++i) pcw[i] = __ldg(reinterpret_cast<const uint4 *>(pc) + i);
+      const int codeA = LG == 6 ? code_of_rt(ca, j, shA) : code_of(ca, LG == 8 ? (j >> 1) : j);
+      int k = (abs(codeA) * Lg) >> prec;
+      if (LG == 8) k = (j & 1) ? max(k - 128, 0) : min(k, 128);
+      const int kb = k - t0A;  // window end relative to this thread's first byte
+      const uint32_t smA = (uint32_t)(codeA >> 31) | 0x01010101u;
+      const int codeB = LG == 6 ? code_of_rt(cb, j, shB) : code_of(cb, LG == 8 ? (j >> 1) : j);
+      const uint32_t u = (uint32_t)(abs(codeB) >> shift);
+      const uint32_t smB = (uint32_t)(codeB >> 31) | 0x01010101u;
+      const int kbmax = __reduce_max_sync(0xffffffffu, kb);
+      const int kbmin = __reduce_min_sync(0xffffffffu, kb);
+      if (!acquire_at(b, s, st.phase ^ (uint32_t)((j / NS) & 1))) return false;
+      tc_fence_after();
+      // ---- a: 16 words -> 16 TMEM columns of this lane
+      uint32_t v[16];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (kbmax <= 16 * i) {  // warp-uniform: past every window
+          v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = 0u;
+        } else if (kbmin >= 16 * i + 16) {  // warp-uniform: inside every window
+          v[4 * i] = v[4 * i + 1] = v[4 * i + 2] = v[4 * i + 3] = smA;
+        } else {
+          const uint32_t kc = (uint32_t)(kb - 16 * i);
+          v[4 * i + 0] = prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x03020100u), 0u, 0xBA98u) & smA;
+          v[4 * i + 1] = prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x07060504u), 0u, 0xBA98u) & smA;
+          v[4 * i + 2] = prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x0B0A0908u), 0u, 0xBA98u) & smA;
+          v[4 * i + 3] = prmt(mad_u32(kc, rep, 0x7F7F7F7Fu - 0x0F0E0D0Cu), 0u, 0xBA98u) & smA;
+        }
+      }
+      tmem_st16(tA + (uint32_t)(s * Cfg::kAStageCols), v);
+      // ---- b: streams into shared memory
+      const uint32_t soff = (uint32_t)s * Cfg::kStageB;
+#pragma unroll
+      for (int i = 0; i < NBC; ++i) {
+        st_shared_v4(sB[i] + soff,
+                     prmt(mad_u32(u, rep, pcw[i].x), 0u, 0xBA98u) & smB,
+                     prmt(mad_u32(u, rep, pcw[i].y), 0u, 0xBA98u) & smB,
+                     prmt(mad_u32(u, rep, pcw[i].z), 0u, 0xBA98u) & smB,
+                     prmt(mad_u32(u, rep, pcw[i].w), 0u, 0xBA98u) & smB);
+      }
+      // publish: b to the async proxy, the TMEM stores complete, then one
+      // release per warp
+      fence_async_smem();
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.full[s]);
+    }
+    if ((G / NS) & 1) st.phase ^= 1u;
+    pbase += 8;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// e2m1 operands.  {-1, 0, +1} are exact e2m1 values (nibbles 0xA, 0x0, 0x2),
+// so with every block scale 1.0 the kind::mxf4 MMA computes the same bit
+// products as kind::i8 at twice the elements per instruction: a 128-byte
+// stage row carries 256 stream positions.  Nibble i (bits 4i .. 4i + 3) of
+// word w of a row's k-block holds stream position 8 w + i; a and b use the
+// same order, which is all the inner product needs.
+//
+//   a: positions t < k set: word = the sigma pattern (0x22222222 or
+//      0xAAAAAAAA) cut to its low 4 (k - t0) - 32 w bits, one funnel shift
+//      with the shift clamped to [0, 32];
+//   b: [R[d'][t] < u] for the 8 positions of a word from two byte-SWAR
+//      compares against a pool complement whose 8-byte groups hold positions
+//      (0, 2, 4, 6 | 1, 3, 5, 7): even positions land in the low nibbles, odd
+//      ones in the high nibbles, then the sigma pattern masks each nibble.
+__device__ __forceinline__ uint32_t window_word_e2m1(uint32_t pattern, int k4, int w) {
+  return __funnelshift_lc(pattern, 0u, (uint32_t)__viaddmax_s32(k4, -32 * w, 0));
+}
+__device__ __forceinline__ uint32_t stream_word_e2m1(uint32_t u, uint32_t rep, uint32_t pc_even,
+                                                     uint32_t pc_odd, uint32_t pattern) {
+  const uint32_t e = prmt(mad_u32(u, rep, pc_even), 0u, 0xBA98u);
+  const uint32_t o = prmt(mad_u32(u, rep, pc_odd), 0u, 0xBA98u);
+  return ((e & 0x0F0F0F0Fu) | (o & 0xF0F0F0F0u)) & pattern;
+}
+
+// Row producers of the e2m1 CTA pairs (Lp = 128 or 256; a stage = 256 stream
+// positions of 256 a rows and `nb` b rows).  Thread pt owns a row pt % 256
+// (bytes 64 (pt / 256) .. + 63, i.e. 128 positions: with Lp = 128 the whole
+// stream of reduction index 2 j + pt / 256 of k-block j, with Lp = 256 the
+// half pt / 256 of index j) and b row pt % 128 (bytes 32 (pt / 128) .. + 31:
+// 64 positions).  Codes arrive 8 reduction indices per 16-byte load.
+template <int LG, int NS>
+__device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &st,
+                                 uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
+                                 int64_t slice_b, int64_t m0, int64_t n0, int nb) {
+  static_assert(LG == 7 || LG == 8, "e2m1 producers take Lp = 128 or 256");
+  constexpr int G = (8 << LG) / 256;  // k-blocks per macro step of 8 indices: 4 or 8
+  constexpr int LPB = 1 << LG;
+  static_assert(G % NS == 0, "a macro step is a whole number of ring turns");
+  const GemmProblem &P = prm.P;
+  const int pt = threadIdx.x - 32;
+  const int ra = pt & 255;
+  const int hA = pt >> 8;
+  const int rbn = pt & 127;
+  const int cB0 = 2 * (pt >> 7);  // b chunks cB0, cB0 + 1
+  const bool doB = rbn < nb;
+  const int64_t gmA = m0 + ra;
+  const bool vA = gmA < prm.m_rows;
+  const int64_t growA = slice * P.M + (vA ? gmA : prm.m_rows - 1);
+  int Lg = 0;
+  if (vA) {
+    const int L = row_stream_len(P, slice, growA);
+    Lg = L > 0 ? L : 0;
+  }
+  const int64_t gnB = n0 + rbn;
+  const int64_t growB = slice_b * P.N + (gnB < prm.n_rows ? gnB : prm.n_rows - 1);
+  const uint4 *pa = reinterpret_cast<const uint4 *>(P.qa.code + growA * P.ldk);
+  const uint4 *pb = reinterpret_cast<const uint4 *>(P.qb.code + growB * P.ldk);
+  uint32_t sA[4], sB[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sA[i] = smem_s + sw128_offset(ra, 4 * hA + i);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) sB[i] = smem_s + stage_a_bytes + sw128_offset(rbn, cB0 + i);
+  const int t0A = LG == 8 ? 128 * hA : 0;
+  // Lp = 128: k-block j holds indices 2 j (bytes 0-63) and 2 j + 1 (64-127)
+  const uint32_t shA = 16u - 16u * (uint32_t)hA;
+  const uint32_t shB = 16u - 16u * (uint32_t)(cB0 >> 2);
+  const uint32_t rep = prm.rep;
+  const int prec = P.prec;
+  const int shift = prm.shift_pool;
+  const int nmacro = (int)(P.ldk >> 3);
+  // pool complement: k-block j of a macro step starts 256 bytes after j - 1;
+  // this thread's 64 positions are 64 bytes at 32 cB0 into it
+  const uint8_t *pc_thr = P.pool_comp + 32 * cB0;
+  const int prow_lim = (int)P.ldk;
+  auto prefetch_macro = [&](int prow) {
+    if (lane < LPB / 16 && prow < prow_lim)
+      prefetch_l1(P.pool_comp + (size_t)prow * LPB + 128 * lane);
+  };
+  int pbase = 0;
+  uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
+  prefetch_macro(0);
+#pragma unroll 1
+  for (int mc = 0; mc < nmacro; ++mc) {
+    const uint4 ca = ca_n, cb = cb_n;
+    if (mc + 1 < nmacro) {
+      ca_n = ld_stream_v4(pa + mc + 1);
+      cb_n = ld_stream_v4(pb + mc + 1);
+    }
+    prefetch_macro(pbase + 8);
+    const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * j);
+      const uint4 q0 = __ldg(pc), q1 = __ldg(pc + 1), q2 = __ldg(pc + 2), q3 = __ldg(pc + 3);
+      const int codeA = LG == 7 ? code_of_rt(ca, j, shA) : code_of(ca, j);
+      const int k = (abs(codeA) * Lg) >> prec;
+      const int k4 = 4 * (k - t0A);
+      const uint32_t patA = codeA < 0 ? 0xAAAAAAAAu : 0x22222222u;
+      const int codeB = LG == 7 ? code_of_rt(cb, j, shB) : code_of(cb, j);
+      const uint32_t u = (uint32_t)(abs(codeB) >> shift);
+      const uint32_t patB = codeB < 0 ? 0xAAAAAAAAu : 0x22222222u;
+      if (!acquire_at(b, j % NS, st.phase ^ (uint32_t)((j / NS) & 1))) return false;
+      const uint32_t soff = (uint32_t)(j % NS) * prm.stage_bytes;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        st_shared_v4(sA[i] + soff, window_word_e2m1(patA, k4, 4 * i),
+                     window_word_e2m1(patA, k4, 4 * i + 1), window_word_e2m1(patA, k4, 4 * i + 2),
+                     window_word_e2m1(patA, k4, 4 * i + 3));
+      if (doB) {
+        st_shared_v4(sB[0] + soff, stream_word_e2m1(u, rep, q0.x, q0.y, patB),
+                     stream_word_e2m1(u, rep, q0.z, q0.w, patB),
+                     stream_word_e2m1(u, rep, q1.x, q1.y, patB),
+                     stream_word_e2m1(u, rep, q1.z, q1.w, patB));
+        st_shared_v4(sB[1] + soff, stream_word_e2m1(u, rep, q2.x, q2.y, patB),
+                     stream_word_e2m1(u, rep, q2.z, q2.w, patB),
+                     stream_word_e2m1(u, rep, q3.x, q3.y, patB),
+                     stream_word_e2m1(u, rep, q3.z, q3.w, patB));
+      }
+      publish_at(b, j % NS, lane);
+    }
+    if ((G / NS) & 1) st.phase ^= 1u;
+    pbase += 8;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
 // Epilogue: TMEM -> smem transpose -> rescale -> bias -> coalesced stores.
 // The stage ring is idle (every MMA of this tile has completed), so each warp
 // stages its 32x32 blocks there; a producer-only barrier keeps the next
 // tile's operand writes out until all are done.
-template <int BN, bool kSeg, bool kPair = false>
+// kF32: the accumulators hold fp32 counts (e2m1 pairs: exact integers, see
+// gemm_tc_pair_fp4_kernel) in two blocks of prm.ncols columns; columns past
+// prm.ncols are not part of the tile.
+template <int BN, bool kSeg, bool kPair = false, bool kF32 = false>
 __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
                               unsigned char *smem, uint32_t tmem_base, int warp, int lane,
                               int64_t slice, int64_t slice_b, int64_t m0, int64_t n0, int64_t it) {
   const GemmProblem &P = prm.P;
+  const int ncols = kF32 ? prm.ncols : BN;
   if (!mbar_wait(b.tfull, (uint32_t)(st.g & 1), b.abort)) return false;
   tc_fence_after();
   {
@@ -840,6 +1138,7 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
     const int myL = rowp[lane].x;  // stream length of this lane's row
 #pragma unroll 1
     for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
+      if (kF32 && cc * 32 >= ncols) break;  // warp-uniform
       if constexpr (kSeg) {
         // last segment: finished fp32 values (rescaled and summed in order)
 #pragma unroll 1
@@ -852,16 +1151,18 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         }
       } else {
         uint32_t v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * BN + cc * 32),
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * ncols + cc * 32),
                   v);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = __uint_as_float(v[i]);
+        for (int i = 0; i < 32; ++i)  // int32 counts as their bit patterns
+          stg[lane * 33 + i] =
+              kF32 ? __int_as_float(__float2int_rn(__uint_as_float(v[i]))) : __uint_as_float(v[i]);
       }
       __syncwarp();
       // lane = column now
       const int64_t gn = n0 + cc * 32 + lane;
-      const bool col_ok = gn < prm.n_rows;
+      const bool col_ok = gn < prm.n_rows && (!kF32 || cc * 32 + lane < ncols);
       float sb = 0.f;
       int32_t zb = 0, rsb = 0;
       float bias = 0.f;
@@ -1028,6 +1329,119 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       if (!ok) break;
       if (!tile_epilogue<BN, kSeg>(prm, b, st, smem, tmem_base, warp, lane, slice, slice_b, m0, n0,
                                    it))
+        break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemAlloc));
+  }
+  if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
+}
+
+// Narrow-tile kernel with the window operand in TMEM (unsegmented row
+// producers, BN <= 128): warp 0 issues M = 128 x N = BN MMAs whose A is a TMEM
+// stage and whose B is a shared-memory stage; warps 1..16 generate both and
+// run the epilogue.  The whole TMEM (512 columns) is allocated: one CTA per SM.
+template <int BN, int LG>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_ts_kernel(const TcParams prm) {
+  using Cfg = TsCfg<BN>;
+  constexpr uint32_t kTmemAlloc = 512;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars b;
+  b.full = reinterpret_cast<uint64_t *>(smem + Cfg::kRing);
+  b.empty = b.full + kTsStages;
+  b.tfull = b.empty + kTsStages;
+  b.tempty = b.tfull + 1;
+  b.drain = b.tempty + 1;
+  b.epi = b.drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(b.epi + 1);
+  b.abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTsStages; ++s) {
+      mbar_init(&b.full[s], kProducerWarps);
+      mbar_init(&b.empty[s], 1);
+    }
+    mbar_init(b.tfull, 1);
+    mbar_init(b.tempty, kProducers);
+    mbar_init(b.drain, 1);
+    mbar_init(b.epi, kProducers);
+    *b.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemAlloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ================================================= MMA issuer (lane 0)
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8<BN>();
+      const uint32_t smem0 = smem_u32(smem);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t g = 0;
+      for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++g) {
+        if (g > 0) ok = mbar_wait(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
+        if (!ok) break;
+        tc_fence_after();
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b0 = smem0 + stage * Cfg::kStageB;
+          const uint32_t a0 = tmem_base + Cfg::kAcol + (uint32_t)stage * Cfg::kAStageCols;
+#pragma unroll
+          for (int kk = 0; kk < kKB / 32; ++kk) {
+            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)  // 32 bytes of K = 8 columns
+              tc_mma_i8_ts(tmem_base + j * BN, a0 + (uint32_t)(j * 32 + kk * 8), bdesc, idesc,
+                           (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&b.empty[stage]);
+          if (++stage == kTsStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(b.tfull);
+      }
+      // Drain: everything this thread issued has completed before TMEM is freed.
+      tc_commit(b.drain);
+      mbar_wait(b.drain, 0, b.abort);
+    }
+    __syncwarp();
+  } else {
+    // ============================ producers + epilogue (kProducerWarps warps)
+    const uint32_t smem_s = smem_u32(smem);
+    ProdState st{0, 0u, 0};
+    int64_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < prm.tiles; tile += gridDim.x, ++it) {
+      const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
+      const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+      const int64_t m0 = (rem % prm.tiles_m) * kBM;
+      const int64_t n0 = (rem / prm.tiles_m) * BN;
+      const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
+      if (!produce_rows_ts<BN, LG>(prm, b, st, smem_s, tmem_base, warp, lane, slice, slice_b, m0,
+                                   n0))
+        break;
+      if (!tile_epilogue<BN, false>(prm, b, st, smem, tmem_base, warp, lane, slice, slice_b, m0,
+                                    n0, it))
         break;
     }
   }
@@ -1230,6 +1644,189 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
   if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
 }
 
+// ---------------------------------------------------------------------------
+// CTA pairs on e2m1 operands (tcgen05.mma kind::mxf4, block32 scales all 1.0).
+// Same cluster protocol, stage ring and epilogue as gemm_tc_pair_kernel; a
+// stage carries 256 stream positions, the tile is 512 a rows x prm.ncols b
+// rows (ncols <= 240, a multiple of 16: CTA q generates b rows
+// n0 + q ncols / 2 ..), and TMEM holds the two fp32 accumulators in columns
+// [0, 2 ncols) and the E8M0 scale factors (0x7F = 1.0 in every byte) in
+// columns [kFp4SfCol, 512).  Counts stay exact while K * Lp < 2^24.
+constexpr uint32_t kFp4SfCol = 480;
+constexpr int kFp4MaxCols = 240;
+static_assert(2 * kFp4MaxCols <= (int)kFp4SfCol, "accumulators below the scale factors");
+
+__host__ __device__ constexpr uint32_t idesc_mxf4_pair(int n) {
+  return (1u << 7)                       // A format E2M1
+         | (1u << 10)                    // B format E2M1
+         | ((uint32_t)(n >> 3) << 17)    // N >> 3
+         | (1u << 23)                    // scale factors E8M0
+         | ((uint32_t)(256 >> 4) << 24);  // M = 256 (two CTAs); K = 64
+}
+__device__ __forceinline__ void tc_mma_mxf4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t tmem_sfa,
+                                                 uint32_t tmem_sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], "
+      "p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+template <int LG>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_fp4_kernel(const TcParams prm) {
+  constexpr uint32_t kTmemAlloc = 512;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars b;
+  b.full = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStage);
+  b.empty = b.full + kPairStages;
+  b.pfull = b.empty + kPairStages;
+  b.tfull = b.pfull + kPairStages;
+  b.tempty = b.tfull + 1;
+  b.drain = b.tempty + 1;
+  b.epi = b.drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(b.epi + 1);
+  b.abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int ncols = prm.ncols;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&b.full[s], kProducerWarps);
+      mbar_init(&b.empty[s], 1);
+      mbar_init(&b.pfull[s], 1);
+    }
+    mbar_init(b.tfull, 1);
+    mbar_init(b.tempty, 2);
+    mbar_init(b.drain, 1);
+    mbar_init(b.epi, kProducers);
+    *b.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemAlloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // unit scale factors in this CTA's columns [kFp4SfCol, 512), every lane
+  // (warps 1-4 cover the four lane quarters)
+  if (warp >= 1 && warp <= 4) {
+    uint32_t one[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) one[i] = 0x7F7F7F7Fu;
+    const uint32_t t = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + kFp4SfCol;
+    tmem_st16(t, one);
+    tmem_st16(t + 16, one);
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers and scale factors exist before any MMA
+  tc_fence_after();
+  b.pfull_cl = mapa_shared(smem_u32(b.pfull), 0);
+  b.tempty_cl = mapa_shared(smem_u32(b.tempty), 0);
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t nclusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ====================================== MMA issuer (even CTA, lane 0)
+    if (rank == 0 && lane == 0) {
+      const uint32_t smem0 = smem_u32(smem);
+      const uint32_t idesc = idesc_mxf4_pair(ncols);
+      const uint32_t sf = tmem_base + kFp4SfCol;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t g = 0;
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++g) {
+        if (g > 0) ok = mbar_wait_cl(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
+        if (!ok) break;
+        tc_fence_after();
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.full[stage], phase, b.abort) ||
+              !mbar_wait_cl(&b.pfull[stage], phase, b.abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem0 + stage * kPairStage;
+          const uint32_t b0 = a0 + kPairStageA;
+#pragma unroll
+          for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
+            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+              // a and b read their (all-equal) scale factors from the same columns
+              tc_mma_mxf4_pair(tmem_base + (uint32_t)(j * ncols), adesc, bdesc, idesc, sf, sf,
+                               (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit_pair_both(&b.empty[stage]);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair_both(b.tfull);
+      }
+      tc_commit_pair_local(b.drain);
+      mbar_wait_cl(b.drain, 0, b.abort);
+    } else if (rank == 1 && lane == 0) {
+      // ============ forwarder (odd CTA): each filled stage of this CTA is
+      // announced to the MMA thread with one cluster-scope release
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters) {
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
+          mbar_arrive_cluster(b.pfull_cl + 8u * (uint32_t)stage);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ============================ producers + epilogue (kProducerWarps warps)
+    const uint32_t smem_s = smem_u32(smem);
+    ProdState st{0, 0u, 0};
+    int64_t it = 0;
+    const int half = ncols / 2;
+    for (int64_t tile = cluster; tile < prm.tiles; tile += nclusters, ++it) {
+      const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
+      const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+      const int64_t m0 = (rem % prm.tiles_m) * (2 * kBM) + (int64_t)rank * kBM;
+      const int64_t n0 = (rem / prm.tiles_m) * ncols;
+      const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
+      if (!produce_rows_fp4<LG, kPairStages>(prm, b, st, smem_s, kPairStageA, lane, slice,
+                                             slice_b, m0, n0 + (int64_t)rank * half, half))
+        break;
+      if (!tile_epilogue<256, false, true, true>(prm, b, st, smem, tmem_base, warp, lane, slice,
+                                                 slice_b, m0, n0, it))
+        break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while the pair may still touch its memory
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemAlloc));
+  }
+  if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
+}
+
 template <int BN, int kProd, int LG, bool kSeg>
 cudaError_t launch_bn(TcParams prm, int sms, cudaStream_t s) {
   const size_t smem = TcCfg<BN>::smem_bytes(kProd == kProdTable);
@@ -1322,6 +1919,81 @@ cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
   return launch_pair_v<LG, false>(prm, dev, tmap, s);
 }
 
+// b rows per e2m1 pair tile: fewest computed columns with a per-tile cost of
+// 32 columns (epilogue, a rows generated again), the wider tile on ties.
+int fp4_tile_cols(int64_t n_rows) {
+  int best = kFp4MaxCols;
+  int64_t best_cost = -1;
+  for (int nt = kFp4MaxCols; nt >= 128; nt -= 16) {
+    const int64_t cost = ((n_rows + nt - 1) / nt) * (nt + 32);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = nt;
+    }
+  }
+  return best;
+}
+
+template <int LG>
+cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
+  auto kern = gemm_tc_pair_fp4_kernel<LG>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+  if (e != cudaSuccess) return e;
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = kPairStage;
+  prm.ncols = fp4_tile_cols(prm.n_rows);
+  prm.nkb = (prm.P.ldk << LG) / 256;  // 256 stream positions per stage
+  prm.nkb_seg = prm.nkb;
+  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
+  prm.tiles_n = (prm.n_rows + prm.ncols - 1) / prm.ncols;
+  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int max_clusters[64] = {};
+  int clusters = dev >= 0 && dev < 64 ? max_clusters[dev] : 0;
+  if (clusters <= 0) {
+    cfg.gridDim = dim3(2, 1, 1);
+    if ((e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg)) != cudaSuccess) return e;
+    if (clusters <= 0) return cudaErrorInvalidConfiguration;
+    if (dev >= 0 && dev < 64) max_clusters[dev] = clusters;
+  }
+  const int64_t grid = prm.tiles < clusters ? prm.tiles : clusters;
+  cfg.gridDim = dim3((unsigned)(2 * grid), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, prm);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <int BN, int LG>
+cudaError_t launch_ts_lg(TcParams prm, int sms, cudaStream_t s) {
+  const size_t smem = TsCfg<BN>::smem_bytes;
+  auto kern = gemm_tc_ts_kernel<BN, LG>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = TsCfg<BN>::kStageB;
+  const int64_t grid = prm.tiles < sms ? prm.tiles : sms;
+  kern<<<(unsigned)grid, kThreads, smem, s>>>(prm);
+  return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_ts(const TcParams &prm, int sms, cudaStream_t s) {
+  if (prm.lp_log2 == 6) return launch_ts_lg<BN, 6>(prm, sms, s);
+  if (prm.lp_log2 == 7) return launch_ts_lg<BN, 7>(prm, sms, s);
+  return launch_ts_lg<BN, 8>(prm, sms, s);
+}
+
 template <int BN, bool kSeg>
 cudaError_t launch_rows(const TcParams &prm, int sms, cudaStream_t s) {
   if (prm.lp_log2 == 6) return launch_bn<BN, kProdRows, 6, kSeg>(prm, sms, s);
@@ -1394,6 +2066,15 @@ bool tc_row_producers(const GemmProblem &P) {
 
 int tc_block_n(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
 
+// The e2m1 CTA pairs take what the int8 pairs would (row producers, one K
+// segment, wide b, more than one a tile) at Lp = 128 / 256 with counts below
+// 2^24 (exact in fp32), unless b comes prepacked as int8 bytes.
+bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows) {
+  const int lg = padded_stream_log2(P);
+  return tc_row_producers(P) && P.nseg == 1 && (lg == 7 || lg == 8) && m_rows > kBM &&
+         tc_block_n(n_rows) == 256 && P.b_streams == nullptr && (P.ldk << lg) < (1LL << 24);
+}
+
 int tc_tile_n(const GemmProblem &P, int64_t N) {
   const int bn = tc_block_n(N);
   return (P.nseg > 1 && bn > 128) ? 128 : bn;
@@ -1426,6 +2107,10 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   if (tc_row_producers(P)) {
     // pairs pay off only with two a tiles per pair (one accumulator per CTA
     // would generate as many rows per MAC as a single CTA)
+    if (tc_nibble_pairs(P, m_rows, n_rows)) {
+      if (lg == 7) return launch_pair_fp4<7>(prm, dev, s);
+      return launch_pair_fp4<8>(prm, dev, s);
+    }
     if (P.nseg == 1 && bn == 256 && m_rows > kBM) {
       if (lg == 6) return launch_pair<6>(prm, dev, s);
       if (lg == 7) return launch_pair<7>(prm, dev, s);
@@ -1435,8 +2120,9 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
       if (bn == 64) return launch_rows<64, true>(prm, sms, s);
       return launch_rows<128, true>(prm, sms, s);
     }
-    if (bn == 64) return launch_rows<64, false>(prm, sms, s);
-    if (bn == 128) return launch_rows<128, false>(prm, sms, s);
+    // narrow tiles: the window operand goes through TMEM, not shared memory
+    if (bn == 64) return launch_ts<64>(prm, sms, s);
+    if (bn == 128) return launch_ts<128>(prm, sms, s);
     return launch_rows<256, false>(prm, sms, s);
   }
   if (P.nseg > 1) {

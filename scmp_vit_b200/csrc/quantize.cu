@@ -260,12 +260,14 @@ __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_d
 // stream bits.
 __global__ void pool_complement_kernel(const uint8_t *__restrict__ pool, int pool_dims,
                                        int64_t rows, int prec, int lp_log2, int shift,
-                                       uint8_t *__restrict__ out) {
+                                       int nibble_pairs, uint8_t *__restrict__ out) {
   const int64_t bytes = rows << lp_log2;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t d = i >> lp_log2;
-    const int64_t t = i & ((1 << lp_log2) - 1);
+    const int64_t slot = i & ((1 << lp_log2) - 1);
+    // group slot j < 4 holds position 2 j, slot j >= 4 position 2 (j - 4) + 1
+    const int64_t t = nibble_pairs ? (slot & ~7) + (((slot & 3) << 1) | ((slot >> 2) & 1)) : slot;
     out[i] = d < pool_dims ? (uint8_t)(0x7F - (pool[(d << prec) + t] >> shift)) : (uint8_t)0x7F;
   }
 }
@@ -393,12 +395,13 @@ cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, ui
 }
 
 cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t rows, int prec,
-                                   int lp_log2, int shift, uint8_t *out, cudaStream_t s) {
+                                   int lp_log2, int shift, bool nibble_pairs, uint8_t *out,
+                                   cudaStream_t s) {
   if (rows < pool_dims) rows = pool_dims;
   const int64_t bytes = rows << lp_log2;
   const int64_t blocks = (bytes + 255) / 256;
   pool_complement_kernel<<<(unsigned)(blocks < 296 ? blocks : 296), 256, 0, s>>>(
-      pool, pool_dims, rows, prec, lp_log2, shift, out);
+      pool, pool_dims, rows, prec, lp_log2, shift, nibble_pairs ? 1 : 0, out);
   return cudaGetLastError();
 }
 

@@ -108,9 +108,11 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
 // PC over max(pool_dims, rows) rows of 2^lp_log2 bytes (rows past the pool
-// hold 0x7F)
+// hold 0x7F).  nibble_pairs: each 8-byte group holds stream positions
+// (0, 2, 4, 6, 1, 3, 5, 7) of its 8 (the e2m1 producers' order).
 cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t rows, int prec,
-                                   int lp_log2, int shift, uint8_t *out, cudaStream_t s);
+                                   int lp_log2, int shift, bool nibble_pairs, uint8_t *out,
+                                   cudaStream_t s);
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 // b operand bytes of every row and k-block at Lp = 2^prec, as the row
 // producers would generate them: out[n][k-block][128]
@@ -124,6 +126,9 @@ int tc_tile_n(const GemmProblem &P, int64_t N);
 bool tc_row_producers(const GemmProblem &P);
 // log2 of the padded stream length Lp the tensor-core engine uses
 int tc_stream_log2(const GemmProblem &P);
+// true when launch_gemm_tc runs the e2m1 CTA-pair kernel on this window (its
+// pool complement is laid out with nibble_pairs)
+bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows);
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
                            unsigned int *error, cudaStream_t s);
 

@@ -1,0 +1,126 @@
+"""Parity of the e2m1 CTA-pair kernel (tcgen05.mma kind::mxf4 with unit block
+scales) against the oracle.
+
+The engine routes a problem there when it would otherwise run the int8 CTA
+pairs at Lp = 128 or 256: row producers, one K segment, more than 256 rows of
+a and more than 128 rows of b.  Counts must be bit-exact (the fp32
+accumulators hold integers below 2^24) and the rescaled outputs within 1e-5
+relative, exactly as on the int8 path.  Shapes cover every tile width the
+column heuristic picks (128 .. 240 b rows per tile), ragged a and b tails,
+early termination, Lp = 256 with the shifted p = 8 compare, per-row stream
+lengths, unipolar codes, batched slices, bias and bf16 output.
+"""
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sc_oracle
+from scmp_vit_b200 import _lib
+from scmp_vit_b200 import config_helpers as ch
+from scmp_vit_b200 import sc_matmul
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-5
+
+
+def _run(dev, a, b, p, L, *, mode="bipolar", granularity="per_row", bias=None, rowL=None,
+         out_dtype=None):
+    random.seed(p * 977 + L)
+    K = a.shape[-1]
+    cfg = ch.make_sobol_simple_config(K, K, p)
+    BH = a.shape[0] if a.dim() == 3 else 1
+    M, N = a.shape[-2], b.shape[-2]
+    acc = torch.empty(BH * M * N, dtype=torch.int32, device=dev)
+    kw = {}
+    if rowL is not None:
+        kw["row_stoc_len"] = torch.from_numpy(rowL)
+    y = sc_matmul(a.to(dev), b.to(dev), granularity=granularity, mode=mode, sc_prec=p,
+                  config=cfg, stoc_len=L, acc_out=acc, engine="tcgen05",
+                  bias=None if bias is None else bias.to(dev), out_dtype=out_dtype, **kw)
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    acc_ref, y_ref = sc_oracle.sc_matmul_ref(
+        a.numpy(), b.numpy(), granularity=granularity, mode=mode, sc_prec=p, pool=cfg["table"],
+        stoc_len=L, bias=None if bias is None else bias.numpy(), L_row=rowL)
+    np.testing.assert_array_equal(acc.view(BH, M, N).cpu().numpy(), acc_ref)
+    return y.reshape(BH, M, N).float().cpu().numpy(), y_ref
+
+
+@pytest.mark.parametrize("M,N,K,p,L", [
+    (512, 256, 64, 7, 128),     # one pair tile, 240-wide: the last 16 b rows in a second tile
+    (300, 300, 64, 7, 128),     # 160-wide tiles, odd CTA's a rows mostly past the end
+    (1024, 1024, 32, 7, 128),   # 208-wide tiles, last one partly past N
+    (600, 3072, 16, 7, 128),    # 240-wide tiles (13 per row of tiles)
+    (520, 400, 40, 7, 100),     # early termination inside Lp = 128, ragged everything
+    (512, 272, 24, 8, 256),     # Lp = 256 (p = 8: shifted compare), 2 positions per half-row
+    (768, 384, 40, 8, 200),     # Lp = 256 with early termination
+    (513, 257, 72, 7, 128),     # 257th a row and b column on the CUDA-core strips
+    (4096, 2560, 16, 7, 128),   # many tiles per cluster
+    (600, 640, 257, 7, 128),    # K = 257: codes padded to 264
+])
+def test_fp4_pair_shapes(cuda_device, M, N, K, p, L):
+    g = torch.Generator().manual_seed(M * 7 + N * 3 + K)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    y, y_ref = _run(cuda_device, a, b, p, L)
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_pair_row_stream_lengths(cuda_device):
+    """Per-row stream lengths (the MP split): windows k = |c| L_m >> p."""
+    g = torch.Generator().manual_seed(11)
+    M, N, K, p = 640, 320, 48, 7
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.1
+    rowL = np.random.default_rng(3).choice(np.array([16, 64, 100, 128], np.int32), size=M)
+    y, y_ref = _run(cuda_device, a, b, p, 128, rowL=rowL)
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_pair_unipolar(cuda_device):
+    g = torch.Generator().manual_seed(12)
+    a = torch.rand(600, 40, generator=g)
+    b = torch.rand(288, 40, generator=g)
+    y, y_ref = _run(cuda_device, a, b, 7, 128, mode="unipolar")
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_pair_sign_patterns(cuda_device):
+    """Rows and columns whose codes are all negative, all positive or zero:
+    every nibble value (0x0, 0x2, 0xA) in both operands."""
+    g = torch.Generator().manual_seed(13)
+    M, N, K = 520, 300, 32
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    a[:64] = -a[:64].abs()
+    a[64:128] = a[64:128].abs()
+    a[128:140] = 0.0
+    b[:40] = -b[:40].abs()
+    b[40:80] = 0.0
+    y, y_ref = _run(cuda_device, a, b, 7, 128)
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_pair_batched_bias_bf16(cuda_device):
+    """Batched slices with a shared b (a weight), bias and bf16 output: the
+    bf16 result is the fp32 result rounded to nearest even."""
+    g = torch.Generator().manual_seed(14)
+    a = torch.randn(3, 300, 64, generator=g)
+    b = torch.randn(400, 64, generator=g) * 0.05
+    bias = torch.randn(400, generator=g)
+    y, y_ref = _run(cuda_device, a, b, 7, 128, bias=bias, out_dtype=torch.bfloat16)
+    ref_bf16 = torch.from_numpy(y_ref.astype(np.float32)).to(torch.bfloat16).float().numpy()
+    np.testing.assert_allclose(y, ref_bf16, rtol=1e-2, atol=1e-2)
+    y32, y_ref32 = _run(cuda_device, a, b, 7, 128, bias=bias)
+    np.testing.assert_allclose(y32, y_ref32, rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_pair_batched_per_slice_b(cuda_device):
+    """Batched a and b (batch_b = batch), as Q @ K^T per head at M > 256."""
+    g = torch.Generator().manual_seed(15)
+    a = torch.randn(2, 520, 64, generator=g)
+    b = torch.randn(2, 300, 64, generator=g)
+    y, y_ref = _run(cuda_device, a, b, 7, 128, granularity="per_head")
+    np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
