@@ -178,22 +178,27 @@ int check_packable(const scmp_matmul_args *x) {
 
 // Layout of a prepacked b buffer (offsets from its base): the b operand
 // (group stats, int16 codes [N][ldk], per-row scale / zero / row sum), the
-// pool complement at row stride 2^p, and the operand bytes [N][ldk * 2^p].
+// pool complement at row stride 2^p, and the operand bytes: e2m1 nibbles
+// [N][ldk * 2^p / 2] for the e2m1 CTA pairs (2^p = 128 or 256, N > 128, counts
+// below 2^24), else int8 bytes [N][ldk * 2^p].
 struct PackPlan {
   OperandLayout B;
   size_t pool_comp = 0, streams = 0, total = 0;
   int64_t ldk = 0, pool_rows = 0;
+  bool e2m1 = false;
 };
 
 PackPlan make_pack_plan(const scmp_matmul_args *x) {
   PackPlan p;
   Carver c;
   p.ldk = (x->K + 7) / 8 * 8;
+  p.e2m1 = (x->sc_prec == 7 || x->sc_prec == 8) && x->N > 128 &&
+           (p.ldk << x->sc_prec) < ((int64_t)1 << 24);
   p.B.g = make_groups(x->granularity, 1, x->N, x->group_b);
   layout_operand(c, p.B, x->K, p.ldk);
   p.pool_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
   p.pool_comp = c.take((size_t)p.pool_rows << x->sc_prec);
-  p.streams = c.take((size_t)x->N * (size_t)(p.ldk << x->sc_prec));
+  p.streams = c.take((size_t)x->N * (size_t)(p.ldk << x->sc_prec) >> (p.e2m1 ? 1 : 0));
   p.total = c.off;
   return p;
 }
@@ -310,7 +315,8 @@ int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_byt
                                   false, pb + pk.pool_comp, s)) != cudaSuccess)
     return cuda_fail(e, "pool_complement launch");
   if ((e = launch_pack_b_streams(reinterpret_cast<const int16_t *>(pb + pk.B.code), x.N, pk.ldk,
-                                 x.sc_prec, shift, pb + pk.pool_comp, pb + pk.streams, s)) !=
+                                 x.sc_prec, shift, pk.e2m1, pb + pk.pool_comp, pb + pk.streams,
+                                 s)) !=
       cudaSuccess)
     return cuda_fail(e, "pack_b_streams launch");
   count_launches(2);
@@ -358,6 +364,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
     auto *pb = static_cast<unsigned char *>(const_cast<void *>(x.b));
     P.qb = plane_of(pk.B, pb);
     P.b_streams = pb + pk.streams;
+    P.b_e2m1 = pk.e2m1 ? 1 : 0;
   } else {
     P.qb = plane_of(plan.B, ws);
   }

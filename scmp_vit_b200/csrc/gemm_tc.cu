@@ -1000,7 +1000,8 @@ __device__ __forceinline__ uint32_t stream_word_e2m1(uint32_t u, uint32_t rep, u
 // stream of reduction index 2 j + pt / 256 of k-block j, with Lp = 256 the
 // half pt / 256 of index j) and b row pt % 128 (bytes 32 (pt / 128) .. + 31:
 // 64 positions).  Codes arrive 8 reduction indices per 16-byte load.
-template <int LG, int NS>
+// kNoB: b arrives by TMA from a prepacked buffer; only the a rows are generated.
+template <int LG, int NS, bool kNoB>
 __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &st,
                                  uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
                                  int64_t slice_b, int64_t m0, int64_t n0, int nb) {
@@ -1049,21 +1050,30 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
       prefetch_l1(P.pool_comp + (size_t)prow * LPB + 128 * lane);
   };
   int pbase = 0;
-  uint4 ca_n = ld_stream_v4(pa), cb_n = ld_stream_v4(pb);
-  prefetch_macro(0);
+  uint4 ca_n = ld_stream_v4(pa), cb_n = make_uint4(0, 0, 0, 0);
+  if constexpr (!kNoB) {
+    cb_n = ld_stream_v4(pb);
+    prefetch_macro(0);
+  }
 #pragma unroll 1
   for (int mc = 0; mc < nmacro; ++mc) {
     const uint4 ca = ca_n, cb = cb_n;
     if (mc + 1 < nmacro) {
       ca_n = ld_stream_v4(pa + mc + 1);
-      cb_n = ld_stream_v4(pb + mc + 1);
+      if constexpr (!kNoB) cb_n = ld_stream_v4(pb + mc + 1);
     }
-    prefetch_macro(pbase + 8);
+    if constexpr (!kNoB) prefetch_macro(pbase + 8);
     const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * j);
-      const uint4 q0 = __ldg(pc), q1 = __ldg(pc + 1), q2 = __ldg(pc + 2), q3 = __ldg(pc + 3);
+      uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0, q2 = q0, q3 = q0;
+      if constexpr (!kNoB) {
+        q0 = __ldg(pc);
+        q1 = __ldg(pc + 1);
+        q2 = __ldg(pc + 2);
+        q3 = __ldg(pc + 3);
+      }
       const int codeA = LG == 7 ? code_of_rt(ca, j, shA) : code_of(ca, j);
       const int k = (abs(codeA) * Lg) >> prec;
       const int k4 = 4 * (k - t0A);
@@ -1078,7 +1088,7 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
         st_shared_v4(sA[i] + soff, window_word_e2m1(patA, k4, 4 * i),
                      window_word_e2m1(patA, k4, 4 * i + 1), window_word_e2m1(patA, k4, 4 * i + 2),
                      window_word_e2m1(patA, k4, 4 * i + 3));
-      if (doB) {
+      if (!kNoB && doB) {
         st_shared_v4(sB[0] + soff, stream_word_e2m1(u, rep, q0.x, q0.y, patB),
                      stream_word_e2m1(u, rep, q0.z, q0.w, patB),
                      stream_word_e2m1(u, rep, q1.x, q1.y, patB),
@@ -1674,8 +1684,12 @@ __device__ __forceinline__ void tc_mma_mxf4_pair(uint32_t tmem_d, uint64_t adesc
       : "memory");
 }
 
-template <int LG>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_fp4_kernel(const TcParams prm) {
+// With kPackedB the b halves come from a prepacked e2m1 buffer by TMA: warp
+// kTmaWarp loads this CTA's ncols / 2 b rows of each stage and the producers
+// generate only the a rows.
+template <int LG, bool kPackedB>
+__global__ void __launch_bounds__(kThreads + 32, 1)
+    gemm_tc_pair_fp4_kernel(const TcParams prm, const __grid_constant__ CUtensorMap tmap) {
   constexpr uint32_t kTmemAlloc = 512;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
@@ -1698,7 +1712,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_fp4_kernel(const TcP
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&b.full[s], kProducerWarps);
+      // this CTA's producer warps (+ the TMA thread's expect_tx arrival)
+      mbar_init(&b.full[s], kProducerWarps + (kPackedB ? 1 : 0));
       mbar_init(&b.empty[s], 1);
       mbar_init(&b.pfull[s], 1);
     }
@@ -1796,6 +1811,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_fp4_kernel(const TcP
       }
     }
     __syncwarp();
+  } else if (kPackedB && warp == kTmaWarp) {
+    // ========================== b loader (lane 0): prepacked rows by TMA
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+      const uint32_t smem0 = smem_u32(smem);
+      const uint32_t bytes = (uint32_t)(ncols / 2) * kKB;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t it = 0;
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++it) {
+        const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+        const int nb0 = (int)((rem / prm.tiles_m) * ncols + (int64_t)rank * (ncols / 2));
+        // the previous tile's epilogue stages its transpose in the ring
+        if (it > 0 && !mbar_wait(b.epi, (uint32_t)((it - 1) & 1), b.abort)) break;
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.empty[stage], phase ^ 1, b.abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(&b.full[stage], bytes);
+          tma_load_2d(smem0 + stage * kPairStage + kPairStageA, &tmap, (int)(kb * kKB), nb0,
+                      &b.full[stage]);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
   } else {
     // ============================ producers + epilogue (kProducerWarps warps)
     const uint32_t smem_s = smem_u32(smem);
@@ -1808,8 +1848,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_pair_fp4_kernel(const TcP
       const int64_t m0 = (rem % prm.tiles_m) * (2 * kBM) + (int64_t)rank * kBM;
       const int64_t n0 = (rem / prm.tiles_m) * ncols;
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
-      if (!produce_rows_fp4<LG, kPairStages>(prm, b, st, smem_s, kPairStageA, lane, slice,
-                                             slice_b, m0, n0 + (int64_t)rank * half, half))
+      if (!produce_rows_fp4<LG, kPairStages, kPackedB>(prm, b, st, smem_s, kPairStageA, lane,
+                                                       slice, slice_b, m0,
+                                                       n0 + (int64_t)rank * half, half))
         break;
       if (!tile_epilogue<256, false, true, true>(prm, b, st, smem, tmem_base, warp, lane, slice,
                                                  slice_b, m0, n0, it))
@@ -1900,7 +1941,7 @@ cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
   // prepacked b (bytes laid out at Lp = 2^prec) serves calls whose padded
   // stream length is the full 2^prec
   const GemmProblem &P = prm.P;
-  if (P.b_streams && P.batch_b == 1 && LG == P.prec) {
+  if (P.b_streams && !P.b_e2m1 && P.batch_b == 1 && LG == P.prec) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (enc) {
       const cuuint64_t row_bytes = (cuuint64_t)(P.ldk << LG);
@@ -1934,27 +1975,20 @@ int fp4_tile_cols(int64_t n_rows) {
   return best;
 }
 
-template <int LG>
-cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
-  auto kern = gemm_tc_pair_fp4_kernel<LG>;
+template <int LG, bool kPackedB>
+cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &tmap,
+                              cudaStream_t s) {
+  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
   if (e != cudaSuccess) return e;
-  prm.rep = 0x01010101u;
-  prm.stage_bytes = kPairStage;
-  prm.ncols = fp4_tile_cols(prm.n_rows);
-  prm.nkb = (prm.P.ldk << LG) / 256;  // 256 stream positions per stage
-  prm.nkb_seg = prm.nkb;
-  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
-  prm.tiles_n = (prm.n_rows + prm.ncols - 1) / prm.ncols;
-  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kThreads + (kPackedB ? 32 : 0), 1, 1);
   cfg.dynamicSmemBytes = kPairSmem;
   cfg.stream = s;
   cfg.attrs = attr;
@@ -1969,9 +2003,43 @@ cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
   }
   const int64_t grid = prm.tiles < clusters ? prm.tiles : clusters;
   cfg.gridDim = dim3((unsigned)(2 * grid), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, prm);
+  e = cudaLaunchKernelEx(&cfg, kern, prm, tmap);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+template <int LG>
+cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = kPairStage;
+  prm.ncols = fp4_tile_cols(prm.n_rows);
+  prm.nkb = (prm.P.ldk << LG) / 256;  // 256 stream positions per stage
+  prm.nkb_seg = prm.nkb;
+  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
+  prm.tiles_n = (prm.n_rows + prm.ncols - 1) / prm.ncols;
+  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
+  CUtensorMap tmap;
+  memset(&tmap, 0, sizeof(tmap));
+  // prepacked e2m1 b (positions laid out at Lp = 2^prec) serves calls whose
+  // padded stream length is the full 2^prec
+  const GemmProblem &P = prm.P;
+  if (P.b_streams && P.b_e2m1 && P.batch_b == 1 && LG == P.prec) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc) {
+      const cuuint64_t row_bytes = (cuuint64_t)((P.ldk << LG) / 2);
+      cuuint64_t gdim[2] = {row_bytes, (cuuint64_t)P.N};
+      cuuint64_t gstride[1] = {row_bytes};
+      cuuint32_t box[2] = {(cuuint32_t)kKB, (cuuint32_t)(prm.ncols / 2)};
+      cuuint32_t estride[2] = {1u, 1u};
+      const CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                             const_cast<uint8_t *>(P.b_streams), gdim, gstride, box, estride,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r == CUDA_SUCCESS) return launch_pair_fp4_v<LG, true>(prm, dev, tmap, s);
+    }
+    // no encoder or a rejected map: generate b from the packed codes instead
+  }
+  return launch_pair_fp4_v<LG, false>(prm, dev, tmap, s);
 }
 
 template <int BN, int LG>
@@ -2068,11 +2136,14 @@ int tc_block_n(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
 
 // The e2m1 CTA pairs take what the int8 pairs would (row producers, one K
 // segment, wide b, more than one a tile) at Lp = 128 / 256 with counts below
-// 2^24 (exact in fp32), unless b comes prepacked as int8 bytes.
+// 2^24 (exact in fp32), unless b comes prepacked as int8 bytes (prepacked
+// e2m1 bytes are loaded by TMA when Lp = 2^prec, else b is generated from the
+// packed codes).
 bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows) {
   const int lg = padded_stream_log2(P);
   return tc_row_producers(P) && P.nseg == 1 && (lg == 7 || lg == 8) && m_rows > kBM &&
-         tc_block_n(n_rows) == 256 && P.b_streams == nullptr && (P.ldk << lg) < (1LL << 24);
+         tc_block_n(n_rows) == 256 && (P.b_streams == nullptr || P.b_e2m1) &&
+         (P.ldk << lg) < (1LL << 24);
 }
 
 int tc_tile_n(const GemmProblem &P, int64_t N) {

@@ -309,17 +309,58 @@ __global__ void pack_b_streams_kernel(const int16_t *__restrict__ code, int64_t 
   }
 }
 
+// e2m1 form: one thread per 16 output bytes = 32 positions of one reduction
+// index.  Nibble i of word w is position 8 w + i; each nibble is
+// sigma * [R >> shift < u] as 0x2 (+1), 0xA (-1) or 0x0, formed as the e2m1
+// pair producers form it from even / odd position complements.
+__global__ void pack_b_streams_e2m1_kernel(const int16_t *__restrict__ code, int64_t N,
+                                           int64_t ldk, int prec, int shift,
+                                           const uint8_t *__restrict__ pool_comp,
+                                           uint8_t *__restrict__ out) {
+  const int64_t row_bytes = (ldk << prec) >> 1;
+  const int64_t per_row = row_bytes >> 4;
+  const int64_t total = N * per_row;
+  const int64_t tmask = (1 << prec) - 1;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / per_row;
+    const int64_t pos = (i % per_row) << 5;  // first of 32 positions
+    const int64_t d = pos >> prec;
+    const int c = code[n * ldk + d];
+    const uint32_t u = (uint32_t)(abs(c) >> shift);
+    const uint32_t pat = c < 0 ? 0xAAAAAAAAu : 0x22222222u;
+    const uint4 *pc = reinterpret_cast<const uint4 *>(pool_comp + (d << prec) + (pos & tmask));
+    const uint4 p0 = pc[0], p1 = pc[1];
+    const uint32_t w8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    uint32_t r[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      uint32_t ev, od;  // complements of positions 8g + {0, 2, 4, 6} / {1, 3, 5, 7}
+      asm("prmt.b32 %0, %1, %2, 0x6420;" : "=r"(ev) : "r"(w8[2 * g]), "r"(w8[2 * g + 1]));
+      asm("prmt.b32 %0, %1, %2, 0x7531;" : "=r"(od) : "r"(w8[2 * g]), "r"(w8[2 * g + 1]));
+      const uint32_t e = prmt_sign(u * 0x01010101u + ev);
+      const uint32_t o = prmt_sign(u * 0x01010101u + od);
+      r[g] = ((e & 0x0F0F0F0Fu) | (o & 0xF0F0F0F0u)) & pat;
+    }
+    *reinterpret_cast<uint4 *>(out + n * row_bytes + (pos >> 1)) = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, int prec,
-                                  int shift, const uint8_t *pool_comp, uint8_t *out,
+                                  int shift, bool e2m1, const uint8_t *pool_comp, uint8_t *out,
                                   cudaStream_t s) {
-  const int64_t total = N * ((ldk << prec) >> 4);
+  const int64_t total = N * ((ldk << prec) >> (e2m1 ? 5 : 4));
   if (total == 0) return cudaSuccess;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift, pool_comp,
-                                                         out);
+  if (e2m1)
+    pack_b_streams_e2m1_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift,
+                                                                pool_comp, out);
+  else
+    pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift, pool_comp,
+                                                           out);
   return cudaGetLastError();
 }
 

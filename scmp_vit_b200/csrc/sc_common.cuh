@@ -59,8 +59,10 @@ struct GemmProblem {
   // pool complement PC[pool_dims][2^p] = 0x7F - (R >> shift) (tensor-core
   // row producers; shift = 1 for bipolar p = 8, else 0)
   const uint8_t *pool_comp;
-  // prepacked b operand bytes [N][ldk * 2^p] (nullable; batch_b = 1)
+  // prepacked b operand bytes (nullable; batch_b = 1): int8 [N][ldk * 2^p],
+  // or with b_e2m1 e2m1 nibbles [N][ldk * 2^p / 2] (the e2m1 pair order)
   const uint8_t *b_streams;
+  int b_e2m1;
   // window of (a row, b row) pairs per slice this launch computes
   int64_t m_lo, m_hi, n_lo, n_hi;
 };
@@ -115,9 +117,11 @@ cudaError_t launch_pool_complement(const uint8_t *pool, int pool_dims, int64_t r
                                    cudaStream_t s);
 cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 // b operand bytes of every row and k-block at Lp = 2^prec, as the row
-// producers would generate them: out[n][k-block][128]
+// producers would generate them: out[n][k-block][128].  e2m1: nibbles in the
+// e2m1 pair producers' order, 256 positions per 128 bytes (pool_comp is the
+// natural-order complement either way).
 cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, int prec,
-                                  int shift, const uint8_t *pool_comp, uint8_t *out,
+                                  int shift, bool e2m1, const uint8_t *pool_comp, uint8_t *out,
                                   cudaStream_t s);
 bool tc_supported(const GemmProblem &P);
 int tc_block_n(int64_t N);

@@ -263,26 +263,34 @@ def _sc_linear_mp(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int, mod
     return result.to(x.dtype).reshape(*orig_shape[:-1], D_out)
 
 
-_PREPACK = False
+_PREPACK = None  # None: automatic (see set_weight_prepack)
 
 
-def set_weight_prepack(enabled: bool) -> None:
+def set_weight_prepack(enabled) -> None:
     """Whether ``SCLinear`` keeps its weight's SC operand bytes expanded once
     (``sc.prepack_b``) instead of regenerating them in every call.  Results
-    are bit-identical either way; prepacking costs about ``N * K * 2**p``
-    bytes of device memory per layer and is redone when the weight changes.
-    Off by default: on B200 the large-N kernel is bound by shared-memory
-    traffic (operand stores + MMA reads), which a TMA-fed b does not reduce,
-    so the packed path measures the same speed (qkv_proj 16.36 vs 16.34 ms)."""
+    are bit-identical either way; the cache is rebuilt when the weight
+    changes.  ``None`` (the default) prepacks where it pays on B200: p = 7 or
+    8 with more than 128 output features, whose packed bytes are e2m1 nibbles
+    (``N * K * 2**p / 2`` bytes per layer) that the e2m1 CTA-pair kernel loads
+    by TMA so that its producers generate only the activation windows
+    (qkv_proj at 256 images: 11.7 -> 9.6 ms).  The int8 form (p = 5 / 6, or
+    N <= 128) does not pay (the int8 kernel is bound by shared-memory traffic,
+    which a TMA-fed b does not reduce), so automatic mode leaves it off;
+    ``True`` / ``False`` force it on / off."""
     global _PREPACK
-    _PREPACK = bool(enabled)
+    _PREPACK = None if enabled is None else bool(enabled)
 
 
 def _prepack_applies(weight: torch.Tensor, sc_prec: int, mode: str, stoc_len, chunk_d: int) -> bool:
     from . import sc as _sc
-    return (_PREPACK and not USE_NOISE_MODEL and weight.is_cuda and chunk_d == 0
-            and 5 <= sc_prec <= 8 and not (mode == "unipolar" and sc_prec == 8)
-            and stoc_len in (None, 1 << sc_prec) and _sc._DEFAULT_ENGINE != "popc")
+    if _PREPACK is False or USE_NOISE_MODEL or not weight.is_cuda or chunk_d != 0:
+        return False
+    if not (5 <= sc_prec <= 8) or (mode == "unipolar" and sc_prec == 8):
+        return False
+    if stoc_len not in (None, 1 << sc_prec) or _sc._DEFAULT_ENGINE == "popc":
+        return False
+    return _PREPACK is True or (sc_prec in (7, 8) and weight.shape[0] > 128)
 
 
 class SCLinear(nn.Module):

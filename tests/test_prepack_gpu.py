@@ -1,8 +1,9 @@
 """Prepacked weights (scmp_prepack_b / sc.prepack_b) on the engine (B200).
 
 A prepacked b must give exactly what the weight itself gives: the same
-popcount sums and the same outputs, on the CTA-pair kernel that loads the
-packed bytes with TMA (including b tiles past the last weight row), on the
+popcount sums and the same outputs, on the CTA-pair kernels that load the
+packed bytes with TMA (int8 bytes, or e2m1 nibbles for p = 7 / 8; including
+b tiles past the last weight row), on the
 single-CTA and CUDA-core paths that read the packed codes, and through
 SCLinear's cache (rebuilt when the weight changes in place).
 """
@@ -48,6 +49,11 @@ def _same(dev, a, w, p, L=None, mode="bipolar", granularity="per_row", bias=None
     (700, 260, 72, 6, None),     # Lp = 64
     (600, 384, 256, 7, 64),      # shorter stream: Lp 64 != 2^p, codes path
     (200, 384, 128, 7, None),    # one a tile: single-CTA kernel on the packed codes
+    # e2m1 packed bytes (p = 7 / 8, N > 128) by TMA at the tile widths the
+    # pair kernel picks: 208 b rows (104-row boxes), 240 (120-row boxes)
+    (600, 1024, 64, 7, None),
+    (520, 3072, 32, 7, None),
+    (700, 520, 48, 8, 256),
 ])
 def test_prepacked_equals_weight(cuda_device, M, N, K, p, L):
     g = torch.Generator().manual_seed(M + N + K)
@@ -99,6 +105,6 @@ def test_sclinear_cache_follows_the_weight(cuda_device):
         scl.set_weight_prepack(False)
         torch.testing.assert_close(y2, m(x), rtol=0, atol=0)
     finally:
-        scl.set_weight_prepack(False)
+        scl.set_weight_prepack(None)
     torch.cuda.synchronize()
     assert _lib.engine_status(reset=True) == 0
