@@ -179,42 +179,54 @@ def int8_tensor_peak(dev) -> float:
     return 2.0 * n ** 3 / best
 
 
-# DRAM bytes (read + write) of one qkv_proj pair-kernel launch per image, from
-# the ncu capture of 64 images (profiles/gemm_tc_pair_vit_l14_qkv_b64.md:
-# 292.2 MB + 145.9 MB); traffic grows with the a rows, i.e. per image.
-QKV_DRAM_BYTES_PER_IMAGE = (292.2e6 + 145.9e6) / 64
+# DRAM bytes (read + write) of one qkv_proj e2m1 pair-kernel launch per image
+# (prepacked weight), from the ncu capture of 64 images
+# (profiles/gemm_tc_pair_fp4_vit_l14_qkv_b64.md); traffic grows with the a
+# rows, i.e. per image.
+QKV_DRAM_BYTES_PER_IMAGE = (585.3e6 + 77.1e6) / 64
+QKV_DRAM_SOURCE = ("ncu dram__bytes_read+write of the e2m1 pair kernel at 64 images, "
+                   "scaled per image")
 
 
-def _tensor_peak_alt() -> dict:
-    """int8 denominator from the driver's measured bf16 GEMM rate (x2: the
-    tensor cores run int8 at twice the bf16 rate), or the recipe's fallback."""
+def _tensor_peak_alt(mult: int) -> dict:
+    """Tensor-core denominator from the driver's measured bf16 GEMM rate
+    (x2 for int8, x4 for e2m1: the dense rates are 2x / 4x bf16), or the
+    recipe's fallback."""
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             bf16 = float(json.load(f)["bf16_tflops"])
-        return {"value": 2 * bf16, "source": "of measured: MEASURED_PEAKS.json bf16_tflops x2"}
+        return {"value": mult * bf16,
+                "source": f"of measured: MEASURED_PEAKS.json bf16_tflops x{mult}"}
     except (OSError, KeyError, ValueError, TypeError):
-        return {"value": 2 * 1590.0, "source": "of fallback: 1.59 PFLOP/s bf16 x2"}
+        return {"value": mult * 1590.0, "source": f"of fallback: 1.59 PFLOP/s bf16 x{mult}"}
 
 
-def roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops, images=None) -> dict:
+def roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops, images=None,
+             e2m1=False) -> dict:
     """Roofline of the dominant kernel (the qkv_proj SC matmul).  One SC
-    bit-product = one int8 multiply-add on the tensor-core engine (2 ops) and
-    one counted AND bit on the CUDA-core engine."""
+    bit-product = one multiply-add on the tensor-core engine (2 ops: int8,
+    or e2m1 with unit block scales on the e2m1 CTA pairs, whose dense rate is
+    twice int8's) and one counted AND bit on the CUDA-core engine."""
     base = {"kernel": "sc_matmul qkv_proj", "per_launch_ms": qkv_ms,
             "algorithmic_per_launch": qkv_bitops, "algorithmic_unit": "bit-products",
             "traffic": (QKV_DRAM_BYTES_PER_IMAGE * images) if (images and on_tc) else None,
-            "traffic_source": "ncu dram__bytes_read+write of the pair kernel at 64 images, "
-                              "scaled per image",
+            "traffic_source": QKV_DRAM_SOURCE,
             "int_pipe_peak_tbitops": peak_popc / 1e12,
             "x_int_pipe_roofline": (achieved / peak_popc) if achieved else None}
     if on_tc:
-        base.update({"bound": "tensor", "engine": "tcgen05 kind::i8",
+        mult = 2 if e2m1 else 1
+        base.update({"bound": "tensor",
+                     "engine": ("tcgen05 kind::mxf4 (e2m1 operands, unit block scales), "
+                                "prepacked weight by TMA") if e2m1 else "tcgen05 kind::i8",
                      "achieved": 2 * achieved / 1e12 if achieved else None,
-                     "peak": peak_i8 / 1e12, "unit": "TOP/s (int8)",
-                     "frac": (2 * achieved / peak_i8) if achieved else None,
-                     "peak_source": "measured cuBLAS int8 GEMM 8192^3 (torch._int_mm), best of 10"})
-        alt = _tensor_peak_alt()
+                     "peak": mult * peak_i8 / 1e12,
+                     "unit": "TOP/s (e2m1)" if e2m1 else "TOP/s (int8)",
+                     "frac": (2 * achieved / (mult * peak_i8)) if achieved else None,
+                     "peak_source": ("2 x " if e2m1 else "") +
+                                    "measured cuBLAS int8 GEMM 8192^3 (torch._int_mm), best of 10"
+                                    + (" (dense e2m1 = 2 x int8 rate)" if e2m1 else "")})
+        alt = _tensor_peak_alt(4 if e2m1 else 2)
         if achieved:
             alt["frac"] = 2 * achieved / 1e12 / alt["value"]
         base["peak_alt_tops"] = alt
@@ -432,6 +444,8 @@ def main():
     peak_popc = _lib.probe_int_peak(0)
     peak_i8 = int8_tensor_peak(dev)
     on_tc = args.engine in ("auto", "tcgen05") and 5 <= WORKLOADS[args.config]["sc_prec"] <= 8
+    # qkv_proj runs on the e2m1 CTA pairs at p = 7 / 8 (Lp = 128 / 256)
+    e2m1 = on_tc and WORKLOADS[args.config]["sc_prec"] in (7, 8)
 
     # end to end: pinned host images in, logits out, through the public API
     e2e = None
@@ -473,7 +487,7 @@ def main():
             "e2e": e2e,
             "gpu_launches": int(launches),
             "roofline": roofline(on_tc, achieved, peak_i8, peak_popc, qkv_ms, qkv_bitops,
-                                 images=bl),
+                                 images=bl, e2m1=e2m1),
             "ms_per_step_split": split,
             "cpu_baseline": cpu,
             "clocks": clk,
