@@ -815,8 +815,8 @@ __device__ bool produce_rows(const TcParams &prm, const Bars &b, ProdState &st, 
 // then kTsStages stages of 64 columns: half h (a rows 128 h .. + 127, one per
 // lane) at +32 h, its 128 bytes of k-block as 32 columns of 4 int8 each.
 constexpr int kTsStages = 4;
-constexpr uint32_t kEpiStagingBytes =
-    kProducerWarps * 32 * 33 * 4 + kProducerWarps * 32 * 16;  // tile_epilogue's transpose + rows
+constexpr uint32_t kEpiStagingBytes =  // tile_epilogue's transpose, row records, row factors
+    kProducerWarps * 32 * 33 * 4 + kProducerWarps * 32 * 16 + kProducerWarps * 32 * 4;
 
 template <int BN>
 struct TsCfg {
@@ -998,24 +998,35 @@ __device__ __forceinline__ uint32_t stream_word_e2m1(uint32_t u, uint32_t rep, u
 // positions of 256 a rows and `nb` b rows).  Thread pt owns a row pt % 256
 // (bytes 64 (pt / 256) .. + 63, i.e. 128 positions: with Lp = 128 the whole
 // stream of reduction index 2 j + pt / 256 of k-block j, with Lp = 256 the
-// half pt / 256 of index j) and b row pt % 128 (bytes 32 (pt / 128) .. + 31:
-// 64 positions).  Codes arrive 8 reduction indices per 16-byte load.
+// half pt / 256 of index j) and, for pt < 4 nb, b row pt % nb (bytes
+// 32 (pt / nb) .. + 31: 64 positions).  Codes arrive 8 reduction indices per
+// 16-byte load.
 // kNoB: b arrives by TMA from a prepacked buffer; only the a rows are generated.
-template <int LG, int NS, bool kNoB>
+// kOneAcc: 128 a rows per CTA (one accumulator); thread pt owns a row pt % 128
+// and its bytes 32 (pt / 128) .. + 31 (64 positions), like its b row.
+template <int LG, int NS, bool kNoB, bool kOneAcc>
 __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &st,
                                  uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
                                  int64_t slice_b, int64_t m0, int64_t n0, int nb) {
   static_assert(LG == 7 || LG == 8, "e2m1 producers take Lp = 128 or 256");
   constexpr int G = (8 << LG) / 256;  // k-blocks per macro step of 8 indices: 4 or 8
   constexpr int LPB = 1 << LG;
-  static_assert(G % NS == 0, "a macro step is a whole number of ring turns");
+  constexpr int RA = kOneAcc ? 128 : 256;  // a rows per CTA
+  constexpr int NCA = kOneAcc ? 2 : 4;     // a chunks (16 bytes) per thread
+  // a macro step that is a whole number of ring turns starts at stage 0:
+  // stage and phase of each k-block are then known at compile time
+  constexpr bool kStatic = (G % NS) == 0;
   const GemmProblem &P = prm.P;
   const int pt = threadIdx.x - 32;
-  const int ra = pt & 255;
-  const int hA = pt >> 8;
-  const int rbn = pt & 127;
-  const int cB0 = 2 * (pt >> 7);  // b chunks cB0, cB0 + 1
-  const bool doB = rbn < nb;
+  const int ra = pt & (RA - 1);
+  const int cA0 = NCA * (pt / RA);  // a chunks cA0 .. cA0 + NCA - 1
+  const int hA = cA0 >> 2;          // Lp = 128: index 2 j + hA of k-block j
+  // b: nb rows x 4 chunk pairs = 4 nb tasks over threads 0 .. 4 nb - 1, rows
+  // fastest, so a narrow b side (Attn@V: 32 rows per CTA) is spread over
+  // warps of all four SM sub-partitions instead of one
+  const bool doB = pt < 4 * nb;
+  const int rbn = doB ? pt % nb : 0;
+  const int cB0 = doB ? 2 * (pt / nb) : 0;  // b chunks cB0, cB0 + 1
   const int64_t gmA = m0 + ra;
   const bool vA = gmA < prm.m_rows;
   const int64_t growA = slice * P.M + (vA ? gmA : prm.m_rows - 1);
@@ -1028,12 +1039,13 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
   const int64_t growB = slice_b * P.N + (gnB < prm.n_rows ? gnB : prm.n_rows - 1);
   const uint4 *pa = reinterpret_cast<const uint4 *>(P.qa.code + growA * P.ldk);
   const uint4 *pb = reinterpret_cast<const uint4 *>(P.qb.code + growB * P.ldk);
-  uint32_t sA[4], sB[2];
+  uint32_t sA[NCA], sB[2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) sA[i] = smem_s + sw128_offset(ra, 4 * hA + i);
+  for (int i = 0; i < NCA; ++i) sA[i] = smem_s + sw128_offset(ra, cA0 + i);
 #pragma unroll
   for (int i = 0; i < 2; ++i) sB[i] = smem_s + stage_a_bytes + sw128_offset(rbn, cB0 + i);
-  const int t0A = LG == 8 ? 128 * hA : 0;
+  // first position of this thread's a bytes inside its reduction index
+  const int t0A = LG == 8 ? 32 * cA0 : 32 * (cA0 & 3);
   // Lp = 128: k-block j holds indices 2 j (bytes 0-63) and 2 j + 1 (64-127)
   const uint32_t shA = 16u - 16u * (uint32_t)hA;
   const uint32_t shB = 16u - 16u * (uint32_t)(cB0 >> 2);
@@ -1052,7 +1064,7 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
   int pbase = 0;
   uint4 ca_n = ld_stream_v4(pa), cb_n = make_uint4(0, 0, 0, 0);
   if constexpr (!kNoB) {
-    cb_n = ld_stream_v4(pb);
+    if (doB) cb_n = ld_stream_v4(pb);
     prefetch_macro(0);
   }
 #pragma unroll 1
@@ -1060,7 +1072,7 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
     const uint4 ca = ca_n, cb = cb_n;
     if (mc + 1 < nmacro) {
       ca_n = ld_stream_v4(pa + mc + 1);
-      if constexpr (!kNoB) cb_n = ld_stream_v4(pb + mc + 1);
+      if (!kNoB && doB) cb_n = ld_stream_v4(pb + mc + 1);
     }
     if constexpr (!kNoB) prefetch_macro(pbase + 8);
     const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
@@ -1068,7 +1080,7 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
     for (int j = 0; j < G; ++j) {
       const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * j);
       uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0, q2 = q0, q3 = q0;
-      if constexpr (!kNoB) {
+      if (!kNoB && doB) {
         q0 = __ldg(pc);
         q1 = __ldg(pc + 1);
         q2 = __ldg(pc + 2);
@@ -1081,10 +1093,16 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
       const int codeB = LG == 7 ? code_of_rt(cb, j, shB) : code_of(cb, j);
       const uint32_t u = (uint32_t)(abs(codeB) >> shift);
       const uint32_t patB = codeB < 0 ? 0xAAAAAAAAu : 0x22222222u;
-      if (!acquire_at(b, j % NS, st.phase ^ (uint32_t)((j / NS) & 1))) return false;
-      const uint32_t soff = (uint32_t)(j % NS) * prm.stage_bytes;
+      uint32_t soff;
+      if constexpr (kStatic) {
+        if (!acquire_at(b, j % NS, st.phase ^ (uint32_t)((j / NS) & 1))) return false;
+        soff = (uint32_t)(j % NS) * prm.stage_bytes;
+      } else {
+        if (!acquire_stage(b, st, lane)) return false;
+        soff = mad_u32((uint32_t)st.stage, prm.stage_bytes, 0u);
+      }
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < NCA; ++i)
         st_shared_v4(sA[i] + soff, window_word_e2m1(patA, k4, 4 * i),
                      window_word_e2m1(patA, k4, 4 * i + 1), window_word_e2m1(patA, k4, 4 * i + 2),
                      window_word_e2m1(patA, k4, 4 * i + 3));
@@ -1098,9 +1116,14 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
                      stream_word_e2m1(u, rep, q3.x, q3.y, patB),
                      stream_word_e2m1(u, rep, q3.z, q3.w, patB));
       }
-      publish_at(b, j % NS, lane);
+      if constexpr (kStatic)
+        publish_at(b, j % NS, lane);
+      else
+        publish_stage<NS>(b, st, lane);
     }
-    if ((G / NS) & 1) st.phase ^= 1u;
+    if constexpr (kStatic) {
+      if ((G / NS) & 1) st.phase ^= 1u;
+    }
     pbase += 8;
   }
   return true;
@@ -1113,11 +1136,14 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
 // tile's operand writes out until all are done.
 // kF32: the accumulators hold fp32 counts (e2m1 pairs: exact integers, see
 // gemm_tc_pair_fp4_kernel) in two blocks of prm.ncols columns; columns past
-// prm.ncols are not part of the tile.
-template <int BN, bool kSeg, bool kPair = false, bool kF32 = false>
+// prm.ncols are not part of the tile.  kOneAcc: one accumulator of 128 a rows
+// (lanes) x prm.ncols columns; warp pw takes the 32-column chunks pw / 4,
+// pw / 4 + 4, ...
+template <int BN, bool kSeg, bool kPair = false, bool kF32 = false, bool kOneAcc = false>
 __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
                               unsigned char *smem, uint32_t tmem_base, int warp, int lane,
                               int64_t slice, int64_t slice_b, int64_t m0, int64_t n0, int64_t it) {
+  static_assert(!kOneAcc || kF32, "one-accumulator tiles are e2m1 pair tiles");
   const GemmProblem &P = prm.P;
   const int ncols = kF32 ? prm.ncols : BN;
   if (!mbar_wait(b.tfull, (uint32_t)(st.g & 1), b.abort)) return false;
@@ -1125,10 +1151,15 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
   {
     const int pw = warp - 1;                 // producer warp 0..15
     const int quarter = warp & 3;            // TMEM lanes this warp may access
-    const int acc_j = (pw >> 2) & 1;         // accumulator (a rows 0-127 / 128-255)
+    const int acc_j = kOneAcc ? 0 : (pw >> 2) & 1;  // accumulator (a rows 0-127 / 128-255)
     const int col_half = pw >> 3;            // which half of the BN columns
+    const int cc_begin = kOneAcc ? (pw >> 2) : col_half * (BN / 64);
+    const int cc_end = kOneAcc ? (ncols + 31) / 32 : (col_half + 1) * (BN / 64);
+    const int cc_step = kOneAcc ? 4 : 1;
     float *stg = reinterpret_cast<float *>(smem) + pw * (32 * 33);
     int4 *rowp = reinterpret_cast<int4 *>(smem + kProducerWarps * 32 * 33 * 4) + pw * 32;
+    float *rowF = reinterpret_cast<float *>(smem + kProducerWarps * 32 * 33 * 4 +
+                                            kProducerWarps * 32 * 16) + pw * 32;
     const int64_t mrow0 = m0 + acc_j * 128 + quarter * 32;  // first row of this warp
     {
       const int64_t gm = mrow0 + lane;
@@ -1142,12 +1173,13 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         rsa = P.qa.rowsum[grow];
       }
       rowp[lane] = make_int4(L, __float_as_int(sa), za, rsa);
+      rowF[lane] = L > 0 ? sc_rescale_factor(P.mode, P.prec, L) : 0.0f;
     }
     __syncwarp();
     const int64_t grow0 = slice * P.M + mrow0;
     const int myL = rowp[lane].x;  // stream length of this lane's row
 #pragma unroll 1
-    for (int cc = col_half * (BN / 64); cc < (col_half + 1) * (BN / 64); ++cc) {
+    for (int cc = cc_begin; cc < cc_end; cc += cc_step) {
       if (kF32 && cc * 32 >= ncols) break;  // warp-uniform
       if constexpr (kSeg) {
         // last segment: finished fp32 values (rescaled and summed in order)
@@ -1192,7 +1224,7 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         if constexpr (kSeg) {
           if (rp.x > 0) y = stg[r * 33 + lane];
         } else if (rp.x > 0) {
-          y = sc_rescale(P.mode, P.prec, rp.x, a, P.K, __int_as_float(rp.y), rp.z, rp.w, sb, zb,
+          y = sc_rescale_f(P.mode, rowF[r], a, P.K, __int_as_float(rp.y), rp.z, rp.w, sb, zb,
                          rsb);
         }
         if (P.bias) y = __fadd_rn(y, bias);
@@ -1687,18 +1719,35 @@ __device__ __forceinline__ void tc_mma_mxf4_pair(uint32_t tmem_d, uint64_t adesc
 // With kPackedB the b halves come from a prepacked e2m1 buffer by TMA: warp
 // kTmaWarp loads this CTA's ncols / 2 b rows of each stage and the producers
 // generate only the a rows.
-template <int LG, bool kPackedB>
+//
+// kOneAcc: 256-row tiles (128 a rows per CTA, one accumulator of ncols <= 256
+// columns, M = 256 MMAs once per 64 positions); stages are 32 KB.  Taken when
+// one 512-row tile would be half empty or the b side is narrow (Q@K^T and
+// Attn@V per head: 256 x 256 and 256 x 64).
+template <bool kOneAcc>
+struct Fp4PairCfg {
+  static constexpr uint32_t kStageA = (kOneAcc ? 128 : 256) * kKB;
+  static constexpr uint32_t kStage = kStageA + kPairStageB;
+  // four stages either way (six 32 KB stages measured no faster on Q@K^T)
+  static constexpr int kStages = kPairStages;
+  static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 /*align*/ + 256;
+  static_assert(kStages * kStage >= kEpiStagingBytes, "the ring holds the epilogue staging");
+};
+
+template <int LG, bool kPackedB, bool kOneAcc>
 __global__ void __launch_bounds__(kThreads + 32, 1)
     gemm_tc_pair_fp4_kernel(const TcParams prm, const __grid_constant__ CUtensorMap tmap) {
+  using Cfg = Fp4PairCfg<kOneAcc>;
   constexpr uint32_t kTmemAlloc = 512;
+  constexpr int kAcc = kOneAcc ? 1 : 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars b;
-  b.full = reinterpret_cast<uint64_t *>(smem + kPairStages * kPairStage);
-  b.empty = b.full + kPairStages;
-  b.pfull = b.empty + kPairStages;
-  b.tfull = b.pfull + kPairStages;
+  b.full = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStage);
+  b.empty = b.full + Cfg::kStages;
+  b.pfull = b.empty + Cfg::kStages;
+  b.tfull = b.pfull + Cfg::kStages;
   b.tempty = b.tfull + 1;
   b.drain = b.tempty + 1;
   b.epi = b.drain + 1;
@@ -1711,7 +1760,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
   const int ncols = prm.ncols;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
       // this CTA's producer warps (+ the TMA thread's expect_tx arrival)
       mbar_init(&b.full[s], kProducerWarps + (kPackedB ? 1 : 0));
       mbar_init(&b.empty[s], 1);
@@ -1775,13 +1824,13 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem0 + stage * kPairStage;
-          const uint32_t b0 = a0 + kPairStageA;
+          const uint32_t a0 = smem0 + stage * Cfg::kStage;
+          const uint32_t b0 = a0 + Cfg::kStageA;
 #pragma unroll
           for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
             const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
+            for (int j = 0; j < kAcc; ++j) {
               const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
               // a and b read their (all-equal) scale factors from the same columns
               tc_mma_mxf4_pair(tmem_base + (uint32_t)(j * ncols), adesc, bdesc, idesc, sf, sf,
@@ -1789,7 +1838,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
           }
           tc_commit_pair_both(&b.empty[stage]);
-          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
         tc_commit_pair_both(b.tfull);
@@ -1806,7 +1855,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         for (int64_t kb = 0; kb < prm.nkb; ++kb) {
           if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
           mbar_arrive_cluster(b.pfull_cl + 8u * (uint32_t)stage);
-          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
         }
       }
     }
@@ -1829,9 +1878,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         for (int64_t kb = 0; kb < prm.nkb; ++kb) {
           if (!mbar_wait(&b.empty[stage], phase ^ 1, b.abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&b.full[stage], bytes);
-          tma_load_2d(smem0 + stage * kPairStage + kPairStageA, &tmap, (int)(kb * kKB), nb0,
+          tma_load_2d(smem0 + stage * Cfg::kStage + Cfg::kStageA, &tmap, (int)(kb * kKB), nb0,
                       &b.full[stage]);
-          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
         }
       }
     }
@@ -1845,15 +1894,16 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     for (int64_t tile = cluster; tile < prm.tiles; tile += nclusters, ++it) {
       const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
       const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
-      const int64_t m0 = (rem % prm.tiles_m) * (2 * kBM) + (int64_t)rank * kBM;
+      constexpr int64_t kRowsA = kOneAcc ? 128 : 256;  // a rows per CTA
+      const int64_t m0 = (rem % prm.tiles_m) * (2 * kRowsA) + (int64_t)rank * kRowsA;
       const int64_t n0 = (rem / prm.tiles_m) * ncols;
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
-      if (!produce_rows_fp4<LG, kPairStages, kPackedB>(prm, b, st, smem_s, kPairStageA, lane,
-                                                       slice, slice_b, m0,
-                                                       n0 + (int64_t)rank * half, half))
+      if (!produce_rows_fp4<LG, Cfg::kStages, kPackedB, kOneAcc>(
+              prm, b, st, smem_s, Cfg::kStageA, lane, slice, slice_b, m0,
+              n0 + (int64_t)rank * half, half))
         break;
-      if (!tile_epilogue<256, false, true, true>(prm, b, st, smem, tmem_base, warp, lane, slice,
-                                                 slice_b, m0, n0, it))
+      if (!tile_epilogue<256, false, true, true, kOneAcc>(prm, b, st, smem, tmem_base, warp, lane,
+                                                          slice, slice_b, m0, n0, it))
         break;
     }
   }
@@ -1863,6 +1913,161 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemAlloc));
+  }
+  if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
+}
+
+// ---------------------------------------------------------------------------
+// Narrow e2m1 tiles on one CTA (N <= 128, e.g. Attn@V per head): 256 a rows as
+// two M = 128 accumulators x BN columns (fp32) in TMEM columns [0, 2 BN), the
+// unit scale factors at kFp4SfCol, kind::mxf4 MMAs of cta_group::1.  With the
+// b side this narrow a CTA pair would only split its few b rows, while each
+// stage's fixed costs (barriers, the cross-CTA hop) would be paid on half the
+// a rows; here a stage carries 256 a rows x 256 positions.
+template <int BN>
+struct Fp4NarrowCfg {
+  static constexpr uint32_t kStageA = kBM * kKB;  // 32 KB
+  static constexpr uint32_t kStage = kStageA + BN * kKB;
+  static constexpr int kStages = 4;
+  static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 /*align*/ + 256;
+  static_assert(kStages * kStage >= kEpiStagingBytes, "the ring holds the epilogue staging");
+  static_assert(2 * BN <= (int)kFp4SfCol, "accumulators below the scale factors");
+};
+
+__host__ __device__ constexpr uint32_t idesc_mxf4_m128(int n) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t tmem_sf, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%5], "
+      "p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sf)
+      : "memory");
+}
+
+template <int BN, int LG>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const TcParams prm) {
+  using Cfg = Fp4NarrowCfg<BN>;
+  constexpr uint32_t kTmemAlloc = 512;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars b;
+  b.full = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStage);
+  b.empty = b.full + Cfg::kStages;
+  b.tfull = b.empty + Cfg::kStages;
+  b.tempty = b.tfull + 1;
+  b.drain = b.tempty + 1;
+  b.epi = b.drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(b.epi + 1);
+  b.abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&b.full[s], kProducerWarps);
+      mbar_init(&b.empty[s], 1);
+    }
+    mbar_init(b.tfull, 1);
+    mbar_init(b.tempty, kProducers);
+    mbar_init(b.drain, 1);
+    mbar_init(b.epi, kProducers);
+    *b.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemAlloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // unit scale factors in columns [kFp4SfCol, 512) of every lane
+  if (warp >= 1 && warp <= 4) {
+    uint32_t one[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) one[i] = 0x7F7F7F7Fu;
+    const uint32_t t = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + kFp4SfCol;
+    tmem_st16(t, one);
+    tmem_st16(t + 16, one);
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    // ================================================= MMA issuer (lane 0)
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_mxf4_m128(BN);
+      const uint32_t smem0 = smem_u32(smem);
+      const uint32_t sf = tmem_base + kFp4SfCol;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t g = 0;
+      for (int64_t tile = blockIdx.x; tile < prm.tiles && ok; tile += gridDim.x, ++g) {
+        if (g > 0) ok = mbar_wait(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
+        if (!ok) break;
+        tc_fence_after();
+        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+          if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem0 + stage * Cfg::kStage;
+          const uint32_t b0 = a0 + Cfg::kStageA;
+#pragma unroll
+          for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
+            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+              tc_mma_mxf4(tmem_base + (uint32_t)(j * BN), adesc, bdesc, idesc, sf,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit(&b.empty[stage]);
+          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(b.tfull);
+      }
+      tc_commit(b.drain);
+      mbar_wait(b.drain, 0, b.abort);
+    }
+    __syncwarp();
+  } else {
+    // ============================ producers + epilogue (kProducerWarps warps)
+    const uint32_t smem_s = smem_u32(smem);
+    ProdState st{0, 0u, 0};
+    int64_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < prm.tiles; tile += gridDim.x, ++it) {
+      const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
+      const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+      const int64_t m0 = (rem % prm.tiles_m) * kBM;
+      const int64_t n0 = (rem / prm.tiles_m) * BN;
+      const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
+      if (!produce_rows_fp4<LG, Cfg::kStages, false, false>(prm, b, st, smem_s, Cfg::kStageA,
+                                                             lane, slice, slice_b, m0, n0, BN))
+        break;
+      if (!tile_epilogue<BN, false, false, true>(prm, b, st, smem, tmem_base, warp, lane, slice,
+                                                 slice_b, m0, n0, it))
+        break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kTmemAlloc));
   }
   if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
@@ -1961,11 +2166,15 @@ cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
 }
 
 // b rows per e2m1 pair tile: fewest computed columns with a per-tile cost of
-// 32 columns (epilogue, a rows generated again), the wider tile on ties.
-int fp4_tile_cols(int64_t n_rows) {
-  int best = kFp4MaxCols;
+// 32 columns (epilogue, a rows generated again), the wider tile on ties.  One
+// accumulator leaves room for 256 columns; a b side that fits one tile is
+// taken whole (a multiple of 16, at least 16: the M = 256 MMA's N).
+int fp4_tile_cols(int64_t n_rows, bool one_acc) {
+  const int max_cols = one_acc ? 256 : kFp4MaxCols;
+  if (n_rows <= max_cols) return n_rows <= 16 ? 16 : (int)((n_rows + 15) / 16 * 16);
+  int best = max_cols;
   int64_t best_cost = -1;
-  for (int nt = kFp4MaxCols; nt >= 128; nt -= 16) {
+  for (int nt = max_cols; nt >= 128; nt -= 16) {
     const int64_t cost = ((n_rows + nt - 1) / nt) * (nt + 32);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
@@ -1975,12 +2184,13 @@ int fp4_tile_cols(int64_t n_rows) {
   return best;
 }
 
-template <int LG, bool kPackedB>
+template <int LG, bool kPackedB, bool kOneAcc>
 cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &tmap,
                               cudaStream_t s) {
-  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB>;
+  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB, kOneAcc>;
+  constexpr size_t kSmem = Fp4PairCfg<kOneAcc>::kSmem;
   cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -1989,7 +2199,7 @@ cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &t
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(kThreads + (kPackedB ? 32 : 0), 1, 1);
-  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -2008,14 +2218,15 @@ cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &t
   return cudaGetLastError();
 }
 
-template <int LG>
+template <int LG, bool kOneAcc>
 cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
   prm.rep = 0x01010101u;
-  prm.stage_bytes = kPairStage;
-  prm.ncols = fp4_tile_cols(prm.n_rows);
+  prm.stage_bytes = Fp4PairCfg<kOneAcc>::kStage;
+  prm.ncols = fp4_tile_cols(prm.n_rows, kOneAcc);
   prm.nkb = (prm.P.ldk << LG) / 256;  // 256 stream positions per stage
   prm.nkb_seg = prm.nkb;
-  prm.tiles_m = (prm.m_rows + 2 * kBM - 1) / (2 * kBM);
+  const int64_t rows_tile = kOneAcc ? 256 : 2 * kBM;
+  prm.tiles_m = (prm.m_rows + rows_tile - 1) / rows_tile;
   prm.tiles_n = (prm.n_rows + prm.ncols - 1) / prm.ncols;
   prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
   CUtensorMap tmap;
@@ -2035,11 +2246,34 @@ cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
                              const_cast<uint8_t *>(P.b_streams), gdim, gstride, box, estride,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-      if (r == CUDA_SUCCESS) return launch_pair_fp4_v<LG, true>(prm, dev, tmap, s);
+      if (r == CUDA_SUCCESS) return launch_pair_fp4_v<LG, true, kOneAcc>(prm, dev, tmap, s);
     }
     // no encoder or a rejected map: generate b from the packed codes instead
   }
-  return launch_pair_fp4_v<LG, false>(prm, dev, tmap, s);
+  return launch_pair_fp4_v<LG, false, kOneAcc>(prm, dev, tmap, s);
+}
+
+template <int BN, int LG>
+cudaError_t launch_fp4_narrow_lg(TcParams prm, int sms, cudaStream_t s) {
+  using Cfg = Fp4NarrowCfg<BN>;
+  auto kern = gemm_tc_fp4_narrow_kernel<BN, LG>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+  if (e != cudaSuccess) return e;
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = Cfg::kStage;
+  prm.ncols = BN;
+  prm.nkb = (prm.P.ldk << LG) / 256;  // 256 stream positions per stage
+  prm.nkb_seg = prm.nkb;
+  const int64_t grid = prm.tiles < sms ? prm.tiles : sms;
+  kern<<<(unsigned)grid, kThreads, Cfg::kSmem, s>>>(prm);
+  return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_fp4_narrow(const TcParams &prm, int sms, cudaStream_t s) {
+  if (prm.lp_log2 == 7) return launch_fp4_narrow_lg<BN, 7>(prm, sms, s);
+  return launch_fp4_narrow_lg<BN, 8>(prm, sms, s);
 }
 
 template <int BN, int LG>
@@ -2134,16 +2368,16 @@ bool tc_row_producers(const GemmProblem &P) {
 
 int tc_block_n(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
 
-// The e2m1 CTA pairs take what the int8 pairs would (row producers, one K
-// segment, wide b, more than one a tile) at Lp = 128 / 256 with counts below
-// 2^24 (exact in fp32), unless b comes prepacked as int8 bytes (prepacked
-// e2m1 bytes are loaded by TMA when Lp = 2^prec, else b is generated from the
-// packed codes).
+// The e2m1 CTA pairs take every row-producer problem with one K segment at
+// Lp = 128 / 256 whose counts stay below 2^24 (exact in fp32), unless b comes
+// prepacked as int8 bytes (prepacked e2m1 bytes are loaded by TMA when
+// Lp = 2^prec, else b is generated from the packed codes).
 bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows) {
+  (void)m_rows;
+  (void)n_rows;
   const int lg = padded_stream_log2(P);
-  return tc_row_producers(P) && P.nseg == 1 && (lg == 7 || lg == 8) && m_rows > kBM &&
-         tc_block_n(n_rows) == 256 && (P.b_streams == nullptr || P.b_e2m1) &&
-         (P.ldk << lg) < (1LL << 24);
+  return tc_row_producers(P) && P.nseg == 1 && (lg == 7 || lg == 8) &&
+         (P.b_streams == nullptr || P.b_e2m1) && (P.ldk << lg) < (1LL << 24);
 }
 
 int tc_tile_n(const GemmProblem &P, int64_t N) {
@@ -2179,8 +2413,16 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
     // pairs pay off only with two a tiles per pair (one accumulator per CTA
     // would generate as many rows per MAC as a single CTA)
     if (tc_nibble_pairs(P, m_rows, n_rows)) {
-      if (lg == 7) return launch_pair_fp4<7>(prm, dev, s);
-      return launch_pair_fp4<8>(prm, dev, s);
+      // narrow b on one CTA (prepacked int8-free b is generated from codes)
+      if (n_rows <= 128) {
+        if (bn == 64) return launch_fp4_narrow<64>(prm, sms, s);
+        return launch_fp4_narrow<128>(prm, sms, s);
+      }
+      // two accumulators (512-row tiles) when both sides are wide
+      const bool two = m_rows > kBM && n_rows > 128;
+      if (lg == 7) return two ? launch_pair_fp4<7, false>(prm, dev, s)
+                              : launch_pair_fp4<7, true>(prm, dev, s);
+      return two ? launch_pair_fp4<8, false>(prm, dev, s) : launch_pair_fp4<8, true>(prm, dev, s);
     }
     if (P.nseg == 1 && bn == 256 && m_rows > kBM) {
       if (lg == 6) return launch_pair<6>(prm, dev, s);

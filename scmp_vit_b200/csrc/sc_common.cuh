@@ -82,11 +82,15 @@ __device__ __forceinline__ void store_out(const GemmProblem &P, int64_t o, float
     static_cast<float *>(P.out)[o] = y;
 }
 
-// Rescale of one accumulator (bit-exact restatement of oracle/sc_oracle.c).
-__device__ __forceinline__ float sc_rescale(int mode, int prec, int L, int32_t acc, int64_t K,
-                                            float sa, int32_t za, int32_t rsa, float sb,
-                                            int32_t zb, int32_t rsb) {
-  const float F = __fdiv_rn((float)(1u << (2 * prec)), (float)((mode == SCMP_BIPOLAR ? 4 : 1) * L));
+// Rescale of one accumulator (bit-exact restatement of oracle/sc_oracle.c):
+// F = 2^(2p) / (u L) depends on the row only, so epilogues compute it once per
+// row (sc_rescale_factor) and apply it per element (sc_rescale_f).
+__device__ __forceinline__ float sc_rescale_factor(int mode, int prec, int L) {
+  return __fdiv_rn((float)(1u << (2 * prec)), (float)((mode == SCMP_BIPOLAR ? 4 : 1) * L));
+}
+__device__ __forceinline__ float sc_rescale_f(int mode, float F, int32_t acc, int64_t K, float sa,
+                                              int32_t za, int32_t rsa, float sb, int32_t zb,
+                                              int32_t rsb) {
   if (mode == SCMP_BIPOLAR) {
     const float fb = __fmul_rn(sb, F);
     return __fmul_rn(__fmul_rn((float)acc, sa), fb);
@@ -94,6 +98,11 @@ __device__ __forceinline__ float sc_rescale(int mode, int prec, int L, int32_t a
   const long long corr = (long long)za * rsb + (long long)zb * rsa - K * (long long)za * (long long)zb;
   const float t = __fsub_rn(__fmul_rn((float)acc, F), __ll2float_rn(corr));
   return __fmul_rn(__fmul_rn(t, sa), sb);
+}
+__device__ __forceinline__ float sc_rescale(int mode, int prec, int L, int32_t acc, int64_t K,
+                                            float sa, int32_t za, int32_t rsa, float sb,
+                                            int32_t zb, int32_t rsb) {
+  return sc_rescale_f(mode, sc_rescale_factor(mode, prec, L), acc, K, sa, za, rsa, sb, zb, rsb);
 }
 
 // Launchers (return cudaError_t of the launch).

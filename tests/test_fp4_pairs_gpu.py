@@ -1,9 +1,10 @@
 """Parity of the e2m1 CTA-pair kernel (tcgen05.mma kind::mxf4 with unit block
 scales) against the oracle.
 
-The engine routes a problem there when it would otherwise run the int8 CTA
-pairs at Lp = 128 or 256: row producers, one K segment, more than 256 rows of
-a and more than 128 rows of b.  Counts must be bit-exact (the fp32
+The engine routes every row-producer problem with one K segment at Lp = 128
+or 256 there: 512-row tiles with two accumulators when a has more than 256
+rows and b more than 128, else 256-row tiles with one accumulator of up to
+256 columns (Q@Kᵀ and Attn@V per head).  Counts must be bit-exact (the fp32
 accumulators hold integers below 2^24) and the rescaled outputs within 1e-5
 relative, exactly as on the int8 path.  Shapes cover every tile width the
 column heuristic picks (128 .. 240 b rows per tile), ragged a and b tails,
@@ -124,3 +125,47 @@ def test_fp4_pair_batched_per_slice_b(cuda_device):
     b = torch.randn(2, 300, 64, generator=g)
     y, y_ref = _run(cuda_device, a, b, 7, 128, granularity="per_head")
     np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
+
+
+@pytest.mark.parametrize("M,N,K,p,L", [
+    (256, 256, 64, 7, 128),     # Q@Kᵀ-shaped tile: one accumulator, 256 columns
+    (200, 64, 264, 7, 128),     # Attn@V-shaped: 64 columns, odd CTA's a rows partly past the end
+    (100, 16, 40, 7, 128),      # a rows only in the even CTA, the narrowest MMA (N = 16)
+    (256, 100, 72, 8, 256),     # Lp = 256, 112 columns
+    (240, 600, 48, 7, 96),      # 3 column tiles of up to 256, early termination
+    (1024, 64, 32, 7, 128),     # narrow b with many a tiles
+    (257, 200, 64, 7, 128),     # 257th a row on the CUDA-core strip
+])
+def test_fp4_one_accumulator_shapes(cuda_device, M, N, K, p, L):
+    g = torch.Generator().manual_seed(M * 5 + N * 11 + K)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    y, y_ref = _run(cuda_device, a, b, p, L)
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_one_accumulator_attention(cuda_device):
+    """Q@Kᵀ per head (per_head scales, batched b) and Attn@V per row on
+    peaked softmax rows, 257 tokens: one-accumulator tiles plus the strips."""
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(3, 257, 64, generator=g)
+    k = torch.randn(3, 257, 64, generator=g)
+    y, y_ref = _run(cuda_device, q, k, 7, 128, granularity="per_head")
+    np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
+    attn = torch.softmax(torch.randn(3, 257, 257, generator=g) * 3.0, dim=-1)
+    vt = torch.randn(3, 64, 257, generator=g)
+    y, y_ref = _run(cuda_device, attn, vt, 7, 128)
+    np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
+
+
+def test_fp4_one_accumulator_row_lengths_unipolar(cuda_device):
+    g = torch.Generator().manual_seed(22)
+    a = torch.randn(240, 48, generator=g)
+    b = torch.randn(96, 48, generator=g) * 0.1
+    rowL = np.random.default_rng(5).choice(np.array([0, 32, 77, 128], np.int32), size=240)
+    y, y_ref = _run(cuda_device, a, b, 7, 128, rowL=rowL)
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+    a = torch.rand(250, 40, generator=g)
+    b = torch.rand(120, 40, generator=g)
+    y, y_ref = _run(cuda_device, a, b, 7, 128, mode="unipolar")
+    np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
