@@ -1063,8 +1063,23 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
   };
   int pbase = 0;
   uint4 ca_n = ld_stream_v4(pa), cb_n = make_uint4(0, 0, 0, 0);
+  // One-accumulator tiles (8 a words per thread) have the registers to load
+  // the next stage's pool complement words one stage ahead, keeping their
+  // latency off each stage's acquire -> store -> publish chain; the others
+  // load them at the top of the stage.
+  constexpr bool kAheadPC = kOneAcc;
+  uint4 qn0 = make_uint4(0, 0, 0, 0), qn1 = qn0, qn2 = qn0, qn3 = qn0;
   if constexpr (!kNoB) {
-    if (doB) cb_n = ld_stream_v4(pb);
+    if (doB) {
+      cb_n = ld_stream_v4(pb);
+      if constexpr (kAheadPC) {
+        const uint4 *pc = reinterpret_cast<const uint4 *>(pc_thr);
+        qn0 = __ldg(pc);
+        qn1 = __ldg(pc + 1);
+        qn2 = __ldg(pc + 2);
+        qn3 = __ldg(pc + 3);
+      }
+    }
     prefetch_macro(0);
   }
 #pragma unroll 1
@@ -1078,9 +1093,18 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
     const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
-      const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * j);
-      uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0, q2 = q0, q3 = q0;
-      if (!kNoB && doB) {
+      uint4 q0 = qn0, q1 = qn1, q2 = qn2, q3 = qn3;
+      if (kAheadPC && !kNoB && doB && (j + 1 < G || mc + 1 < nmacro)) {
+        // stage j + 1 of this macro step, or stage 0 of the next one (which
+        // starts 8 rows = 8 LPB bytes later)
+        const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * (j + 1));
+        qn0 = __ldg(pc);
+        qn1 = __ldg(pc + 1);
+        qn2 = __ldg(pc + 2);
+        qn3 = __ldg(pc + 3);
+      }
+      if (!kAheadPC && !kNoB && doB) {
+        const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * j);
         q0 = __ldg(pc);
         q1 = __ldg(pc + 1);
         q2 = __ldg(pc + 2);
