@@ -81,7 +81,9 @@ class PackedWeight:
     ``sc_matmul`` with the same granularity, mode, sc_prec, config and
     group_b.  Results are bit-identical to passing the weight itself; the
     engine loads the bytes with TMA instead of generating them in every call.
-    Holds about ``N * K * 2**sc_prec`` bytes of device memory."""
+    Holds about ``N * K * 2**sc_prec / 2`` bytes of device memory for
+    sc_prec 7 / 8 with N > 128 (e2m1 nibbles for the e2m1 CTA pairs), else
+    ``N * K * 2**sc_prec`` (int8 bytes)."""
 
     def __init__(self, buf: torch.Tensor, N: int, K: int, granularity: str, mode: str,
                  sc_prec: int, config: dict, group_b: int):
