@@ -1004,7 +1004,11 @@ __device__ __forceinline__ uint32_t stream_word_e2m1(uint32_t u, uint32_t rep, u
 // kNoB: b arrives by TMA from a prepacked buffer; only the a rows are generated.
 // kOneAcc: 128 a rows per CTA (one accumulator); thread pt owns a row pt % 128
 // and its bytes 32 (pt / 128) .. + 31 (64 positions), like its b row.
-template <int LG, int NS, bool kNoB, bool kOneAcc>
+// kSkipA: a 32-position chunk that lies past every window of the warp's 32
+// rows is stored as zeros, one inside all of them as the sign pattern, both
+// without arithmetic (exact; pays where windows are all short or all long,
+// e.g. softmax rows in Attn@V).
+template <int LG, int NS, bool kNoB, bool kOneAcc, bool kSkipA = false>
 __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &st,
                                  uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
                                  int64_t slice_b, int64_t m0, int64_t n0, int nb) {
@@ -1125,11 +1129,22 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
         if (!acquire_stage(b, st, lane)) return false;
         soff = mad_u32((uint32_t)st.stage, prm.stage_bytes, 0u);
       }
+      // window end relative to this thread's first position, over the warp
+      const int relmax = kSkipA ? __reduce_max_sync(0xffffffffu, k - t0A) : 0;
+      const int relmin = kSkipA ? __reduce_min_sync(0xffffffffu, k - t0A) : 0;
 #pragma unroll
-      for (int i = 0; i < NCA; ++i)
-        st_shared_v4(sA[i] + soff, window_word_e2m1(patA, k4, 4 * i),
-                     window_word_e2m1(patA, k4, 4 * i + 1), window_word_e2m1(patA, k4, 4 * i + 2),
-                     window_word_e2m1(patA, k4, 4 * i + 3));
+      for (int i = 0; i < NCA; ++i) {
+        if (kSkipA && relmax <= 32 * i) {  // warp-uniform: past every window
+          st_shared_v4(sA[i] + soff, 0u, 0u, 0u, 0u);
+        } else if (kSkipA && relmin >= 32 * i + 32) {  // warp-uniform: inside every window
+          st_shared_v4(sA[i] + soff, patA, patA, patA, patA);
+        } else {
+          st_shared_v4(sA[i] + soff, window_word_e2m1(patA, k4, 4 * i),
+                       window_word_e2m1(patA, k4, 4 * i + 1),
+                       window_word_e2m1(patA, k4, 4 * i + 2),
+                       window_word_e2m1(patA, k4, 4 * i + 3));
+        }
+      }
       if (!kNoB && doB) {
         st_shared_v4(sB[0] + soff, stream_word_e2m1(u, rep, q0.x, q0.y, patB),
                      stream_word_e2m1(u, rep, q0.z, q0.w, patB),
@@ -2079,8 +2094,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
       const int64_t m0 = (rem % prm.tiles_m) * kBM;
       const int64_t n0 = (rem / prm.tiles_m) * BN;
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
-      if (!produce_rows_fp4<LG, Cfg::kStages, false, false>(prm, b, st, smem_s, Cfg::kStageA,
-                                                             lane, slice, slice_b, m0, n0, BN))
+      if (!produce_rows_fp4<LG, Cfg::kStages, false, false, true>(
+              prm, b, st, smem_s, Cfg::kStageA, lane, slice, slice_b, m0, n0, BN))
         break;
       if (!tile_epilogue<BN, false, false, true>(prm, b, st, smem, tmem_base, warp, lane, slice,
                                                  slice_b, m0, n0, it))

@@ -169,3 +169,18 @@ def test_fp4_one_accumulator_row_lengths_unipolar(cuda_device):
     b = torch.rand(120, 40, generator=g)
     y, y_ref = _run(cuda_device, a, b, 7, 128, mode="unipolar")
     np.testing.assert_allclose(y[0], y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+@pytest.mark.parametrize("temp", [0.01, 1.0, 30.0])
+def test_fp4_narrow_window_chunk_shortcuts(cuda_device, temp):
+    """Attn@V on flat (temp 0.01: every window near full length), mixed and
+    peaked (temp 30: almost every window empty) softmax rows: the narrow
+    kernel stores whole 32-position chunks without arithmetic when they lie
+    inside or past every window of a warp's rows; counts stay exact."""
+    g = torch.Generator().manual_seed(int(temp * 100) + 7)
+    attn = torch.softmax(torch.randn(2, 257, 257, generator=g) * temp, dim=-1)
+    vt = torch.randn(2, 64, 257, generator=g)
+    y, y_ref = _run(cuda_device, attn, vt, 7, 128)
+    np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
+    y, y_ref = _run(cuda_device, attn, vt, 8, 256)
+    np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
