@@ -231,6 +231,17 @@ int quantize_operand(const void *x, bool x_bf16, const OperandLayout &o, int64_t
   auto *gscale = reinterpret_cast<float *>(ws + o.gscale);
   auto *ginv = reinterpret_cast<float *>(ws + o.ginv);
   auto *gzero = reinterpret_cast<int32_t *>(ws + o.gzero);
+  if (o.g.group_rows == 1) {
+    // one row per scale group: stats, scale and codes in one launch
+    if ((e = launch_quantize_rows(x, x_bf16, o.g.rows, K, o.ldc, mode, prec,
+                                  reinterpret_cast<int16_t *>(ws + o.code),
+                                  reinterpret_cast<float *>(ws + o.rscale),
+                                  reinterpret_cast<int32_t *>(ws + o.rzero),
+                                  reinterpret_cast<int32_t *>(ws + o.rsum), s)) != cudaSuccess)
+      return cuda_fail(e, "quantize_rows launch");
+    if (o.g.rows > 0) count_launches(1);
+    return SCMP_OK;
+  }
   if ((e = launch_row_stats(x, x_bf16, o.g.rows, K, mode, stat, s)) != cudaSuccess)
     return cuda_fail(e, "row_stats launch");
   if ((e = launch_group_stats(stat, o.g, mode, prec, gscale, ginv, gzero, s)) != cudaSuccess)

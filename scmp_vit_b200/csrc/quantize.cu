@@ -104,26 +104,36 @@ __global__ void row_stats_kernel(const T *__restrict__ x, int64_t rows, int64_t 
   if (active && lane == 0) stat[row] = make_float2(lo, hi);
 }
 
-// Scale of one group from its min / max (shared by both group kernels).
-__device__ __forceinline__ void write_group_scale(int64_t grp, float lo, float hi, int mode,
-                                                  int prec, float *__restrict__ gscale,
-                                                  float *__restrict__ ginv,
-                                                  int32_t *__restrict__ gzero) {
+// Scale, inverse scale and zero point of one group from its min / max.
+__device__ __forceinline__ void group_scale_of(float lo, float hi, int mode, int prec,
+                                               float &scale, float &inv, int32_t &zero) {
   if (mode == SCMP_BIPOLAR) {
     const float qmax = (float)((1 << (prec - 1)) - 1);
     const float amax = hi > 1e-6f ? hi : 1e-6f;
-    gscale[grp] = __fdiv_rn(amax, qmax);
-    ginv[grp] = __fdiv_rn(qmax, amax);
-    gzero[grp] = 0;
+    scale = __fdiv_rn(amax, qmax);
+    inv = __fdiv_rn(qmax, amax);
+    zero = 0;
   } else {
     const float qmax = (float)((1 << prec) - 1);
     float rng = __fsub_rn(hi, lo);
     if (!(rng > 1e-6f)) rng = 1e-6f;
-    const float inv = __fdiv_rn(qmax, rng);
-    gscale[grp] = __fdiv_rn(rng, qmax);
-    ginv[grp] = inv;
-    gzero[grp] = __float2int_rn(__fmul_rn(-lo, inv));
+    inv = __fdiv_rn(qmax, rng);
+    scale = __fdiv_rn(rng, qmax);
+    zero = __float2int_rn(__fmul_rn(-lo, inv));
   }
+}
+
+// Scale of one group (shared by both group kernels).
+__device__ __forceinline__ void write_group_scale(int64_t grp, float lo, float hi, int mode,
+                                                  int prec, float *__restrict__ gscale,
+                                                  float *__restrict__ ginv,
+                                                  int32_t *__restrict__ gzero) {
+  float scale, inv;
+  int32_t zero;
+  group_scale_of(lo, hi, mode, prec, scale, inv, zero);
+  gscale[grp] = scale;
+  ginv[grp] = inv;
+  gzero[grp] = zero;
 }
 
 // Small groups (per-row scaling, a few rows per group): one thread per group.
@@ -225,6 +235,66 @@ __global__ void quantize_kernel(const T *__restrict__ x, GroupShape g, int64_t K
   acc = group_sum<LPR>(acc);
   if (active && lane == 0) {
     rscale[row] = gscale[grp];
+    rzero[row] = z;
+    rsum[row] = acc;
+  }
+}
+
+// One-row scale groups (per-row scaling with group size 1), fused: the row's
+// min / max, its scale and its codes in one launch.  The LPR lanes of a row
+// read it twice, the second time from L1; the arithmetic and its order are
+// those of row_stats_kernel + group_stats_small_kernel + quantize_kernel, so
+// the codes and scales are identical.
+template <typename T, int LPR>
+__global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int64_t K,
+                                     int64_t ldc, int mode, int prec,
+                                     int16_t *__restrict__ code, float *__restrict__ rscale,
+                                     int32_t *__restrict__ rzero, int32_t *__restrict__ rsum) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LPR;
+  const int lane = threadIdx.x % LPR;
+  const bool active = row < rows;  // inactive lanes still take part in the shuffles
+  const int64_t r = active ? row : 0;
+  const T *xr = x + r * K;
+  int16_t *cr = code + r * ldc;
+  const int64_t kk = active ? K : 0;
+  float lo = INFINITY, hi = -INFINITY;
+  for (int64_t i = lane; i < kk; i += LPR) {
+    const float v = ldx(xr + i);
+    if (mode == SCMP_BIPOLAR) {
+      hi = fmaxf(hi, fabsf(v));
+    } else {
+      lo = fminf(lo, v);
+      hi = fmaxf(hi, v);
+    }
+  }
+  hi = group_max<LPR>(hi);
+  lo = group_min<LPR>(lo);
+  float scale, inv;
+  int32_t z;
+  group_scale_of(lo, hi, mode, prec, scale, inv, z);
+  if (active)
+    for (int64_t i = K + lane; i < ldc; i += LPR) cr[i] = 0;
+  int acc = 0;
+  if (mode == SCMP_BIPOLAR) {
+    const int iq = (1 << (prec - 1)) - 1;
+    for (int64_t i = lane; i < kk; i += LPR) {
+      int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv));
+      q = max(-iq, min(iq, q));
+      cr[i] = (int16_t)(2 * q);
+      acc += 2 * abs(q);
+    }
+  } else {
+    const int iq = (1 << prec) - 1;
+    for (int64_t i = lane; i < kk; i += LPR) {
+      int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv)) + z;
+      q = max(0, min(iq, q));
+      cr[i] = (int16_t)q;
+      acc += q;
+    }
+  }
+  acc = group_sum<LPR>(acc);
+  if (active && lane == 0) {
+    rscale[row] = scale;
     rzero[row] = z;
     rsum[row] = acc;
   }
@@ -426,6 +496,30 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
   else
     SCMP_QUANTIZE(float, 32, xf);
 #undef SCMP_QUANTIZE
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64_t K,
+                                 int64_t ldc, int mode, int prec, int16_t *code, float *rscale,
+                                 int32_t *rzero, int32_t *rsum, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int threads = 256;
+  const int lpr = ldc <= 128 ? 8 : 32;  // short rows: 8 lanes per row
+  const int64_t blocks = (rows * lpr + threads - 1) / threads;
+  const auto *xb = static_cast<const __nv_bfloat16 *>(x);
+  const auto *xf = static_cast<const float *>(x);
+#define SCMP_QUANTIZE_ROWS(T, LPR, X)                                                        \
+  quantize_rows_kernel<T, LPR><<<(unsigned)blocks, threads, 0, s>>>(X, rows, K, ldc, mode, prec, \
+                                                                    code, rscale, rzero, rsum)
+  if (x_bf16 && lpr == 8)
+    SCMP_QUANTIZE_ROWS(__nv_bfloat16, 8, xb);
+  else if (x_bf16)
+    SCMP_QUANTIZE_ROWS(__nv_bfloat16, 32, xb);
+  else if (lpr == 8)
+    SCMP_QUANTIZE_ROWS(float, 8, xf);
+  else
+    SCMP_QUANTIZE_ROWS(float, 32, xf);
+#undef SCMP_QUANTIZE_ROWS
   return cudaGetLastError();
 }
 

@@ -116,6 +116,11 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
                             const float *gscale, const float *ginv, const int32_t *gzero,
                             int16_t *code, float *rscale, int32_t *rzero, int32_t *rsum,
                             cudaStream_t s);
+// One-row scale groups: row stats, scale and codes in one launch (identical
+// results to launch_row_stats + launch_group_stats + launch_quantize).
+cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64_t K,
+                                 int64_t ldc, int mode, int prec, int16_t *code, float *rscale,
+                                 int32_t *rzero, int32_t *rsum, cudaStream_t s);
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
 // PC over max(pool_dims, rows) rows of 2^lp_log2 bytes (rows past the pool
