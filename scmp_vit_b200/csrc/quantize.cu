@@ -257,14 +257,51 @@ __global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int6
   const T *xr = x + r * K;
   int16_t *cr = code + r * ldc;
   const int64_t kk = active ? K : 0;
-  float lo = INFINITY, hi = -INFINITY;
-  for (int64_t i = lane; i < kk; i += LPR) {
-    const float v = ldx(xr + i);
-    if (mode == SCMP_BIPOLAR) {
-      hi = fmaxf(hi, fabsf(v));
+  // VEC elements per 16-byte load (4 fp32 or 8 bf16) when the row, its
+  // length and the code row allow it; one element at a time otherwise
+  constexpr int VEC = std::is_same<T, float>::value ? 4 : 8;
+  const bool vec = (K % VEC) == 0 && (ldc % VEC) == 0 && ((uintptr_t)xr & 15) == 0 &&
+                   ((uintptr_t)cr & (2 * VEC - 1)) == 0;
+  auto load_vec = [&](int64_t i, float (&v)[VEC]) {
+    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(xr + i));
+    if constexpr (std::is_same<T, float>::value) {
+      v[0] = __uint_as_float(w.x);
+      v[1] = __uint_as_float(w.y);
+      v[2] = __uint_as_float(w.z);
+      v[3] = __uint_as_float(w.w);
     } else {
-      lo = fminf(lo, v);
-      hi = fmaxf(hi, v);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] = __uint_as_float(ws[j] << 16);  // bf16 -> fp32, exact
+        v[2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+      }
+    }
+  };
+  float lo = INFINITY, hi = -INFINITY;
+  if (vec) {
+    for (int64_t i = lane * VEC; i < kk; i += LPR * VEC) {
+      float v[VEC];
+      load_vec(i, v);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        if (mode == SCMP_BIPOLAR) {
+          hi = fmaxf(hi, fabsf(v[j]));
+        } else {
+          lo = fminf(lo, v[j]);
+          hi = fmaxf(hi, v[j]);
+        }
+      }
+    }
+  } else {
+    for (int64_t i = lane; i < kk; i += LPR) {
+      const float v = ldx(xr + i);
+      if (mode == SCMP_BIPOLAR) {
+        hi = fmaxf(hi, fabsf(v));
+      } else {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+      }
     }
   }
   hi = group_max<LPR>(hi);
@@ -275,7 +312,37 @@ __global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int6
   if (active)
     for (int64_t i = K + lane; i < ldc; i += LPR) cr[i] = 0;
   int acc = 0;
-  if (mode == SCMP_BIPOLAR) {
+  if (vec) {
+    const bool bip = mode == SCMP_BIPOLAR;
+    const int iq = bip ? (1 << (prec - 1)) - 1 : (1 << prec) - 1;
+    for (int64_t i = lane * VEC; i < kk; i += LPR * VEC) {
+      float v[VEC];
+      load_vec(i, v);
+      uint32_t p[VEC / 2];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        int q = __float2int_rn(__fmul_rn(v[j], inv));
+        int c;
+        if (bip) {
+          q = max(-iq, min(iq, q));
+          c = 2 * q;
+          acc += 2 * abs(q);
+        } else {
+          q = max(0, min(iq, q + z));
+          c = q;
+          acc += q;
+        }
+        if (j & 1)
+          p[j >> 1] |= (uint32_t)(uint16_t)c << 16;
+        else
+          p[j >> 1] = (uint16_t)c;
+      }
+      if constexpr (VEC == 4)
+        *reinterpret_cast<uint2 *>(cr + i) = make_uint2(p[0], p[1]);
+      else
+        *reinterpret_cast<uint4 *>(cr + i) = make_uint4(p[0], p[1], p[2], p[3]);
+    }
+  } else if (mode == SCMP_BIPOLAR) {
     const int iq = (1 << (prec - 1)) - 1;
     for (int64_t i = lane; i < kk; i += LPR) {
       int q = __float2int_rn(__fmul_rn(ldx(xr + i), inv));
