@@ -140,14 +140,26 @@ SCMP_API int scmp_sc_matmul_noalloc(const scmp_matmul_args *args, void *stream);
  * SCMP_IO_B_PACKED and identical N, K, mode, granularity, group_b, sc_prec
  * and pool, and the engine loads those bytes with TMA instead of generating
  * them.  Results are bit-identical to passing b itself.  The buffer holds the
- * int16 codes, per-row scales and the bytes [N][ceil8(K) * 2^p] (about
- * N * K * 2^p bytes: 403 MB for a 3072 x 1024 weight at p = 7).
+ * int16 codes, per-row scales and the operand bytes: e2m1 nibbles
+ * [N][ceil8(K) * 2^p / 2] when sc_prec is 7 or 8 and N > 128 (loaded by the
+ * e2m1 CTA pairs; 201 MB for a 3072 x 1024 weight at p = 7), else int8 bytes
+ * [N][ceil8(K) * 2^p].
  * scmp_prepack_b_size returns its size (0 on invalid arguments; a, M and
  * the stream lengths are ignored); scmp_prepack_b writes it asynchronously on
  * `stream` (b fp32 or bf16 per io_flags). */
 SCMP_API size_t scmp_prepack_b_size(const scmp_matmul_args *args);
 SCMP_API int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_bytes,
                             void *stream);
+
+/* Split the fused qkv projection output of an attention block into the SC
+ * matmul operands (the reshape / unbind / transpose of the qkv output in
+ * cls/sc_attention_patch.py:248-328): qkv [B, N, 3, H, D] row-major ->
+ * q, k [B, H, N, D] and vt [B, H, D, N] (v transposed), so that the per-head
+ * Q@K^T and per-row Attn@V calls read contiguous slices.  Elements are
+ * copied bit for bit (elem_bytes 2 for bf16 / fp16, 4 for fp32).  Requires
+ * B * H <= 65535 and D <= 256.  Asynchronous on `stream`; two launches. */
+SCMP_API int scmp_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D,
+                            int elem_bytes, void *q, void *k, void *vt, void *stream);
 
 /* Message of the last failure on this thread ("" if none). */
 SCMP_API const char *scmp_last_error(void);

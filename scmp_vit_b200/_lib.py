@@ -115,6 +115,11 @@ def load() -> ctypes.CDLL:
         lib.scmp_engine_status.restype = ctypes.c_int
         lib.scmp_probe_int_peak.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
         lib.scmp_probe_int_peak.restype = ctypes.c_int
+        lib.scmp_split_qkv.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p]
+        lib.scmp_split_qkv.restype = ctypes.c_int
         if lib.scmp_abi_version() != ABI_VERSION:
             raise RuntimeError(
                 f"engine ABI {lib.scmp_abi_version()} != expected {ABI_VERSION}")

@@ -259,6 +259,26 @@ def _glue_dtype(x: torch.Tensor) -> Optional[torch.dtype]:
     return torch.bfloat16 if x.dtype == torch.bfloat16 else None
 
 
+def split_qkv(qkv: torch.Tensor, num_heads: int):
+    """``qkv`` [B, N, 3 C] (the fused projection output, C = H D) -> q, k
+    [B, H, N, D] contiguous and v [B, H, N, D] as the transposed view of a
+    contiguous v^T [B, H, D, N]: the layouts the per-head Q@K^T and per-row
+    Attn@V engine calls read without further copies.  One engine pass
+    (``scmp_split_qkv``), bit-identical to unbind + transpose."""
+    from . import _lib
+    B, N, C3 = qkv.shape
+    H = num_heads
+    D = C3 // (3 * H)
+    src = qkv.contiguous()
+    q = torch.empty(B, H, N, D, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty_like(q)
+    vt = torch.empty(B, H, D, N, dtype=qkv.dtype, device=qkv.device)
+    stream = torch.cuda.current_stream(qkv.device).cuda_stream
+    _lib.check(_lib.load().scmp_split_qkv(src.data_ptr(), B, N, H, D, src.element_size(),
+                                          q.data_ptr(), k.data_ptr(), vt.data_ptr(), stream))
+    return q, k, vt.transpose(-1, -2)
+
+
 def make_sc_attention_forward(sc_prec: int, sc_av: bool, sc_qk: bool = True,
                               qk_mp_cfg: MPConfig | None = None,
                               av_mp_cfg: MPConfig | None = None, *,
@@ -272,9 +292,12 @@ def make_sc_attention_forward(sc_prec: int, sc_av: bool, sc_qk: bool = True,
         B, N, C = x.shape
         H = self.num_heads
         D = C // H
-        qkv = self.qkv(x).reshape(B, N, 3, H, D)
-        q, k, v = torch.unbind(qkv, 2)
-        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        qkv = self.qkv(x)
+        if qkv.is_cuda and qkv.element_size() in (2, 4) and B * H <= 65535 and D <= 256:
+            q, k, v = split_qkv(qkv, H)
+        else:
+            q, k, v = torch.unbind(qkv.reshape(B, N, 3, H, D), 2)
+            q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if sc_qk:
             attn = sc_qk_fn(q, k, sc_prec, mp_cfg=qk_mp_cfg, cfg_for=cfg_for,
                             out_dtype=_glue_dtype(x))

@@ -334,6 +334,23 @@ int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_byt
   return SCMP_OK;
 }
 
+int scmp_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D, int elem_bytes,
+                   void *q, void *k, void *vt, void *stream) {
+  g_last_error.clear();
+  if (B < 0 || N < 0 || H < 0 || D < 0) return fail(SCMP_EINVAL, "negative size");
+  if (elem_bytes != 2 && elem_bytes != 4)
+    return fail(SCMP_EINVAL, "elem_bytes must be 2 or 4, got %d", elem_bytes);
+  if (B * H > 65535 || D > 256)
+    return fail(SCMP_EUNSUPPORTED, "split_qkv supports B * H <= 65535 and D <= 256");
+  if (B == 0 || N == 0 || H == 0 || D == 0) return SCMP_OK;
+  if (!qkv || !q || !k || !vt) return fail(SCMP_EINVAL, "qkv, q, k and vt must be non-NULL");
+  const cudaError_t e =
+      launch_split_qkv(qkv, B, N, H, D, elem_bytes, q, k, vt, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "split_qkv launch");
+  count_launches(2);
+  return SCMP_OK;
+}
+
 size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args) {
   if (validate(args) != SCMP_OK) return 0;
   if (args->batch == 0 || args->M == 0 || args->N == 0) return kAlign;

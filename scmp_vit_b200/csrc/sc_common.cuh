@@ -123,6 +123,9 @@ cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64
                                  int32_t *rzero, int32_t *rsum, cudaStream_t s);
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 cudaStream_t s);
+// qkv [B, N, 3, H, D] -> q, k [B, H, N, D], vt [B, H, D, N] (elem_bytes 2 or 4)
+cudaError_t launch_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D,
+                             int elem_bytes, void *q, void *k, void *vt, cudaStream_t s);
 // PC over max(pool_dims, rows) rows of 2^lp_log2 bytes (rows past the pool
 // hold 0x7F).  nibble_pairs: each 8-byte group holds stream positions
 // (0, 2, 4, 6, 1, 3, 5, 7) of its 8 (the e2m1 producers' order).
