@@ -49,28 +49,33 @@ __global__ void split_qk_elem_kernel(const E *__restrict__ qkv, int64_t B, int64
   }
 }
 
-// v^T: block (b h, 32-token tile) stages v[b, t0 .. t0 + 31, 2, h, :] in
+// v^T: block (b h, 64-token tile) stages v[b, t0 .. t0 + 63, 2, h, :] in
 // shared memory (one column of padding against bank conflicts) and writes
-// v^T rows d, 32 consecutive tokens at a time.
+// v^T rows d, 64 consecutive tokens at a time.  Warp w loads tokens w, w + 8,
+// ... (its lanes along D) and stores rows d = w, w + 8, ... (its lanes along
+// the tokens), so every access is coalesced and the index math stays 32-bit
+// inside the tile.
+constexpr int kVtTile = 64;
+
 template <typename E>
-__global__ void split_vt_kernel(const E *__restrict__ qkv, int64_t N, int64_t H, int64_t D,
-                                E *__restrict__ vt) {
+__global__ void __launch_bounds__(256) split_vt_kernel(const E *__restrict__ qkv, int64_t N,
+                                                       int64_t H, int D, E *__restrict__ vt) {
   extern __shared__ unsigned char smem_raw[];
-  E *tile = reinterpret_cast<E *>(smem_raw);  // [32][D + 1]
+  E *tile = reinterpret_cast<E *>(smem_raw);  // [kVtTile][D + 1]
   const int64_t bh = blockIdx.y;
   const int64_t b = bh / H, h = bh % H;
-  const int64_t t0 = (int64_t)blockIdx.x * 32;
-  const int64_t ld = D + 1;
-  for (int64_t i = threadIdx.x; i < 32 * D; i += blockDim.x) {
-    const int64_t tt = i / D, d = i % D;
-    const int64_t t = t0 + tt;
-    if (t < N) tile[tt * ld + d] = qkv[(((b * N + t) * 3 + 2) * H + h) * D + d];
+  const int64_t t0 = (int64_t)blockIdx.x * kVtTile;
+  const int nt = (int)(N - t0 < kVtTile ? N - t0 : kVtTile);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ld = D + 1;
+  for (int tt = warp; tt < nt; tt += 8) {
+    const E *src = qkv + (((b * N + t0 + tt) * 3 + 2) * H + h) * (int64_t)D;
+    for (int d = lane; d < D; d += 32) tile[tt * ld + d] = src[d];
   }
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < 32 * D; i += blockDim.x) {
-    const int64_t d = i / 32, tt = i % 32;
-    const int64_t t = t0 + tt;
-    if (t < N) vt[(bh * D + d) * N + t] = tile[tt * ld + d];
+  for (int d = warp; d < D; d += 8) {
+    E *dst = vt + (bh * D + d) * N + t0;
+    for (int tt = lane; tt < nt; tt += 32) dst[tt] = tile[tt * ld + d];
   }
 }
 
@@ -93,9 +98,14 @@ cudaError_t launch_split(const void *qkv, int64_t B, int64_t N, int64_t H, int64
         static_cast<const E *>(qkv), B, N, H, D, static_cast<E *>(q), static_cast<E *>(k));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const size_t smem = (size_t)32 * (size_t)(D + 1) * sizeof(E);
-  const dim3 grid((unsigned)((N + 31) / 32), (unsigned)(B * H));
-  split_vt_kernel<E><<<grid, 256, smem, s>>>(static_cast<const E *>(qkv), N, H, D,
+  const size_t smem = (size_t)kVtTile * (size_t)(D + 1) * sizeof(E);  // <= 66 KB (D <= 256)
+  if (smem > 48 * 1024) {
+    e = cudaFuncSetAttribute(split_vt_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const dim3 grid((unsigned)((N + kVtTile - 1) / kVtTile), (unsigned)(B * H));
+  split_vt_kernel<E><<<grid, 256, smem, s>>>(static_cast<const E *>(qkv), N, H, (int)D,
                                                static_cast<E *>(vt));
   return cudaGetLastError();
 }

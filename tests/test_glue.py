@@ -33,6 +33,7 @@ def test_split_qkv_rejects_bad_arguments():
     (3, 257, 4, 64, torch.float32),
     (2, 33, 3, 36, torch.bfloat16),     # 72-byte rows: element-by-element path
     (1, 70, 5, 20, torch.float32),      # 80-byte rows, ragged token tiles
+    (1, 130, 2, 256, torch.float32),    # the widest head: 66 KB transpose tile
 ])
 def test_split_qkv_matches_torch(cuda_device, B, N, H, D, dtype):
     g = torch.Generator().manual_seed(B * 100 + N + H + D)
