@@ -48,7 +48,7 @@ enum scmp_status {
   SCMP_EINVAL = -1,       /* bad shape / argument */
   SCMP_ECUDA = -2,        /* a CUDA runtime call failed */
   SCMP_EWORKSPACE = -3,   /* workspace missing or too small */
-  SCMP_EUNSUPPORTED = -4, /* valid request this build does not implement */
+  SCMP_EUNSUPPORTED = -4, /* valid request this library does not implement */
   SCMP_ETIMEOUT = -5      /* a bounded device-side wait gave up */
 };
 
