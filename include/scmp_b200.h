@@ -129,7 +129,10 @@ SCMP_API int scmp_sc_matmul(const scmp_matmul_args *args, void *stream);
  * contents (the engine writes all scratch before reading it); calls whose
  * kernels overlap on the GPU race on it, so keep them on one stream.  The
  * first call on each device looks up the array's address with that device
- * current; make it before any stream capture begins. */
+ * current and caches it per (device, driver context): a host that makes
+ * its own contexts (cuCtxCreate) gets the address in the context current at
+ * the call.  Make the first call in each context before any stream capture
+ * begins. */
 SCMP_API int scmp_sc_matmul_noalloc(const scmp_matmul_args *args, void *stream);
 
 /* Prepacked weights (no reference counterpart: the reference regenerates a
@@ -178,10 +181,27 @@ SCMP_API uint64_t scmp_kernel_launches(void);
  * reference counterpart. */
 SCMP_API int scmp_engine_status(int reset, unsigned int *flags);
 
+/* Give-up path of the bounded device waits (test and instrumentation hooks;
+ * no reference counterpart).  Every wait of the tensor-core engine on an
+ * mbarrier spins for at most a limit, then marks its CTA aborted: the CTA
+ * stops issuing work, waits for the tensor-core operations it already issued,
+ * frees its tensor memory and returns, and the launch raises bit 0 of
+ * scmp_engine_status.  scmp_debug_set_wait_limit sets that limit for later
+ * launches on the current device (ns > 0; the default is 2 s).
+ * scmp_debug_hold_producers(1) makes the operand producers of the e2m1
+ * kernels (Lp = 128 / 256) first wait on a device flag that nothing sets, so
+ * that every wait of those launches runs out (their outputs are not written);
+ * scmp_debug_hold_producers(0) restores normal operation.  Both are
+ * synchronous and apply to the current device only. */
+SCMP_API int scmp_debug_set_wait_limit(uint64_t ns);
+SCMP_API int scmp_debug_hold_producers(int on);
+
 /* Roofline probe (synchronous; allocates a small scratch buffer): runs a
  * register-only loop of one instruction class on every SM of the current
  * device and returns its rate.  kind 0 = LOP3+POPC (bit-products/s),
- * 1 = mma.sync b1 AND.POPC (bit-products/s), 2 = mma.sync s8 (MACs/s).
+ * 1 = mma.sync b1 AND.POPC (bit-products/s), 2 = mma.sync s8 (MACs/s),
+ * 3 / 4 = tcgen05.mma kind::mxf4 M128 x N256 / N64 x K64 issued back to back
+ * (MACs/s; one MAC of {-1, 0, +1} e2m1 operands is one SC bit-product).
  * Instrumentation only; no reference counterpart. */
 SCMP_API int scmp_probe_int_peak(int kind, double *ops_per_second);
 

@@ -33,6 +33,11 @@ EXPORTED_SYMBOLS = (
     "scmp_kernel_launches",
     "scmp_engine_status",
     "scmp_probe_int_peak",
+    "scmp_debug_set_wait_limit",
+    "scmp_debug_hold_producers",
+    "scmp_prepack_b_size",
+    "scmp_prepack_b",
+    "scmp_split_qkv",
 )
 
 
@@ -120,6 +125,10 @@ def load() -> ctypes.CDLL:
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p]
         lib.scmp_split_qkv.restype = ctypes.c_int
+        lib.scmp_debug_set_wait_limit.argtypes = [ctypes.c_uint64]
+        lib.scmp_debug_set_wait_limit.restype = ctypes.c_int
+        lib.scmp_debug_hold_producers.argtypes = [ctypes.c_int]
+        lib.scmp_debug_hold_producers.restype = ctypes.c_int
         if lib.scmp_abi_version() != ABI_VERSION:
             raise RuntimeError(
                 f"engine ABI {lib.scmp_abi_version()} != expected {ABI_VERSION}")
@@ -140,10 +149,23 @@ def engine_status(reset: bool = False) -> int:
     return int(v.value)
 
 
+def set_wait_limit(ns: int) -> None:
+    """Limit of the engine's bounded device waits on the current device
+    (default 2 s); a test hook for the give-up path."""
+    check(load().scmp_debug_set_wait_limit(int(ns)))
+
+
+def hold_producers(on: bool) -> None:
+    """Test hook: make the e2m1 kernels' bounded waits run out (see
+    ``scmp_debug_hold_producers`` in the header)."""
+    check(load().scmp_debug_hold_producers(1 if on else 0))
+
+
 def probe_int_peak(kind: int) -> float:
-    """Measured rate of one integer instruction class on the current device
+    """Measured rate of one instruction class on the current device
     (0: LOP3+POPC bit-products/s, 1: mma.sync b1 bit-products/s,
-    2: mma.sync s8 MACs/s)."""
+    2: mma.sync s8 MACs/s, 3 / 4: tcgen05 kind::mxf4 M128 x N256 / N64 MACs/s,
+    i.e. e2m1 bit-products/s)."""
     v = ctypes.c_double(0.0)
     check(load().scmp_probe_int_peak(int(kind), ctypes.byref(v)))
     return float(v.value)

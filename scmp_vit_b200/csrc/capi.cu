@@ -20,18 +20,13 @@ inline void count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_ord
 // engine gave up).  Read with scmp_engine_status.
 __device__ unsigned int g_engine_error;
 std::mutex g_err_mu;
-unsigned int *g_err_ptr[64] = {};
+SymbolCache g_err_ptr[kMaxCachedDevices];
 
 unsigned int *engine_error_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(g_err_mu);
-  if (!g_err_ptr[dev]) {
-    void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_engine_error) != cudaSuccess) return nullptr;
-    g_err_ptr[dev] = static_cast<unsigned int *>(p);
-  }
-  return g_err_ptr[dev];
+  void *p = nullptr;
+  if (cached_symbol_address(g_err_ptr, g_err_mu, g_engine_error, &p) != cudaSuccess)
+    return nullptr;
+  return static_cast<unsigned int *>(p);
 }
 
 // Rows of the tail that the CUDA-core engine takes instead of padding a
@@ -269,6 +264,22 @@ QuantPlane plane_of(const OperandLayout &o, unsigned char *ws) {
 
 void set_last_error(const char *msg) { g_last_error = msg ? msg : ""; }
 
+void *current_context() {
+  using GetCurrent = int (*)(void **);
+  static std::once_flag once;
+  static GetCurrent fn = nullptr;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetCurrent>(p);
+  });
+  void *ctx = nullptr;
+  if (fn && fn(&ctx) != 0) ctx = nullptr;
+  return ctx;
+}
+
 }  // namespace scmp
 
 using namespace scmp;
@@ -291,6 +302,16 @@ int scmp_engine_status(int reset, unsigned int *flags) {
     if (e != cudaSuccess) return cuda_fail(e, "clearing the engine error word");
   }
   return SCMP_OK;
+}
+
+int scmp_debug_set_wait_limit(uint64_t ns) {
+  g_last_error.clear();
+  return debug_set_wait_limit(ns);
+}
+
+int scmp_debug_hold_producers(int on) {
+  g_last_error.clear();
+  return debug_hold_producers(on);
 }
 
 size_t scmp_prepack_b_size(const scmp_matmul_args *args) {

@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -40,7 +41,16 @@ constexpr int kStages = 3;
 constexpr int kProducerWarps = 16;
 constexpr int kProducers = 32 * kProducerWarps;
 constexpr int kThreads = 32 + kProducers;
-constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // default limit: 2 s per wait
+
+// Limit of every bounded pipeline wait on this device (ns; kTimeoutNs unless
+// scmp_debug_set_wait_limit changed it).  Read on the slow path only.
+__device__ unsigned long long g_wait_limit_ns = kTimeoutNs;
+// Test hook for the give-up path (scmp_debug_hold_producers): while set, the
+// operand producers of the e2m1 kernels first wait on g_hold_release, which
+// nothing ever sets, so the pipeline waits of their CTA run out.
+__device__ int g_hold_producers = 0;
+__device__ int g_hold_release = 0;
 
 template <int BN>
 struct TcCfg {
@@ -110,14 +120,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
+  const unsigned long long lim = g_wait_limit_ns;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (now_ns() - t0 > kTimeoutNs) {
+    if (now_ns() - t0 > lim) {
       *abort = 1;
       return false;
     }
   }
+}
+// Wait for this thread's own tensor-core work to complete before its TMEM is
+// freed: ignores the abort word (MMAs already issued always complete) and
+// gives up only after kTimeoutNs.
+__device__ __forceinline__ void mbar_wait_own(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const unsigned long long t0 = now_ns();
+  while (!mbar_try_wait(bar, parity) && now_ns() - t0 <= kTimeoutNs) {
+  }
+}
+// Test hook: with g_hold_producers set, wait on a flag that nothing sets until
+// the wait limit runs out (or the CTA aborts); false = give up.
+__device__ __forceinline__ bool producers_released(volatile int *abort) {
+  if (!*reinterpret_cast<volatile int *>(&g_hold_producers)) return true;
+  const unsigned long long t0 = now_ns();
+  const unsigned long long lim = g_wait_limit_ns;
+  while (!*reinterpret_cast<volatile int *>(&g_hold_release)) {
+    if (*abort) return false;
+    if (now_ns() - t0 > lim) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
 }
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -175,13 +210,21 @@ __device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity)
 __device__ __forceinline__ bool mbar_wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort) {
   if (mbar_try_wait_cl(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
+  const unsigned long long lim = g_wait_limit_ns;
   while (true) {
     if (mbar_try_wait_cl(bar, parity)) return true;
     if (*abort) return false;
-    if (now_ns() - t0 > kTimeoutNs) {
+    if (now_ns() - t0 > lim) {
       *abort = 1;
       return false;
     }
+  }
+}
+// mbar_wait_own with cluster-scope acquire (pair MMAs arrive from the pair).
+__device__ __forceinline__ void mbar_wait_own_cl(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait_cl(bar, parity)) return;
+  const unsigned long long t0 = now_ns();
+  while (!mbar_try_wait_cl(bar, parity) && now_ns() - t0 <= kTimeoutNs) {
   }
 }
 // Both CTAs of the pair reach this point (every path to it is bounded).
@@ -1013,6 +1056,7 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
                                  uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
                                  int64_t slice_b, int64_t m0, int64_t n0, int nb) {
   static_assert(LG == 7 || LG == 8, "e2m1 producers take Lp = 128 or 256");
+  if (!producers_released(b.abort)) return false;  // give-up path test hook
   constexpr int G = (8 << LG) / 256;  // k-blocks per macro step of 8 indices: 4 or 8
   constexpr int LPB = 1 << LG;
   constexpr int RA = kOneAcc ? 128 : 256;  // a rows per CTA
@@ -1384,7 +1428,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const TcParams prm
       }
       // Drain: everything this thread issued has completed before TMEM is freed.
       tc_commit(b.drain);
-      mbar_wait(b.drain, 0, b.abort);
+      mbar_wait_own(b.drain, 0);
     }
     __syncwarp();
   } else {
@@ -1504,7 +1548,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_ts_kernel(const TcParams 
       }
       // Drain: everything this thread issued has completed before TMEM is freed.
       tc_commit(b.drain);
-      mbar_wait(b.drain, 0, b.abort);
+      mbar_wait_own(b.drain, 0);
     }
     __syncwarp();
   } else {
@@ -1654,7 +1698,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       }
       // Drain: everything this thread issued has completed before TMEM is freed.
       tc_commit_pair_local(b.drain);
-      mbar_wait_cl(b.drain, 0, b.abort);
+      mbar_wait_own_cl(b.drain, 0);
     } else if (rank == 1 && lane == 0) {
       // ============ forwarder (odd CTA): each filled stage of this CTA is
       // announced to the MMA thread with one cluster-scope release
@@ -1883,7 +1927,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         tc_commit_pair_both(b.tfull);
       }
       tc_commit_pair_local(b.drain);
-      mbar_wait_cl(b.drain, 0, b.abort);
+      mbar_wait_own_cl(b.drain, 0);
     } else if (rank == 1 && lane == 0) {
       // ============ forwarder (odd CTA): each filled stage of this CTA is
       // announced to the MMA thread with one cluster-scope release
@@ -2080,7 +2124,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
         tc_commit(b.tfull);
       }
       tc_commit(b.drain);
-      mbar_wait(b.drain, 0, b.abort);
+      mbar_wait_own(b.drain, 0);
     }
     __syncwarp();
   } else {
@@ -2110,6 +2154,74 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
                  "r"(kTmemAlloc));
   }
   if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
+}
+
+// ---------------------------------------------------------------------------
+// Rate probe of the e2m1 MMA the engine's tiles are built from: one CTA per
+// SM, one thread issues `iters` x 4 back-to-back kind::mxf4 MMAs of
+// M = 128 x N = BN x K = 64 (unit block scales, zero operands in shared
+// memory) into one TMEM accumulator, then waits for them with a bounded wait.
+// Nothing else runs, so the launch time is the MMA pipe's time.
+template <int BN>
+__global__ void __launch_bounds__(128, 1) probe_mma_mxf4_kernel(int iters, unsigned int *error) {
+  constexpr uint32_t kA = 128 * kKB, kB = BN * kKB;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *done = reinterpret_cast<uint64_t *>(smem + kA + kB);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  const int warp = threadIdx.x >> 5;
+  for (uint32_t i = threadIdx.x; i < (kA + kB) / 16; i += blockDim.x)
+    reinterpret_cast<uint4 *>(smem)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  fence_async_smem();
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512u));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  {  // unit scale factors in columns [kFp4SfCol, 512), warp w covers lanes 32 w ..
+    uint32_t one[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) one[i] = 0x7F7F7F7Fu;
+    const uint32_t t = tmem_base + ((uint32_t)(warp * 32) << 16) + kFp4SfCol;
+    tmem_st16(t, one);
+    tmem_st16(t + 16, one);
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    const uint32_t a0 = smem_u32(smem), b0 = a0 + kA;
+    constexpr uint32_t idesc = idesc_mxf4_m128(BN);
+    const uint32_t sf = tmem_base + kFp4SfCol;
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int kk = 0; kk < kKB / 32; ++kk)
+        tc_mma_mxf4(tmem_base, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                    sf, (it > 0 || kk > 0) ? 1u : 0u);
+    }
+    tc_commit(done);
+    // the issued MMAs always complete: wait for them before the TMEM is freed
+    mbar_wait_own(done, 0);
+    if (!mbar_try_wait(done, 0)) atomicOr(error, 1u);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(512u));
+  }
 }
 
 template <int BN, int kProd, int LG, bool kSeg>
@@ -2348,14 +2460,18 @@ cudaError_t launch_rows(const TcParams &prm, int sms, cudaStream_t s) {
 constexpr size_t kThermBytes = (size_t)2 * 129 * 128;
 __device__ __align__(128) unsigned char g_therm[kThermBytes];
 std::mutex g_therm_mu;
-const unsigned char *g_therm_ptr[64] = {};
+SymbolCache g_therm_ptr[kMaxCachedDevices];
 
+// Filled on first use per (device, context); the cache key follows
+// cached_symbol_address.
 const unsigned char *therm_table(cudaError_t *err) {
   int dev = 0;
   *err = cudaGetDevice(&dev);
-  if (*err != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (*err != cudaSuccess || dev < 0 || dev >= kMaxCachedDevices) return nullptr;
+  void *ctx = current_context();
   std::lock_guard<std::mutex> lock(g_therm_mu);
-  if (!g_therm_ptr[dev]) {
+  SymbolCache &c = g_therm_ptr[dev];
+  if (!c.ptr || c.ctx != ctx) {
     std::vector<unsigned char> h(kThermBytes, 0);
     for (int sg = 0; sg < 2; ++sg)
       for (int q = 0; q <= 128; ++q) {
@@ -2365,9 +2481,10 @@ const unsigned char *therm_table(cudaError_t *err) {
     if ((*err = cudaMemcpyToSymbol(g_therm, h.data(), kThermBytes)) != cudaSuccess) return nullptr;
     void *p = nullptr;
     if ((*err = cudaGetSymbolAddress(&p, g_therm)) != cudaSuccess) return nullptr;
-    g_therm_ptr[dev] = static_cast<const unsigned char *>(p);
+    c.ptr = p;
+    c.ctx = ctx;
   }
-  return g_therm_ptr[dev];
+  return static_cast<const unsigned char *>(c.ptr);
 }
 
 }  // namespace
@@ -2492,6 +2609,58 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   if (bn == 64) return launch_bn<64, kProdChunks, 0, false>(prm, sms, s);
   if (bn == 128) return launch_bn<128, kProdChunks, 0, false>(prm, sms, s);
   return launch_bn<256, kProdChunks, 0, false>(prm, sms, s);
+}
+
+namespace {
+template <typename T>
+int set_device_word(const T &symbol, const T &value, const char *what) {
+  const cudaError_t e = cudaMemcpyToSymbol(symbol, &value, sizeof(T));
+  if (e != cudaSuccess) {
+    char buf[200];
+    snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+    set_last_error(buf);
+    return SCMP_ECUDA;
+  }
+  return SCMP_OK;
+}
+}  // namespace
+
+int debug_set_wait_limit(uint64_t ns) {
+  if (ns == 0) {
+    set_last_error("the wait limit must be positive");
+    return SCMP_EINVAL;
+  }
+  const unsigned long long v = ns;
+  return set_device_word(g_wait_limit_ns, v, "setting the wait limit");
+}
+
+cudaError_t launch_probe_mma_mxf4(int n, int iters, int blocks, unsigned int *error,
+                                  cudaStream_t s) {
+  // more shared memory than two CTAs can share: one CTA (one TMEM owner) per SM
+  const size_t smem = 120 * 1024;
+  static_assert((size_t)(128 + 256) * kKB + 1024 + 64 <= 120 * 1024, "probe tiles fit");
+  cudaError_t e;
+  if (n == 256) {
+    if ((e = cudaFuncSetAttribute(probe_mma_mxf4_kernel<256>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+        cudaSuccess)
+      return e;
+    probe_mma_mxf4_kernel<256><<<blocks, 128, smem, s>>>(iters, error);
+  } else if (n == 64) {
+    if ((e = cudaFuncSetAttribute(probe_mma_mxf4_kernel<64>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+        cudaSuccess)
+      return e;
+    probe_mma_mxf4_kernel<64><<<blocks, 128, smem, s>>>(iters, error);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+int debug_hold_producers(int on) {
+  const int v = on ? 1 : 0;
+  return set_device_word(g_hold_producers, v, "setting the producer hold");
 }
 
 }  // namespace scmp

@@ -19,22 +19,19 @@
 //    reading it, so nothing needs clearing between calls -- but two calls
 //    whose kernels overlap on the GPU (different streams, no ordering) race on
 //    the array and corrupt each other.  Order such calls on one stream.
-//  * The first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress) with that device current, and caches it.  Make
-//    that first call before any stream capture begins.
+//  * The first call on each device (and in each further driver context a
+//    host makes current on it) looks up the array's device address
+//    (cudaGetSymbolAddress) with that device current, and caches it per
+//    (device, context).  Make that first call before any stream capture
+//    begins.
 #include <cstdio>
 #include <mutex>
 
 #include "sc_common.cuh"
 
-namespace scmp {
-void set_last_error(const char *msg);
-}
-
 namespace {
 
 constexpr size_t kScratchBytes = (size_t)SCMP_NOALLOC_SCRATCH_BYTES;
-constexpr int kMaxDevices = 64;
 
 // The scratch array.  In host code `g_noalloc_scratch` names a host-side
 // stand-in, not device memory: pass only the address from
@@ -42,33 +39,18 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 std::mutex g_mu;
-void *g_scratch_ptr[kMaxDevices] = {};
+scmp::SymbolCache g_scratch_ptr[scmp::kMaxCachedDevices];
 
-// Device address of the scratch array on the current device (set-up on the
-// first call per device).
+// Device address of the scratch array in the current context (set-up on the
+// first call per device and context).
 int scratch_for_current_device(void **out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
+  const cudaError_t e = scmp::cached_symbol_address(g_scratch_ptr, g_mu, g_noalloc_scratch, out);
   if (e != cudaSuccess) {
-    scmp::set_last_error(cudaGetErrorString(e));
-    return SCMP_ECUDA;
+    scmp::set_last_error(e == cudaErrorInvalidDevice
+                             ? "device ordinal out of range for the no-alloc scratch table"
+                             : cudaGetErrorString(e));
+    return e == cudaErrorInvalidDevice ? SCMP_EUNSUPPORTED : SCMP_ECUDA;
   }
-  if (dev < 0 || dev >= kMaxDevices) {
-    scmp::set_last_error("device ordinal out of range for the no-alloc scratch table");
-    return SCMP_EUNSUPPORTED;
-  }
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      scmp::set_last_error(e != cudaSuccess ? cudaGetErrorString(e)
-                                            : "cudaGetSymbolAddress returned NULL");
-      return SCMP_ECUDA;
-    }
-    g_scratch_ptr[dev] = p;
-  }
-  *out = g_scratch_ptr[dev];
   return SCMP_OK;
 }
 

@@ -5,12 +5,16 @@
 //   kind 0: LOP3 (AND) + POPC on 32-bit words       -> bit-products per second
 //   kind 1: mma.sync m16n8k256 b1 AND.POPC           -> bit-products per second
 //   kind 2: mma.sync m16n8k32 s8 x s8 -> s32          -> multiply-adds per second
+//   kind 3: tcgen05.mma kind::mxf4 M128 x N256 x K64   -> multiply-adds per second
+//   kind 4: tcgen05.mma kind::mxf4 M128 x N64 x K64    -> multiply-adds per second
 // A bit-product is one (m, n, d, t) term of the SC inner product, i.e. one
-// AND + one counted bit.
+// AND + one counted bit; on the e2m1 tensor-core engine it is one
+// multiply-add of operands in {-1, 0, +1}, so kinds 3 and 4 are the
+// tensor-core engine's bit-product ceilings (the wide tiles' and Attn@V's).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/scmp_b200.h"
+#include "sc_common.cuh"
 
 namespace {
 
@@ -71,14 +75,43 @@ __global__ void probe_mma_s8(uint32_t seed, int iters, uint32_t *out) {
   out[blockIdx.x * blockDim.x + threadIdx.x] = (uint32_t)s;
 }
 
+// kinds 3 / 4: the e2m1 MMA issued back to back on every SM (MACs per second)
+int probe_mxf4(int n, int sms, double *ops_per_second) {
+  constexpr int kMmaIters = 2048;
+  unsigned int *err = nullptr;
+  if (cudaMalloc(&err, sizeof(unsigned int)) != cudaSuccess) return SCMP_ECUDA;
+  cudaMemset(err, 0, sizeof(unsigned int));
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaError_t e = scmp::launch_probe_mma_mxf4(n, 16, sms, err, 0);  // warm-up
+  if (e == cudaSuccess) {
+    cudaEventRecord(e0);
+    e = scmp::launch_probe_mma_mxf4(n, kMmaIters, sms, err, 0);
+    cudaEventRecord(e1);
+  }
+  if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  unsigned int flag = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&flag, err, sizeof(flag), cudaMemcpyDeviceToHost);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(err);
+  if (e != cudaSuccess || flag != 0 || ms <= 0.f) return e != cudaSuccess ? SCMP_ECUDA : SCMP_ETIMEOUT;
+  *ops_per_second = 4.0 * kMmaIters * 128.0 * n * 64.0 * sms / (ms * 1e-3);
+  return SCMP_OK;
+}
+
 }  // namespace
 
 extern "C" SCMP_API int scmp_probe_int_peak(int kind, double *ops_per_second) {
-  if (!ops_per_second || kind < 0 || kind > 2) return SCMP_EINVAL;
+  if (!ops_per_second || kind < 0 || kind > 4) return SCMP_EINVAL;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SCMP_ECUDA;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return SCMP_ECUDA;
+  if (kind >= 3) return probe_mxf4(kind == 3 ? 256 : 64, sms, ops_per_second);
   const int threads = 256, blocks = sms * 8;
   uint32_t *out = nullptr;
   if (cudaMalloc(&out, sizeof(uint32_t) * threads * blocks) != cudaSuccess) return SCMP_ECUDA;

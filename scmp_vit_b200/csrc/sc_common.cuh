@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/scmp_b200.h"
 
 namespace scmp {
@@ -152,5 +154,52 @@ int tc_stream_log2(const GemmProblem &P);
 bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows);
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
                            unsigned int *error, cudaStream_t s);
+
+// Message of the last failure on this thread (capi.cu).
+void set_last_error(const char *msg);
+
+// Driver context current on this thread (NULL if none or unknown).  A device
+// symbol's address belongs to the context that loaded the module, so the
+// per-device caches of symbol addresses are keyed by (ordinal, context): a
+// host that makes its own contexts (cuCtxCreate) or resets a device gets its
+// addresses looked up again instead of another context's.
+void *current_context();
+
+constexpr int kMaxCachedDevices = 64;
+struct SymbolCache {
+  void *ctx = nullptr;
+  void *ptr = nullptr;
+};
+
+// Address of `symbol` in the current context, cached per device ordinal
+// (looked up again when the current context differs from the cached one).
+template <typename T>
+cudaError_t cached_symbol_address(SymbolCache (&cache)[kMaxCachedDevices], std::mutex &mu,
+                                  const T &symbol, void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxCachedDevices) return cudaErrorInvalidDevice;
+  void *ctx = current_context();
+  std::lock_guard<std::mutex> lock(mu);
+  SymbolCache &c = cache[dev];
+  if (!c.ptr || c.ctx != ctx) {
+    void *p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, symbol)) != cudaSuccess) return e;
+    if (!p) return cudaErrorInvalidSymbol;
+    c.ptr = p;
+    c.ctx = ctx;
+  }
+  *out = c.ptr;
+  return cudaSuccess;
+}
+// Give-up path hooks of the tensor-core engine, on the current device
+// (synchronous; SCMP_OK or an SCMP_E* code).
+int debug_set_wait_limit(uint64_t ns);
+int debug_hold_producers(int on);
+// e2m1 MMA-rate probe (kind::mxf4, M = 128 x N = n x K = 64, n = 64 or 256):
+// `blocks` CTAs each issue 4 * iters MMAs; bit 0 of *error = a wait gave up.
+cudaError_t launch_probe_mma_mxf4(int n, int iters, int blocks, unsigned int *error,
+                                  cudaStream_t s);
 
 }  // namespace scmp

@@ -55,36 +55,50 @@ class DispatchEntry:
 def build_range_dispatch(weight: torch.Tensor, cfg: RangeMPConfig,
                          operator: Optional[str] = None, group_size: int = 0
                          ) -> List[DispatchEntry]:
-    """Split the weight's output rows into contiguous groups, classify each
-    by range, and merge groups that share a level into one entry."""
-    out_features = weight.shape[0]
-    g = group_size if 0 < group_size < out_features else out_features
-    num_groups = out_features // g
-    group_sls = classify_groups_by_range(weight, group_size=g, config=cfg, operator=operator)
-    if len(group_sls) != num_groups:
-        raise AssertionError(f"classify_groups_by_range returned {len(group_sls)} levels for "
-                             f"{num_groups} groups")
-    by_level: dict[int, list[int]] = {}
-    for gi, sl in enumerate(group_sls):
-        by_level.setdefault(int(sl), []).extend(range(gi * g, (gi + 1) * g))
-    entries = []
-    for sl, rows in by_level.items():
-        idx = torch.as_tensor(rows, dtype=torch.long, device=weight.device)
-        entries.append(DispatchEntry(stoc_len=int(sl), sc_prec=sc_prec_for_stoc_len(int(sl)),
-                                     weight=weight.index_select(0, idx).contiguous(),
-                                     out_indices=idx))
+    """Static per-output-row stream lengths of a weight (range MP).
+
+    The output rows form contiguous groups of ``group_size`` (the whole weight
+    when 0 or too large); ``classify_groups_by_range`` gives each group a level
+    from its value range.  Every output row inherits its group's level in one
+    ``repeat_interleave``, and one entry per distinct level (in order of first
+    appearance) holds that level's rows and their weight slice, so a forward
+    runs one bucket per level instead of one per group.  Rows past the last
+    whole group belong to no entry, as in the reference
+    (``sc_integration/mp_linear.py:81-119``)."""
+    n_out = weight.shape[0]
+    size = group_size if 0 < group_size < n_out else n_out
+    n_groups = n_out // size
+    levels = torch.as_tensor([int(v) for v in classify_groups_by_range(
+        weight, group_size=size, config=cfg, operator=operator)], dtype=torch.long)
+    if levels.numel() != n_groups:
+        raise AssertionError(f"classify_groups_by_range returned {levels.numel()} levels for "
+                             f"{n_groups} groups")
+    row_level = levels.repeat_interleave(size).to(weight.device)  # level of row r < n_groups*size
+    entries: List[DispatchEntry] = []
+    for level in dict.fromkeys(levels.tolist()):
+        rows = torch.nonzero(row_level == level).flatten()
+        entries.append(DispatchEntry(stoc_len=level, sc_prec=sc_prec_for_stoc_len(level),
+                                     weight=weight.index_select(0, rows).contiguous(),
+                                     out_indices=rows))
     return entries
 
 
+def _row_absmax(x_flat: torch.Tensor) -> torch.Tensor:
+    """The input-row MP metric: the largest magnitude of each row (fp32)."""
+    return torch.linalg.vector_norm(x_flat.float(), ord=float("inf"), dim=-1)
+
+
 def classify_input_rows(x_flat: torch.Tensor, cfg: MPConfig) -> RowAssignment:
-    """Bucket activation rows by abs-max into MP levels."""
-    metric = x_flat.float().abs().amax(dim=-1)
-    return classify_rows_by_metric(metric, cfg.stoc_len_levels, cfg.level_fractions)
+    """Fixed-quantile MP levels of activation rows, ranked by ``_row_absmax``
+    (reference ``sc_integration/mp_linear.py:122-127``)."""
+    return classify_rows_by_metric(_row_absmax(x_flat), cfg.stoc_len_levels,
+                                   cfg.level_fractions)
 
 
 def classify_input_rows_adaptive(x_flat: torch.Tensor, cfg: AdaptiveMPConfig, timestep: int,
                                  total_timesteps: int, operator: Optional[str] = None
                                  ) -> RowAssignment:
-    """Timestep-aware per-row classification (same abs-max metric)."""
-    metric = x_flat.float().abs().amax(dim=-1)
-    return adaptive_classify_rows(metric, timestep, total_timesteps, cfg, operator=operator)
+    """Timestep-aware MP levels of activation rows, same metric
+    (reference ``sc_integration/mp_linear.py:130-147``)."""
+    return adaptive_classify_rows(_row_absmax(x_flat), timestep, total_timesteps, cfg,
+                                  operator=operator)

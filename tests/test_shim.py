@@ -15,7 +15,9 @@ import pytest
 import torch
 import torch.nn as nn
 
-REF = Path(os.environ.get("SCMP_REFERENCE_DIR", "/root/reference"))
+# the reference tree: SCMP_REFERENCE_DIR, else an install under baseline/_ref
+REF = Path(os.environ.get("SCMP_REFERENCE_DIR",
+                          Path(__file__).resolve().parents[1] / "baseline" / "_ref"))
 pytestmark = pytest.mark.skipif(not (REF / "sc_integration" / "sc_linear.py").exists(),
                                 reason="reference tree not available")
 

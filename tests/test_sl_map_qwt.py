@@ -156,7 +156,9 @@ def test_comp_state_save_load_install(tmp_path):
         qwt.load_comp_state(str(tmp_path / "x.pt"))
 
 
-REF = Path(os.environ.get("SCMP_REFERENCE_DIR", "/root/reference"))
+# the reference tree: SCMP_REFERENCE_DIR, else an install under baseline/_ref
+REF = Path(os.environ.get("SCMP_REFERENCE_DIR",
+                          Path(__file__).resolve().parents[1] / "baseline" / "_ref"))
 
 
 @pytest.mark.skipif(not (REF / "sc_integration" / "mp_search.py").exists(),

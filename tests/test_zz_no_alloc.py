@@ -22,12 +22,12 @@ pytestmark = pytest.mark.gpu
 RTOL = 1e-5
 
 
-def _args(a, b, pool, out, acc, *, p, L, dims, bias=None):
+def _args(a, b, pool, out, acc, *, p, L, dims, bias=None, engine="auto"):
     BH, M, K = a.shape
     N = b.shape[-2]
     x = _lib.MatmulArgs()
     x.abi_version = _lib.ABI_VERSION
-    x.engine = _lib.ENGINE["auto"]
+    x.engine = _lib.ENGINE[engine]
     x.a, x.b = a.data_ptr(), b.data_ptr()
     x.batch, x.batch_b, x.M, x.N, x.K = BH, 1 if b.dim() == 2 else b.shape[0], M, N, K
     x.granularity = _lib.GRANULARITY["per_row"]
@@ -44,34 +44,50 @@ def _stream(dev):
     return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
 
-def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
+# A sequence on the one shared array: a large tensor-core problem first, then
+# smaller ones with other K paddings, stream lengths and engine routes, so each
+# later call runs over bytes an earlier, different call left behind.
+SEQUENCE = [
+    # (BH, M, N, K, p, L, engine)
+    (1, 700, 300, 200, 8, 256, "auto"),    # e2m1 CTA pairs, two accumulators
+    (2, 65, 70, 90, 7, 128, "popc"),       # CUDA cores, codes padded 90 -> 96
+    (2, 65, 70, 96, 7, 128, "auto"),       # tensor cores plus the one-row strips
+    (1, 300, 64, 128, 7, 100, "auto"),     # e2m1 narrow tile, L < 2^p
+    (2, 65, 70, 96, 7, 128, "auto"),       # the third call again
+]
+
+
+def test_noalloc_matches_workspace_entry_point_over_a_sequence(cuda_device):
     dev = cuda_device
     lib = _lib.load()
-    random.seed(0)
-    cfg = ch.make_sobol_simple_config(96, 96, 7)
-    pool = device_pool(cfg, dev)
     g = torch.Generator().manual_seed(0)
-    for call in range(2):  # two calls in a row share (and reuse) the static scratch
-        a = torch.randn(2, 65, 96, generator=g).to(dev)
-        b = (torch.randn(70, 96, generator=g) * 0.05).to(dev)
-        bias = torch.randn(70, generator=g).to(dev)
-        out_ref = torch.empty(2, 65, 70, device=dev)
-        acc_ref = torch.empty(2, 65, 70, dtype=torch.int32, device=dev)
-        ref = _args(a, b, pool, out_ref, acc_ref, p=7, L=128, dims=96, bias=bias)
+    for call, (BH, M, N, K, p, L, engine) in enumerate(SEQUENCE):
+        random.seed(call)
+        cfg = ch.make_sobol_simple_config(K, K, p)
+        pool = device_pool(cfg, dev)
+        a = torch.randn(BH, M, K, generator=g).to(dev)
+        b = (torch.randn(N, K, generator=g) * 0.05).to(dev)
+        bias = torch.randn(N, generator=g).to(dev)
+        out_ref = torch.empty(BH, M, N, device=dev)
+        acc_ref = torch.empty(BH, M, N, dtype=torch.int32, device=dev)
+        ref = _args(a, b, pool, out_ref, acc_ref, p=p, L=L, dims=K, bias=bias, engine=engine)
         need = lib.scmp_sc_matmul_workspace_size(ctypes.byref(ref))
         assert 0 < need <= _lib.NOALLOC_SCRATCH_BYTES
-        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        # the workspace entry point on a workspace full of 0xFF bytes (NaN floats)
+        ws = torch.full((need,), 0xFF, dtype=torch.uint8, device=dev)
         ref.workspace, ref.workspace_bytes = ws.data_ptr(), need
         _lib.check(lib.scmp_sc_matmul(ctypes.byref(ref), _stream(dev)))
 
-        out = torch.full((2, 65, 70), float("nan"), device=dev)
-        acc = torch.full((2, 65, 70), -7, dtype=torch.int32, device=dev)
-        na = _args(a, b, pool, out, acc, p=7, L=128, dims=96, bias=bias)
+        out = torch.full((BH, M, N), float("nan"), device=dev)
+        acc = torch.full((BH, M, N), -7, dtype=torch.int32, device=dev)
+        na = _args(a, b, pool, out, acc, p=p, L=L, dims=K, bias=bias, engine=engine)
         _lib.check(lib.scmp_sc_matmul_noalloc(ctypes.byref(na), _stream(dev)))
         torch.cuda.synchronize(dev)
-        np.testing.assert_array_equal(acc.cpu().numpy(), acc_ref.cpu().numpy())
+        assert _lib.engine_status() == 0
+        np.testing.assert_array_equal(acc.cpu().numpy(), acc_ref.cpu().numpy(),
+                                      err_msg=f"call {call}")
         np.testing.assert_allclose(out.cpu().numpy(), out_ref.cpu().numpy(), rtol=RTOL,
-                                   atol=1e-30)
+                                   atol=1e-30, err_msg=f"call {call}")
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda_device):
