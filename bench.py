@@ -416,15 +416,15 @@ def run_reference(args):
 
 # ------------------------------------------------------------------ our arm
 
-def build_model(cfg_id: int, dev, dtype):
-    import torch
-
+def build_model(cfg_id: int, dev, dtype, depth: int = DEPTH, comp_blocks=None):
+    """The workload's SC-patched ViT-L/14 (``depth`` blocks of full width;
+    config 5's compensation on ``comp_blocks``, default blocks 1-22)."""
     from scmp_vit_b200 import config_helpers as ch
     from scmp_vit_b200 import vit
     from scmp_vit_b200.mp import MPConfig, SeededRandomMPConfig
 
     wl = WORKLOADS[cfg_id]
-    model = vit.vit_l14(seed=0).to(dev, dtype)
+    model = vit.vit_l14(seed=0, depth=depth).to(dev, dtype)
     p = wl["sc_prec"]
     if cfg_id == 3:
         vit.patch_vit(model, p, wl["ops"])
@@ -445,7 +445,8 @@ def build_model(cfg_id: int, dev, dtype):
                 return caches[key]
             return cfg_for
         vit.patch_vit(model, p, wl["ops"], block_cfg_for=block_cfg_for,
-                      comp_blocks=range(1, 23), comp_sc_prec=p)
+                      comp_blocks=range(1, 23) if comp_blocks is None else comp_blocks,
+                      comp_sc_prec=p)
     return model
 
 

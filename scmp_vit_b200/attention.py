@@ -32,6 +32,7 @@ from .mp import (
 )
 from .mp_linear import sc_prec_for_stoc_len
 from .noise_matmul import _noisy_matmul_core
+from .config_helpers import make_sobol_simple_config
 from .sc import sc_matmul
 
 CfgFor = Callable[[int, int], dict]
@@ -68,6 +69,55 @@ def _levels_by_prec(levels):
     for L in sorted({int(v) for v in levels if int(v) > 0}):
         by_prec.setdefault(sc_prec_for_stoc_len(L), []).append(L)
     return by_prec
+
+
+# det/sc_patch/sc_matmul.py keeps a pool cache of its own (``_CFG_CACHE`` at
+# :43-53), apart from sc_linear's; SCMatMul draws its pools from this one.
+_DET_CFG_CACHE: dict = {}
+
+
+def _det_get_config(D: int, sc_prec: int) -> dict:
+    """``(D, sc_prec)`` pool of the det ``SCMatMul``, created on first use."""
+    key = (D, sc_prec)
+    if key not in _DET_CFG_CACHE:
+        _DET_CFG_CACHE[key] = make_sobol_simple_config(D, D, sc_prec)
+    return _DET_CFG_CACHE[key]
+
+
+def _create_pools_in_first_use_order(cfg_for: CfgFor, D: int, levels,
+                                     order: Callable[[], list]) -> None:
+    """Pools drawn from Python's ``random`` depend on the order in which they
+    are first created.  The reference's bucket loops create a level's pool
+    when they first reach that level (head order for per-head MP, the levels
+    of each slice longest first for per-row MP), while the grouped launches
+    here run the precisions shortest first.  So when a cache-backed factory
+    lacks one of the pools, create them first in the reference's order
+    (``order()`` lists the levels so; it may read device data, once per
+    missing pool).  Other factories (e.g. LFSR pools seeded per block) do not
+    depend on the order and are left alone."""
+    cache = _scl._CFG_CACHE if cfg_for is _scl._get_config else (
+        _DET_CFG_CACHE if cfg_for is _det_get_config else None)
+    if cache is None:
+        return
+    if all((D, sc_prec_for_stoc_len(int(L))) in cache for L in levels if int(L) > 0):
+        return
+    for L in order():
+        if int(L) > 0:
+            cfg_for(D, sc_prec_for_stoc_len(int(L)))
+
+
+def _levels_in_slice_order(row_L: torch.Tensor, levels) -> list:
+    """Levels of ``row_L`` [S, N] in the order a loop over slices, each
+    visiting its non-empty levels longest first, first reaches them."""
+    desc = sorted({int(v) for v in levels}, reverse=True)
+    lut = torch.tensor(desc, dtype=row_L.dtype, device=row_L.device)
+    present = (row_L.unsqueeze(-1) == lut).any(dim=1).cpu().tolist()  # [S][levels]
+    seen: list = []
+    for row in present:
+        for L, has in zip(desc, row):
+            if has and L not in seen:
+                seen.append(L)
+    return seen
 
 
 def _run_levels(a, b, table: torch.Tensor, levels, per: str, *, granularity: str, mode: str,
@@ -175,6 +225,9 @@ def sc_qk(q: torch.Tensor, k: torch.Tensor, sc_prec: int, *, mp_cfg=None,
         maxL = max(int(v) for v in mp_cfg.stoc_len_levels)
         AutoMPBudgetLogger.record(get_current_block_idx(), "qk", B * H * N * N * maxL,
                                   head_L.clamp(min=0).to(torch.float64).sum() * B * N * N)
+    if not _scl.USE_NOISE_MODEL:  # reference order: buckets by first head (:168-197)
+        _create_pools_in_first_use_order(cfg_for, D, mp_cfg.stoc_len_levels,
+                                         lambda: list(dict.fromkeys(head_L.tolist())))
     slice_L = head_L.to(torch.int32).repeat(B)  # slice b*H + h -> head h
     out = torch.empty(B * H, N, N, dtype=torch.float32, device=q.device)
     counts = None if isinstance(mp_cfg, AdaptiveMPConfig) and mp_cfg.target_fractions is None \
@@ -225,6 +278,10 @@ def sc_av(attn: torch.Tensor, v: torch.Tensor, sc_prec: int, *, mode: str = "bip
     else:
         row_L = quantile_levels_batched(score, mp_cfg.stoc_len_levels, mp_cfg.level_fractions)
     row_L = row_L.reshape(-1).to(torch.int32)
+    if not _scl.USE_NOISE_MODEL:  # reference order: per (b, h), longest level first (:217-240)
+        _create_pools_in_first_use_order(
+            cfg_for, N, mp_cfg.stoc_len_levels,
+            lambda: _levels_in_slice_order(row_L.reshape(B * H, N), mp_cfg.stoc_len_levels))
     if AutoMPBudgetLogger.enabled:
         maxL = max(int(x) for x in mp_cfg.stoc_len_levels)
         AutoMPBudgetLogger.record(get_current_block_idx(), "av", B * H * N * D * maxL,
@@ -364,9 +421,13 @@ class SCMatMul(nn.Module):
             else:
                 sl = classify_rows_by_metric(metric, cfg.stoc_len_levels,
                                              cfg.level_fractions).row_levels
+            # reference order: the assignment's levels, longest first (:113-136)
+            _create_pools_in_first_use_order(
+                _det_get_config, K, cfg.stoc_len_levels,
+                lambda: _levels_in_slice_order(sl.reshape(1, -1), cfg.stoc_len_levels))
             _run_levels(A_flat, B_rm, sl.to(torch.int32), cfg.stoc_len_levels, "slice",
                         granularity="per_row", mode=self.mode, D_pool=K,
-                        cfg_for=_scl._get_config, out=out)
+                        cfg_for=_det_get_config, out=out)
         elif cfg is not None and self.op == "av":
             row_max = A_flat.amax(dim=-1)  # (BH, M)
             if isinstance(cfg, AdaptiveMPConfig):
@@ -376,11 +437,15 @@ class SCMatMul(nn.Module):
                                   for i in range(BH)])
             else:
                 rl = quantile_levels_batched(row_max, cfg.stoc_len_levels, cfg.level_fractions)
+            # reference order: per slice, its levels longest first (:139-160)
+            _create_pools_in_first_use_order(
+                _det_get_config, K, cfg.stoc_len_levels,
+                lambda: _levels_in_slice_order(rl.reshape(BH, M), cfg.stoc_len_levels))
             _run_levels(A_flat, B_rm, rl.reshape(-1).to(torch.int32), cfg.stoc_len_levels,
                         "row", granularity="per_row", mode=self.mode, D_pool=K,
-                        cfg_for=_scl._get_config, out=out)
+                        cfg_for=_det_get_config, out=out)
         else:
             sc_matmul(A_flat, B_rm, granularity="per_row", group_a=1, group_b=1, mode=self.mode,
-                      sc_prec=self.sc_prec, config=_scl._get_config(K, self.sc_prec),
+                      sc_prec=self.sc_prec, config=_det_get_config(K, self.sc_prec),
                       stoc_len=self.stoc_len, out=out)
         return out.reshape(*lead, M, N).to(A.dtype)

@@ -46,6 +46,7 @@ __all__ = [
     "make_sobol_altseed_config",
     "make_lfsr_config",
     "pool_table",
+    "config_from_table",
     "det_kernel_tuning",
 ]
 
@@ -191,6 +192,17 @@ def make_lfsr_config(D_a: int, D_b: int, sc_prec: int, seed: int = 0) -> dict:
         "seed": int(seed), "state0": state0,
         "table": lfsr16_table(state0, p),
     })
+
+
+def config_from_table(table, sc_prec: int) -> dict:
+    """A config around an explicit uint8 pool ``table`` ``[D, 2**sc_prec]``,
+    e.g. a pool recorded from another run or generated elsewhere."""
+    p = _check_prec(sc_prec)
+    tab = np.ascontiguousarray(table, dtype=np.uint8)
+    if tab.ndim != 2 or tab.shape[1] != (1 << p):
+        raise ValueError(f"pool table must be [D, {1 << p}], got {tab.shape}")
+    return _finish({"kind": "table", "sc_prec": p, "dims": int(tab.shape[0]),
+                    "dims_a": int(tab.shape[0]), "table": tab})
 
 
 def pool_table(cfg: dict) -> np.ndarray:

@@ -86,8 +86,9 @@ class PackedWeight:
     ``N * K * 2**sc_prec`` (int8 bytes)."""
 
     def __init__(self, buf: torch.Tensor, N: int, K: int, granularity: str, mode: str,
-                 sc_prec: int, config: dict, group_b: int):
+                 sc_prec: int, config: dict, group_b: int, source: Optional[torch.Tensor] = None):
         self.buf = buf
+        self.source = source  # the weight it was packed from (not read by the engine)
         self.N, self.K = N, K
         self.granularity, self.mode, self.sc_prec = granularity, mode, sc_prec
         self.config = config
@@ -153,7 +154,7 @@ def prepack_b(b: torch.Tensor, *, granularity: str = "per_row", mode: str = "bip
         stream = torch.cuda.current_stream(dev).cuda_stream
         _lib.check(lib.scmp_prepack_b(ctypes.byref(args), ctypes.c_void_p(buf.data_ptr()),
                                       nbytes, ctypes.c_void_p(stream)))
-    return PackedWeight(buf, N, K, granularity, mode, p, config, max(int(group_b), 1))
+    return PackedWeight(buf, N, K, granularity, mode, p, config, max(int(group_b), 1), source=b)
 
 
 @torch.no_grad()
