@@ -87,7 +87,11 @@ def test_gathered_logits_match_single_process(world, gb):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    ref = _forward(_model(), _images(gb))
+    from scmp_vit_b200 import sc_linear
+    try:
+        ref = _forward(_model(), _images(gb))
+    finally:
+        sc_linear.set_noise_model(False)  # the switch is process-wide
     assert full.shape == (gb, 1000)
     torch.testing.assert_close(full, ref, rtol=0, atol=0)
 

@@ -59,6 +59,7 @@ def engine_is_oracle(monkeypatch):
     from scmp_vit_b200 import attention, sc_linear
     monkeypatch.setattr(attention, "sc_matmul", oracle_sc_matmul)
     monkeypatch.setattr(sc_linear, "sc_matmul", oracle_sc_matmul)
+    monkeypatch.setattr(sc_linear, "USE_NOISE_MODEL", False)
 
 
 @pytest.mark.parametrize("name", [n for n, *_ in dropin_cases.det_cases()])

@@ -55,6 +55,12 @@ def _check(got: np.ndarray, want: np.ndarray, what: str):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"{what}: not bit-equal"
 
 
+@pytest.fixture(autouse=True)
+def _no_noise_surrogate(monkeypatch):
+    from scmp_vit_b200 import sc_linear
+    monkeypatch.setattr(sc_linear, "USE_NOISE_MODEL", False)
+
+
 @pytest.mark.parametrize("i", range(len(META["calls"])))
 def test_recorded_reference_call_on_the_engine(cuda_device, i):
     c = META["calls"][i]
