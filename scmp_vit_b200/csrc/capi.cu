@@ -155,15 +155,23 @@ int validate(const scmp_matmul_args *x) {
 
 int64_t seg_len(const scmp_matmul_args *x) { return x->k_segment > 0 ? x->k_segment : x->K; }
 
-// A weight that can be prepacked: one b slice, one K segment, a pool row per
-// reduction index, and 8-bit thresholds that fit the byte compare.
+// A weight that can be prepacked: one b slice, a pool row per reduction index
+// (per index inside its segment for segmented K), and 8-bit thresholds that
+// fit the byte compare.  Segmented K packs e2m1 bytes for the e2m1 pairs only
+// (sc_prec 7 or 8, segments of whole multiples of 8 indices).
 int check_packable(const scmp_matmul_args *x) {
   if (x->batch_b != 1) return fail(SCMP_EINVAL, "prepacked b needs batch_b = 1");
-  if (x->k_segment != 0 && x->k_segment != x->K)
-    return fail(SCMP_EINVAL, "prepacked b needs k_segment = 0");
   if (x->sc_prec < 5 || (x->mode == SCMP_UNIPOLAR && x->sc_prec == 8))
     return fail(SCMP_EUNSUPPORTED, "prepacked b needs 5 <= sc_prec <= 8 (not unipolar p = 8)");
-  if (x->pool_dims < x->K) return fail(SCMP_EINVAL, "prepacked b needs pool_dims >= K");
+  if (x->k_segment > 0 && x->k_segment != x->K) {
+    if (x->sc_prec < 7 || (x->k_segment % 8) != 0)
+      return fail(SCMP_EUNSUPPORTED,
+                  "prepacked segmented b needs sc_prec 7 or 8 and k_segment % 8 == 0");
+    if (x->pool_dims < x->k_segment)
+      return fail(SCMP_EINVAL, "prepacked b needs pool_dims >= k_segment");
+  } else if (x->pool_dims < x->K) {
+    return fail(SCMP_EINVAL, "prepacked b needs pool_dims >= K");
+  }
   const int64_t ldk = (x->K + 7) / 8 * 8;
   if ((ldk << x->sc_prec) >= ((int64_t)1 << 31))
     return fail(SCMP_EUNSUPPORTED, "prepacked b rows of %lld bytes are too long",
@@ -186,11 +194,21 @@ struct PackPlan {
 PackPlan make_pack_plan(const scmp_matmul_args *x) {
   PackPlan p;
   Carver c;
-  p.ldk = (x->K + 7) / 8 * 8;
-  p.e2m1 = (x->sc_prec == 7 || x->sc_prec == 8) && x->N > 128 &&
-           (p.ldk << x->sc_prec) < ((int64_t)1 << 24);
-  p.B.g = make_groups(x->granularity, 1, x->N, x->group_b);
-  layout_operand(c, p.B, x->K, p.ldk);
+  const int64_t kseg = seg_len(x), nseg = x->K / kseg;
+  if (nseg > 1) {
+    // segment rows of kseg codes back to back ([N * nseg, kseg] = [N, K]),
+    // one scale group per (row, segment); e2m1 bytes for the segmented pairs
+    p.ldk = x->K;
+    p.e2m1 = true;
+    p.B.g = make_groups(SCMP_PER_ROW, 1, x->N * nseg, 1);
+    layout_operand(c, p.B, kseg, kseg);
+  } else {
+    p.ldk = (x->K + 7) / 8 * 8;
+    p.e2m1 = (x->sc_prec == 7 || x->sc_prec == 8) && x->N > 128 &&
+             (p.ldk << x->sc_prec) < ((int64_t)1 << 24);
+    p.B.g = make_groups(x->granularity, 1, x->N, x->group_b);
+    layout_operand(c, p.B, x->K, p.ldk);
+  }
   p.pool_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
   p.pool_comp = c.take((size_t)p.pool_rows << x->sc_prec);
   p.streams = c.take((size_t)x->N * (size_t)(p.ldk << x->sc_prec) >> (p.e2m1 ? 1 : 0));
@@ -338,7 +356,8 @@ int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_byt
     return fail(SCMP_EINVAL, "packed buffer must be %zu-byte aligned", kAlign);
   auto *pb = static_cast<unsigned char *>(packed);
   auto s = static_cast<cudaStream_t>(stream);
-  if ((rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, pk.B, x.K, x.mode,
+  const int64_t kseg = seg_len(&x);
+  if ((rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, pk.B, kseg, x.mode,
                              x.sc_prec, pb, s)) != SCMP_OK)
     return rc;
   const int shift = (x.mode == SCMP_BIPOLAR && x.sc_prec == 8) ? 1 : 0;
@@ -347,9 +366,8 @@ int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_byt
                                   false, pb + pk.pool_comp, s)) != cudaSuccess)
     return cuda_fail(e, "pool_complement launch");
   if ((e = launch_pack_b_streams(reinterpret_cast<const int16_t *>(pb + pk.B.code), x.N, pk.ldk,
-                                 x.sc_prec, shift, pk.e2m1, pb + pk.pool_comp, pb + pk.streams,
-                                 s)) !=
-      cudaSuccess)
+                                 x.sc_prec, shift, pk.e2m1, kseg < x.K ? kseg : 0,
+                                 pb + pk.pool_comp, pb + pk.streams, s)) != cudaSuccess)
     return cuda_fail(e, "pack_b_streams launch");
   count_launches(2);
   return SCMP_OK;

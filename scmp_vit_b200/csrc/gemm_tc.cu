@@ -320,6 +320,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                 "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+               "r"(v[7])
+               : "memory");
+}
+
 // K-major, 128-byte-swizzled UMMA shared-memory descriptor: 8-row atoms of
 // 128 B (1024 B apart), version 1, layout SWIZZLE_128B.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
@@ -406,15 +420,17 @@ __device__ __forceinline__ void publish_stage(const Bars &b, ProdState &st, int 
   }
 }
 
-// Segmented tiles: 16 columns (half `h` of 32-column chunk `cc`) of this
-// warp's rows after segment `sd` -- rescale the int32 counts with the
-// segment's scales and add the fp32 sum of the earlier segments (held in
-// TMEM columns 2 BN ..).  Result in y (fp32 bits).
-template <int BN>
-__device__ __forceinline__ void seg_chunk(const TcParams &prm, uint32_t tmem_base, int lane,
-                                          int sd, int cc, int h, int acc_j, int quarter,
-                                          int64_t grow, bool row_ok, int L, int64_t slice_b,
-                                          int64_t n0, uint32_t (&y)[16]) {
+// Segmented tiles: 16 accumulator columns of this warp's 32 rows after
+// segment `sd` -- rescale the counts (int32, or with kF32 the e2m1 tiles'
+// exact fp32 counts) with the segment's scales and add the fp32 sum of the
+// earlier segments.  acc_col / run_col: TMEM columns of the counts and of the
+// running sums; gn0: the b row of the first column.  Result in y (fp32 bits).
+template <bool kF32, int W = 16>
+__device__ __forceinline__ void seg_chunk16(const TcParams &prm, uint32_t lanebase, int lane,
+                                            int sd, uint32_t acc_col, uint32_t run_col,
+                                            int64_t gn0, int64_t grow, bool row_ok, int L,
+                                            int64_t slice_b, uint32_t (&y)[W]) {
+  static_assert(W == 8 || W == 16, "8 or 16 columns");
   const GemmProblem &P = prm.P;
   float sa = 0.f;
   int za = 0, rsa = 0;
@@ -424,7 +440,7 @@ __device__ __forceinline__ void seg_chunk(const TcParams &prm, uint32_t tmem_bas
     za = P.qa.zero[ra];
     rsa = P.qa.rowsum[ra];
   }
-  const int64_t gn = n0 + cc * 32 + h * 16 + (lane & 15);
+  const int64_t gn = gn0 + (lane & (W - 1));
   float sbl = 0.f;
   int zbl = 0, rsbl = 0;
   if (gn < prm.n_rows) {
@@ -433,22 +449,44 @@ __device__ __forceinline__ void seg_chunk(const TcParams &prm, uint32_t tmem_bas
     zbl = P.qb.zero[rb];
     rsbl = P.qb.rowsum[rb];
   }
-  const uint32_t col = (uint32_t)(acc_j * BN + cc * 32 + h * 16);
-  const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
-  uint32_t f[16];
-  tmem_ld16(lanebase + col, y);
-  if (sd > 0) tmem_ld16(lanebase + (uint32_t)(2 * BN) + col, f);
+  uint32_t f[W];
+  if constexpr (W == 16) {
+    tmem_ld16(lanebase + acc_col, y);
+    if (sd > 0) tmem_ld16(lanebase + run_col, f);
+  } else {
+    tmem_ld8(lanebase + acc_col, y);
+    if (sd > 0) tmem_ld8(lanebase + run_col, f);
+  }
+  // the row's rescale factor F = 2^(2p) / (u L), once per call (bit-identical
+  // to computing it per element: it depends on the row only)
+  const bool live = row_ok && L > 0;
+  const float F = live ? sc_rescale_factor(P.mode, P.prec, L) : 0.0f;
+  const bool unipolar = P.mode != SCMP_BIPOLAR;  // bipolar needs no zero points
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < W; ++i) {
     const float sb = __shfl_sync(0xffffffffu, sbl, i);
-    const int zb = __shfl_sync(0xffffffffu, zbl, i);
-    const int rsb = __shfl_sync(0xffffffffu, rsbl, i);
-    const float r = (row_ok && L > 0) ? sc_rescale(P.mode, P.prec, L, (int32_t)y[i], prm.kseg, sa,
-                                                   za, rsa, sb, zb, rsb)
-                                      : 0.0f;
+    int zb = 0, rsb = 0;
+    if (unipolar) {
+      zb = __shfl_sync(0xffffffffu, zbl, i);
+      rsb = __shfl_sync(0xffffffffu, rsbl, i);
+    }
+    const int32_t cnt = kF32 ? __float2int_rn(__uint_as_float(y[i])) : (int32_t)y[i];
+    const float r = live ? sc_rescale_f(P.mode, F, cnt, prm.kseg, sa, za, rsa, sb, zb, rsb) : 0.0f;
     y[i] = __float_as_uint(sd == 0 ? r : __fadd_rn(__uint_as_float(f[i]), r));
   }
+}
+
+// The 2-accumulator layout of the int8 tiles: half `h` of 32-column chunk
+// `cc` of accumulator acc_j, running sums in TMEM columns 2 BN ..
+template <int BN>
+__device__ __forceinline__ void seg_chunk(const TcParams &prm, uint32_t tmem_base, int lane,
+                                          int sd, int cc, int h, int acc_j, int quarter,
+                                          int64_t grow, bool row_ok, int L, int64_t slice_b,
+                                          int64_t n0, uint32_t (&y)[16]) {
+  const uint32_t col = (uint32_t)(acc_j * BN + cc * 32 + h * 16);
+  seg_chunk16<false>(prm, tmem_base + ((uint32_t)(quarter * 32) << 16), lane, sd, col,
+                     (uint32_t)(2 * BN) + col, n0 + cc * 32 + h * 16, grow, row_ok, L, slice_b, y);
 }
 
 // End of a non-final segment: wait for its MMAs, fold the int32 counts into
@@ -482,6 +520,42 @@ __device__ bool segment_drain(const TcParams &prm, const Bars &b, ProdState &st,
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
   tc_fence_before();
   mbar_arrive(b.tempty);
+  ++st.g;
+  return true;
+}
+
+// End of a non-final segment of a one-accumulator e2m1 pair tile (the CTA's
+// 128 a rows in TMEM lanes, ncols fp32 count columns): wait for the segment's
+// MMAs, fold the counts into the fp32 running sums in TMEM columns
+// [ncols, 2 ncols), then hand the accumulator back to the pair's MMA thread
+// (one cluster arrival per CTA once all of its producers are done).  n0: the
+// tile's first b row (the accumulator covers both CTAs' b rows).
+__device__ bool segment_drain_pair(const TcParams &prm, const Bars &b, ProdState &st,
+                                   uint32_t tmem_base, int warp, int lane, int sd, int64_t slice,
+                                   int64_t slice_b, int64_t m0, int64_t n0) {
+  const GemmProblem &P = prm.P;
+  const int ncols = prm.ncols;
+  if (!mbar_wait(b.tfull, (uint32_t)(st.g & 1), b.abort)) return false;
+  tc_fence_after();
+  const int pw = warp - 1;
+  const int quarter = warp & 3;  // the TMEM lanes this warp may access
+  const int64_t gm = m0 + quarter * 32 + lane;
+  const bool row_ok = gm < prm.m_rows;
+  const int64_t grow = slice * P.M + gm;
+  const int L = row_ok ? row_stream_len(P, slice, grow) : -1;
+  const uint32_t lanebase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+  for (int c = 8 * (pw >> 2); c < ncols; c += 32) {  // the quarter's 4 warps share the columns
+    uint32_t y[8];
+    seg_chunk16<true, 8>(prm, lanebase, lane, sd, (uint32_t)c, (uint32_t)(ncols + c), n0 + c,
+                         grow, row_ok, L, slice_b, y);
+    tmem_st8(lanebase + (uint32_t)(ncols + c), y);
+  }
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  tc_fence_before();
+  mbar_arrive(b.epi);
+  if (!mbar_wait(b.epi, (uint32_t)(st.g & 1), b.abort)) return false;
+  if (threadIdx.x == 32) mbar_arrive_cluster(b.tempty_cl);
   ++st.g;
   return true;
 }
@@ -1051,11 +1125,17 @@ __device__ __forceinline__ uint32_t stream_word_e2m1(uint32_t u, uint32_t rep, u
 // rows is stored as zeros, one inside all of them as the sign pattern, both
 // without arithmetic (exact; pays where windows are all short or all long,
 // e.g. softmax rows in Attn@V).
-template <int LG, int NS, bool kNoB, bool kOneAcc, bool kSkipA = false>
+// kSeg (one-accumulator pair tiles): K in segments of prm.kseg indices; the
+// pool rows restart at every segment, and after each non-final segment the
+// producers fold its counts into the running sums (segment_drain_pair, which
+// needs tmem_base, warp and the tile's first b row n0_tile).
+template <int LG, int NS, bool kNoB, bool kOneAcc, bool kSkipA = false, bool kSeg = false>
 __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &st,
                                  uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
-                                 int64_t slice_b, int64_t m0, int64_t n0, int nb) {
+                                 int64_t slice_b, int64_t m0, int64_t n0, int nb,
+                                 uint32_t tmem_base = 0, int warp = 0, int64_t n0_tile = 0) {
   static_assert(LG == 7 || LG == 8, "e2m1 producers take Lp = 128 or 256");
+  static_assert(!kSeg || kOneAcc, "segments run on one-accumulator tiles");
   if (!producers_released(b.abort)) return false;  // give-up path test hook
   constexpr int G = (8 << LG) / 256;  // k-blocks per macro step of 8 indices: 4 or 8
   constexpr int LPB = 1 << LG;
@@ -1110,12 +1190,16 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
       prefetch_l1(P.pool_comp + (size_t)prow * LPB + 128 * lane);
   };
   int pbase = 0;
+  const int msteps_seg = kSeg ? prm.kseg >> 3 : 0;  // macro steps per segment
+  int mseg = 0;                                     // macro steps done in the segment
   uint4 ca_n = ld_stream_v4(pa), cb_n = make_uint4(0, 0, 0, 0);
   // One-accumulator tiles (8 a words per thread) have the registers to load
   // the next stage's pool complement words one stage ahead, keeping their
   // latency off each stage's acquire -> store -> publish chain; the others
   // load them at the top of the stage.
-  constexpr bool kAheadPC = kOneAcc;
+  // (Segmented tiles leave those 16 registers to the segment drain: 17 warps
+  // give each thread at most 96.)
+  constexpr bool kAheadPC = kOneAcc && !kSeg;
   uint4 qn0 = make_uint4(0, 0, 0, 0), qn1 = qn0, qn2 = qn0, qn3 = qn0;
   if constexpr (!kNoB) {
     if (doB) {
@@ -1137,15 +1221,18 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
       ca_n = ld_stream_v4(pa + mc + 1);
       if (!kNoB && doB) cb_n = ld_stream_v4(pb + mc + 1);
     }
-    if constexpr (!kNoB) prefetch_macro(pbase + 8);
+    const bool seg_end = kSeg && mseg + 1 == msteps_seg;  // the next step starts a segment
+    if constexpr (!kNoB) prefetch_macro(seg_end ? 0 : pbase + 8);
     const uint8_t *pcm = pc_thr + (size_t)pbase * LPB;
+    // pool rows of the next macro step: 8 rows on, or row 0 of a new segment
+    const uint8_t *pcm_next = seg_end ? pc_thr : pcm + 256 * G;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       uint4 q0 = qn0, q1 = qn1, q2 = qn2, q3 = qn3;
       if (kAheadPC && !kNoB && doB && (j + 1 < G || mc + 1 < nmacro)) {
-        // stage j + 1 of this macro step, or stage 0 of the next one (which
-        // starts 8 rows = 8 LPB bytes later)
-        const uint4 *pc = reinterpret_cast<const uint4 *>(pcm + 256 * (j + 1));
+        // stage j + 1 of this macro step, or stage 0 of the next one
+        const uint4 *pc = reinterpret_cast<const uint4 *>(j + 1 < G ? pcm + 256 * (j + 1)
+                                                                    : pcm_next);
         qn0 = __ldg(pc);
         qn1 = __ldg(pc + 1);
         qn2 = __ldg(pc + 2);
@@ -1208,6 +1295,17 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
       if ((G / NS) & 1) st.phase ^= 1u;
     }
     pbase += 8;
+    if constexpr (kSeg) {
+      if (++mseg == msteps_seg) {
+        mseg = 0;
+        pbase = 0;
+        // ---- end of a segment (the last one drains in the epilogue)
+        if (mc + 1 < nmacro &&
+            !segment_drain_pair(prm, b, st, tmem_base, warp, lane, (mc + 1) / msteps_seg - 1,
+                                slice, slice_b, m0, n0_tile))
+          return false;
+      }
+    }
   }
   return true;
 }
@@ -1236,8 +1334,11 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
     const int quarter = warp & 3;            // TMEM lanes this warp may access
     const int acc_j = kOneAcc ? 0 : (pw >> 2) & 1;  // accumulator (a rows 0-127 / 128-255)
     const int col_half = pw >> 3;            // which half of the BN columns
-    const int cc_begin = kOneAcc ? (pw >> 2) : col_half * (BN / 64);
-    const int cc_end = kOneAcc ? (ncols + 31) / 32 : (col_half + 1) * (BN / 64);
+    // two accumulators: each column half takes ceil(ncols / 64) 32-column
+    // chunks (BN / 64 of them on the int8 tiles)
+    const int per_half = kF32 ? (ncols + 63) / 64 : BN / 64;
+    const int cc_begin = kOneAcc ? (pw >> 2) : col_half * per_half;
+    const int cc_end = kOneAcc ? (ncols + 31) / 32 : (col_half + 1) * per_half;
     const int cc_step = kOneAcc ? 4 : 1;
     float *stg = reinterpret_cast<float *>(smem) + pw * (32 * 33);
     int4 *rowp = reinterpret_cast<int4 *>(smem + kProducerWarps * 32 * 33 * 4) + pw * 32;
@@ -1264,7 +1365,27 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
 #pragma unroll 1
     for (int cc = cc_begin; cc < cc_end; cc += cc_step) {
       if (kF32 && cc * 32 >= ncols) break;  // warp-uniform
-      if constexpr (kSeg) {
+      if constexpr (kSeg && kF32) {
+        // last segment of an e2m1 tile: accumulator acc_j's counts in columns
+        // acc_j ncols + c, its running sums (kOneAcc ? 1 : 2) ncols further on
+        const uint32_t acc0 = (uint32_t)(acc_j * ncols);
+        const uint32_t run0 = (uint32_t)((kOneAcc ? 1 : 2) * ncols) + acc0;
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          const int c = cc * 32 + h * 8;
+          uint32_t v[8];
+          if (c < ncols) {
+            seg_chunk16<true, 8>(prm, tmem_base + ((uint32_t)(quarter * 32) << 16), lane,
+                                 prm.nseg - 1, acc0 + (uint32_t)c, run0 + (uint32_t)c, n0 + c,
+                                 grow0 + lane, mrow0 + lane < prm.m_rows, myL, slice_b, v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0u;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) stg[lane * 33 + h * 8 + i] = __uint_as_float(v[i]);
+        }
+      } else if constexpr (kSeg) {
         // last segment: finished fp32 values (rescaled and summed in order)
 #pragma unroll 1
         for (int h = 0; h < 2; ++h) {
@@ -1321,12 +1442,15 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
   // every producer is done with the staging area before anyone refills it
   // (a bounded mbarrier wait, not bar.sync: an aborting thread must not
   // leave the others blocked)
+  // On CTA pairs the epi barrier completes once per (tile, segment) --
+  // segment_drain_pair uses it too -- so its phase is that of st.g (= it when
+  // unsegmented); single-CTA tiles use it once per tile.
   if constexpr (kPair) {
     // one thread per CTA hands the accumulators back to the even CTA's MMA
     // thread once every producer of this CTA has read them
     tc_fence_before();
     mbar_arrive(b.epi);
-    if (!mbar_wait(b.epi, (uint32_t)(it & 1), b.abort)) return false;
+    if (!mbar_wait(b.epi, (uint32_t)(st.g & 1), b.abort)) return false;
     if (threadIdx.x == 32) mbar_arrive_cluster(b.tempty_cl);
   } else {
     mbar_arrive(b.epi);
@@ -1807,20 +1931,31 @@ __device__ __forceinline__ void tc_mma_mxf4_pair(uint32_t tmem_d, uint64_t adesc
 // columns, M = 256 MMAs once per 64 positions); stages are 32 KB.  Taken when
 // one 512-row tile would be half empty or the b side is narrow (Q@K^T and
 // Attn@V per head: 256 x 256 and 256 x 64).
-template <bool kOneAcc>
+template <bool kOneAcc, int kNStages = kPairStages>
 struct Fp4PairCfg {
   static constexpr uint32_t kStageA = (kOneAcc ? 128 : 256) * kKB;
   static constexpr uint32_t kStage = kStageA + kPairStageB;
-  // four stages either way (six 32 KB stages measured no faster on Q@K^T)
-  static constexpr int kStages = kPairStages;
+  // four stages (six 32 KB stages measured no faster on Q@K^T or on the
+  // segmented compensation tiles)
+  static constexpr int kStages = kNStages;
   static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 /*align*/ + 256;
   static_assert(kStages * kStage >= kEpiStagingBytes, "the ring holds the epilogue staging");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
+// Ring depth of the segmented one-accumulator tiles (six measured no faster
+// on the compensation shape than four).
+constexpr int kSegPairStages = 4;
 
-template <int LG, bool kPackedB, bool kOneAcc>
+// kSeg (one accumulator): K in prm.nseg segments of prm.nkb_seg k-blocks; the
+// MMA thread restarts the accumulator at every segment and waits for the
+// producers' drain of the previous one (tempty); the fp32 running sums live in
+// TMEM columns [ncols, 2 ncols) (ncols <= 240).  Two accumulators would leave
+// room for 112 columns only and measured slower on the compensation shape.
+template <int LG, bool kPackedB, bool kOneAcc, bool kSeg = false>
 __global__ void __launch_bounds__(kThreads + 32, 1)
     gemm_tc_pair_fp4_kernel(const TcParams prm, const __grid_constant__ CUtensorMap tmap) {
-  using Cfg = Fp4PairCfg<kOneAcc>;
+  static_assert(!kSeg || kOneAcc, "segments run on one-accumulator tiles");
+  using Cfg = Fp4PairCfg<kOneAcc, kSeg ? kSegPairStages : kPairStages>;
   constexpr uint32_t kTmemAlloc = 512;
   constexpr int kAcc = kOneAcc ? 1 : 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -1895,36 +2030,40 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int64_t g = 0;
-      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++g) {
-        if (g > 0) ok = mbar_wait_cl(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
-        if (!ok) break;
-        tc_fence_after();
-        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
-          if (!mbar_wait(&b.full[stage], phase, b.abort) ||
-              !mbar_wait_cl(&b.pfull[stage], phase, b.abort)) {
-            ok = false;
-            break;
-          }
+      int64_t g = 0;  // one per (tile, segment), as on the producer side
+      const int nseg = kSeg ? prm.nseg : 1;
+      const int64_t nkb_seg = kSeg ? prm.nkb_seg : prm.nkb;
+      for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters) {
+        for (int seg = 0; seg < nseg && ok; ++seg, ++g) {
+          if (g > 0) ok = mbar_wait_cl(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t a0 = smem0 + stage * Cfg::kStage;
-          const uint32_t b0 = a0 + Cfg::kStageA;
-#pragma unroll
-          for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
-            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
-#pragma unroll
-            for (int j = 0; j < kAcc; ++j) {
-              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
-              // a and b read their (all-equal) scale factors from the same columns
-              tc_mma_mxf4_pair(tmem_base + (uint32_t)(j * ncols), adesc, bdesc, idesc, sf, sf,
-                               (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int64_t kb = 0; kb < nkb_seg; ++kb) {
+            if (!mbar_wait(&b.full[stage], phase, b.abort) ||
+                !mbar_wait_cl(&b.pfull[stage], phase, b.abort)) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            const uint32_t a0 = smem0 + stage * Cfg::kStage;
+            const uint32_t b0 = a0 + Cfg::kStageA;
+#pragma unroll
+            for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
+              const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+              for (int j = 0; j < kAcc; ++j) {
+                const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+                // a and b read their (all-equal) scale factors from the same columns
+                tc_mma_mxf4_pair(tmem_base + (uint32_t)(j * ncols), adesc, bdesc, idesc, sf, sf,
+                                 (kb > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            tc_commit_pair_both(&b.empty[stage]);
+            if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
           }
-          tc_commit_pair_both(&b.empty[stage]);
-          if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
+          if (!ok) break;
+          tc_commit_pair_both(b.tfull);
         }
-        if (!ok) break;
-        tc_commit_pair_both(b.tfull);
       }
       tc_commit_pair_local(b.drain);
       mbar_wait_own_cl(b.drain, 0);
@@ -1956,8 +2095,11 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++it) {
         const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
         const int nb0 = (int)((rem / prm.tiles_m) * ncols + (int64_t)rank * (ncols / 2));
-        // the previous tile's epilogue stages its transpose in the ring
-        if (it > 0 && !mbar_wait(b.epi, (uint32_t)((it - 1) & 1), b.abort)) break;
+        // the previous tile's epilogue stages its transpose in the ring (the
+        // epi barrier completes once per segment: the epilogue is the tile's
+        // last completion)
+        const int64_t epi_done = it * (kSeg ? prm.nseg : 1) - 1;
+        if (it > 0 && !mbar_wait(b.epi, (uint32_t)(epi_done & 1), b.abort)) break;
         for (int64_t kb = 0; kb < prm.nkb; ++kb) {
           if (!mbar_wait(&b.empty[stage], phase ^ 1, b.abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&b.full[stage], bytes);
@@ -1981,12 +2123,12 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       const int64_t m0 = (rem % prm.tiles_m) * (2 * kRowsA) + (int64_t)rank * kRowsA;
       const int64_t n0 = (rem / prm.tiles_m) * ncols;
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
-      if (!produce_rows_fp4<LG, Cfg::kStages, kPackedB, kOneAcc>(
+      if (!produce_rows_fp4<LG, Cfg::kStages, kPackedB, kOneAcc, false, kSeg>(
               prm, b, st, smem_s, Cfg::kStageA, lane, slice, slice_b, m0,
-              n0 + (int64_t)rank * half, half))
+              n0 + (int64_t)rank * half, half, tmem_base, warp, n0))
         break;
-      if (!tile_epilogue<256, false, true, true, kOneAcc>(prm, b, st, smem, tmem_base, warp, lane,
-                                                          slice, slice_b, m0, n0, it))
+      if (!tile_epilogue<256, kSeg, true, true, kOneAcc>(prm, b, st, smem, tmem_base, warp, lane,
+                                                         slice, slice_b, m0, n0, it))
         break;
     }
   }
@@ -2320,8 +2462,10 @@ cudaError_t launch_pair(TcParams prm, int dev, cudaStream_t s) {
 // 32 columns (epilogue, a rows generated again), the wider tile on ties.  One
 // accumulator leaves room for 256 columns; a b side that fits one tile is
 // taken whole (a multiple of 16, at least 16: the M = 256 MMA's N).
-int fp4_tile_cols(int64_t n_rows, bool one_acc) {
-  const int max_cols = one_acc ? 256 : kFp4MaxCols;
+// Segmented tiles keep fp32 running sums next to the accumulator, so they
+// also stay within kFp4MaxCols.
+int fp4_tile_cols(int64_t n_rows, bool one_acc, bool seg = false) {
+  const int max_cols = one_acc && !seg ? 256 : kFp4MaxCols;
   if (n_rows <= max_cols) return n_rows <= 16 ? 16 : (int)((n_rows + 15) / 16 * 16);
   int best = max_cols;
   int64_t best_cost = -1;
@@ -2335,11 +2479,11 @@ int fp4_tile_cols(int64_t n_rows, bool one_acc) {
   return best;
 }
 
-template <int LG, bool kPackedB, bool kOneAcc>
+template <int LG, bool kPackedB, bool kOneAcc, bool kSeg = false>
 cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &tmap,
                               cudaStream_t s) {
-  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB, kOneAcc>;
-  constexpr size_t kSmem = Fp4PairCfg<kOneAcc>::kSmem;
+  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB, kOneAcc, kSeg>;
+  constexpr size_t kSmem = Fp4PairCfg<kOneAcc, kSeg ? kSegPairStages : kPairStages>::kSmem;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
   if (e != cudaSuccess) return e;
@@ -2402,6 +2546,41 @@ cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
     // no encoder or a rejected map: generate b from the packed codes instead
   }
   return launch_pair_fp4_v<LG, false, kOneAcc>(prm, dev, tmap, s);
+}
+
+// Segmented K on the e2m1 pairs (head-aligned compensation, chunk-D): one
+// accumulator per CTA, a segment = kseg * Lp / 256 whole stages; b by TMA from
+// a prepacked segmented weight at Lp = 2^prec, else generated from its
+// per-segment codes.
+template <int LG>
+cudaError_t launch_pair_fp4_seg(TcParams prm, int dev, cudaStream_t s) {
+  prm.rep = 0x01010101u;
+  prm.stage_bytes = Fp4PairCfg<true, kSegPairStages>::kStage;
+  prm.ncols = fp4_tile_cols(prm.n_rows, true, true);
+  prm.nkb = (prm.P.ldk << LG) / 256;
+  prm.nkb_seg = (prm.P.kseg << LG) / 256;
+  prm.tiles_m = (prm.m_rows + 255) / 256;
+  prm.tiles_n = (prm.n_rows + prm.ncols - 1) / prm.ncols;
+  prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
+  CUtensorMap tmap;
+  memset(&tmap, 0, sizeof(tmap));
+  const GemmProblem &P = prm.P;
+  if (P.b_streams && P.b_e2m1 && P.batch_b == 1 && LG == P.prec) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc) {
+      const cuuint64_t row_bytes = (cuuint64_t)((P.ldk << LG) / 2);
+      cuuint64_t gdim[2] = {row_bytes, (cuuint64_t)P.N};
+      cuuint64_t gstride[1] = {row_bytes};
+      cuuint32_t box[2] = {(cuuint32_t)kKB, (cuuint32_t)(prm.ncols / 2)};
+      cuuint32_t estride[2] = {1u, 1u};
+      const CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                             const_cast<uint8_t *>(P.b_streams), gdim, gstride, box, estride,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r == CUDA_SUCCESS) return launch_pair_fp4_v<LG, true, true, true>(prm, dev, tmap, s);
+    }
+  }
+  return launch_pair_fp4_v<LG, false, true, true>(prm, dev, tmap, s);
 }
 
 template <int BN, int LG>
@@ -2532,8 +2711,11 @@ bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows) {
   (void)m_rows;
   (void)n_rows;
   const int lg = padded_stream_log2(P);
-  return tc_row_producers(P) && P.nseg == 1 && (lg == 7 || lg == 8) &&
-         (P.b_streams == nullptr || P.b_e2m1) && (P.ldk << lg) < (1LL << 24);
+  if (!tc_row_producers(P) || (lg != 7 && lg != 8)) return false;
+  if (P.nseg > 1)  // segments of whole 256-position stages
+    return (P.b_streams == nullptr || P.b_e2m1) && ((P.kseg << lg) % 256) == 0 &&
+           (P.kseg << lg) < (1LL << 24);
+  return (P.b_streams == nullptr || P.b_e2m1) && (P.ldk << lg) < (1LL << 24);
 }
 
 int tc_tile_n(const GemmProblem &P, int64_t N) {
@@ -2569,6 +2751,12 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
     // pairs pay off only with two a tiles per pair (one accumulator per CTA
     // would generate as many rows per MAC as a single CTA)
     if (tc_nibble_pairs(P, m_rows, n_rows)) {
+      if (P.nseg > 1) {
+        // one accumulator per CTA (256 x <= 240 tiles): two accumulators leave
+        // room for 112 columns only, and measured slower on the compensation
+        if (lg == 7) return launch_pair_fp4_seg<7>(prm, dev, s);
+        return launch_pair_fp4_seg<8>(prm, dev, s);
+      }
       // narrow b on one CTA (prepacked int8-free b is generated from codes)
       if (n_rows <= 128) {
         if (bn == 64) return launch_fp4_narrow<64>(prm, sms, s);

@@ -421,7 +421,8 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a) {
 // form it (u * 0x01010101 + PC, sign-replicating byte permute, AND with
 // 0x01010101 or 0xFFFFFFFF).  pool_comp rows are 2^prec bytes apart.
 __global__ void pack_b_streams_kernel(const int16_t *__restrict__ code, int64_t N, int64_t ldk,
-                                      int prec, int shift, const uint8_t *__restrict__ pool_comp,
+                                      int prec, int shift, int64_t pool_period,
+                                      const uint8_t *__restrict__ pool_comp,
                                       uint8_t *__restrict__ out) {
   const int64_t row_bytes = ldk << prec;
   const int64_t per_row = row_bytes >> 4;
@@ -435,8 +436,9 @@ __global__ void pack_b_streams_kernel(const int16_t *__restrict__ code, int64_t 
     const int c = code[n * ldk + d];
     const uint32_t u = (uint32_t)(abs(c) >> shift);
     const uint32_t sm = (uint32_t)(c >> 31) | 0x01010101u;
+    const int64_t prow = pool_period > 0 ? d % pool_period : d;
     const uint4 pc =
-        *reinterpret_cast<const uint4 *>(pool_comp + (d << prec) + (pos & tmask));
+        *reinterpret_cast<const uint4 *>(pool_comp + (prow << prec) + (pos & tmask));
     uint4 w;
     w.x = prmt_sign(u * 0x01010101u + pc.x) & sm;
     w.y = prmt_sign(u * 0x01010101u + pc.y) & sm;
@@ -451,7 +453,7 @@ __global__ void pack_b_streams_kernel(const int16_t *__restrict__ code, int64_t 
 // sigma * [R >> shift < u] as 0x2 (+1), 0xA (-1) or 0x0, formed as the e2m1
 // pair producers form it from even / odd position complements.
 __global__ void pack_b_streams_e2m1_kernel(const int16_t *__restrict__ code, int64_t N,
-                                           int64_t ldk, int prec, int shift,
+                                           int64_t ldk, int prec, int shift, int64_t pool_period,
                                            const uint8_t *__restrict__ pool_comp,
                                            uint8_t *__restrict__ out) {
   const int64_t row_bytes = (ldk << prec) >> 1;
@@ -466,7 +468,8 @@ __global__ void pack_b_streams_e2m1_kernel(const int16_t *__restrict__ code, int
     const int c = code[n * ldk + d];
     const uint32_t u = (uint32_t)(abs(c) >> shift);
     const uint32_t pat = c < 0 ? 0xAAAAAAAAu : 0x22222222u;
-    const uint4 *pc = reinterpret_cast<const uint4 *>(pool_comp + (d << prec) + (pos & tmask));
+    const int64_t prow = pool_period > 0 ? d % pool_period : d;
+    const uint4 *pc = reinterpret_cast<const uint4 *>(pool_comp + (prow << prec) + (pos & tmask));
     const uint4 p0 = pc[0], p1 = pc[1];
     const uint32_t w8[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
     uint32_t r[4];
@@ -486,18 +489,18 @@ __global__ void pack_b_streams_e2m1_kernel(const int16_t *__restrict__ code, int
 }  // namespace
 
 cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, int prec,
-                                  int shift, bool e2m1, const uint8_t *pool_comp, uint8_t *out,
-                                  cudaStream_t s) {
+                                  int shift, bool e2m1, int64_t pool_period,
+                                  const uint8_t *pool_comp, uint8_t *out, cudaStream_t s) {
   const int64_t total = N * ((ldk << prec) >> (e2m1 ? 5 : 4));
   if (total == 0) return cudaSuccess;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (e2m1)
     pack_b_streams_e2m1_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift,
-                                                                pool_comp, out);
+                                                                pool_period, pool_comp, out);
   else
-    pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift, pool_comp,
-                                                           out);
+    pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift,
+                                                           pool_period, pool_comp, out);
   return cudaGetLastError();
 }
 

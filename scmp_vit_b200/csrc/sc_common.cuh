@@ -138,10 +138,11 @@ cudaError_t launch_gemm_popc(const GemmProblem &P, cudaStream_t s);
 // b operand bytes of every row and k-block at Lp = 2^prec, as the row
 // producers would generate them: out[n][k-block][128].  e2m1: nibbles in the
 // e2m1 pair producers' order, 256 positions per 128 bytes (pool_comp is the
-// natural-order complement either way).
+// natural-order complement either way).  pool_period > 0: reduction index d
+// reads pool row d % pool_period (segmented K), else row d.
 cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, int prec,
-                                  int shift, bool e2m1, const uint8_t *pool_comp, uint8_t *out,
-                                  cudaStream_t s);
+                                  int shift, bool e2m1, int64_t pool_period,
+                                  const uint8_t *pool_comp, uint8_t *out, cudaStream_t s);
 bool tc_supported(const GemmProblem &P);
 int tc_block_n(int64_t N);
 int tc_tile_n(const GemmProblem &P, int64_t N);

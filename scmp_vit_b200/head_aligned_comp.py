@@ -44,8 +44,8 @@ class HeadAlignedSCLinear(nn.Module):
         orig_shape = x.shape
         D_in = orig_shape[-1]
         D_out = self.weight.shape[0]
-        x2 = x.reshape(-1, D_in).float()
         if USE_NOISE_MODEL:
+            x2 = x.reshape(-1, D_in).float()
             y = torch.zeros(x2.shape[0], D_out, device=x.device, dtype=torch.float32)
             for h in range(self.n_heads):
                 sl = slice(h * self.D_head, (h + 1) * self.D_head)
@@ -56,7 +56,39 @@ class HeadAlignedSCLinear(nn.Module):
             return y.to(x.dtype).reshape(*orig_shape[:-1], D_out)
         cfg = self.cfg_override if self.cfg_override is not None else _get_config(
             self.D_head, self.sc_prec)
-        y = sc_matmul(x2, self.weight.float(), granularity="per_row", mode=self.mode,
-                      sc_prec=self.sc_prec, config=cfg, k_segment=self.D_head,
-                      bias=self.bias)
+        x2 = x.reshape(-1, D_in)
+        if x2.dtype not in (torch.float32, torch.bfloat16):
+            x2 = x2.float()
+        b = self._packed_weight(cfg) if self._prepack_applies() else self.weight
+        y = sc_matmul(x2, b, granularity="per_row", mode=self.mode, sc_prec=self.sc_prec,
+                      config=cfg, k_segment=self.D_head, bias=self.bias)
         return y.to(x.dtype).reshape(*orig_shape[:-1], D_out)
+
+    def _prepack_applies(self) -> bool:
+        """Whether the weight is packed once for segmented calls (its operand
+        bytes then reach the e2m1 pair tiles by TMA instead of being generated
+        in every call; bit-identical either way).  Only when forced with
+        ``sc_linear.set_weight_prepack(True)``: on B200 the one-accumulator
+        segmented tiles ran slower with TMA-fed b (the compensation at 512
+        images: 30.5 vs 26.1 ms), their L2 reads of the packed bytes being
+        twice those of the two-accumulator linears per multiply-add."""
+        from . import sc_linear
+        if sc_linear._PREPACK is not True or not self.weight.is_cuda:
+            return False
+        if self.sc_prec not in (7, 8) or (self.mode == "unipolar" and self.sc_prec == 8):
+            return False
+        return self.D_head % 8 == 0 and self.D_head < self.in_features
+
+    def _packed_weight(self, cfg: dict):
+        """The weight's segmented prepacked operand (cached; rebuilt when the
+        weight's storage, version counter or the SC settings change)."""
+        from .sc import prepack_b
+        w = self.weight
+        key = (w.data_ptr(), w._version, w.dtype, str(w.device), self.sc_prec, self.mode,
+               cfg["uid"])
+        if key != getattr(self, "_packed_key", None):
+            self._packed = None  # free the old buffer before building the new one
+            self._packed = prepack_b(w.detach(), granularity="per_row", mode=self.mode,
+                                     sc_prec=self.sc_prec, config=cfg, k_segment=self.D_head)
+            self._packed_key = key
+        return self._packed

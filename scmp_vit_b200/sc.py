@@ -86,8 +86,10 @@ class PackedWeight:
     ``N * K * 2**sc_prec`` (int8 bytes)."""
 
     def __init__(self, buf: torch.Tensor, N: int, K: int, granularity: str, mode: str,
-                 sc_prec: int, config: dict, group_b: int, source: Optional[torch.Tensor] = None):
+                 sc_prec: int, config: dict, group_b: int, source: Optional[torch.Tensor] = None,
+                 k_segment: int = 0):
         self.buf = buf
+        self.k_segment = int(k_segment)  # > 0: packed for calls with this k_segment
         self.source = source  # the weight it was packed from (not read by the engine)
         self.N, self.K = N, K
         self.granularity, self.mode, self.sc_prec = granularity, mode, sc_prec
@@ -100,9 +102,10 @@ class PackedWeight:
         return (self.N, self.K)
 
     def matches(self, *, granularity: str, mode: str, sc_prec: int, config: dict,
-                group_b: int) -> bool:
+                group_b: int, k_segment: int = 0) -> bool:
         return (granularity == self.granularity and mode == self.mode and
                 sc_prec == self.sc_prec and config["uid"] == self.config["uid"] and
+                int(k_segment) == self.k_segment and
                 (granularity != "per_row" or max(int(group_b), 1) == self.group_b))
 
 
@@ -123,19 +126,24 @@ def _base_args(engine: str, granularity: str, mode: str, p: int, L: int, group_a
 @torch.no_grad()
 def prepack_b(b: torch.Tensor, *, granularity: str = "per_row", mode: str = "bipolar",
               sc_prec: int = 8, config: Optional[dict] = None,
-              group_b: int = 1) -> PackedWeight:
+              group_b: int = 1, k_segment: int = 0) -> PackedWeight:
     """Quantise the weight ``b`` ([N, K], fp32 or bf16, CUDA) and expand its
-    SC operand bytes once (see ``PackedWeight``)."""
+    SC operand bytes once (see ``PackedWeight``).  ``k_segment > 0`` packs it
+    for segmented calls (each segment quantised on its own, pool rows per
+    index inside the segment; sc_prec 7 or 8)."""
     if granularity not in _lib.GRANULARITY or mode not in _lib.MODE:
         raise ValueError(f"unknown granularity / mode {granularity!r} / {mode!r}")
     if b.dim() != 2 or not b.is_cuda:
         raise ValueError("prepack_b needs a 2-D CUDA weight [N, K]")
     N, K = b.shape
     p = int(sc_prec)
+    kseg = int(k_segment) if 0 < int(k_segment) < K else 0
+    if kseg and K % kseg:
+        raise ValueError(f"k_segment={kseg} must divide K={K}")
     if config is None:
-        config = default_config(K, p)
-    if int(config["sc_prec"]) != p or int(config["dims"]) < K:
-        raise ValueError("config must be (>= K dims, sc_prec) for prepacking")
+        config = default_config(kseg or K, p)
+    if int(config["sc_prec"]) != p or int(config["dims"]) < (kseg or K):
+        raise ValueError("config must be (>= K or k_segment dims, sc_prec) for prepacking")
     bt = b.contiguous() if b.dtype in (torch.float32, torch.bfloat16) else b.float().contiguous()
     dev = b.device
     pool = device_pool(config, dev)
@@ -143,7 +151,8 @@ def prepack_b(b: torch.Tensor, *, granularity: str = "per_row", mode: str = "bip
     args.b = bt.data_ptr()
     args.batch, args.batch_b, args.M, args.N, args.K = 1, 1, 1, N, K
     args.pool = pool.data_ptr()
-    args.pool_dims = K
+    args.pool_dims = kseg or K
+    args.k_segment = kseg
     args.io_flags = _lib.IO_B_BF16 if bt.dtype == torch.bfloat16 else 0
     lib = _lib.load()
     nbytes = lib.scmp_prepack_b_size(ctypes.byref(args))
@@ -154,7 +163,8 @@ def prepack_b(b: torch.Tensor, *, granularity: str = "per_row", mode: str = "bip
         stream = torch.cuda.current_stream(dev).cuda_stream
         _lib.check(lib.scmp_prepack_b(ctypes.byref(args), ctypes.c_void_p(buf.data_ptr()),
                                       nbytes, ctypes.c_void_p(stream)))
-    return PackedWeight(buf, N, K, granularity, mode, p, config, max(int(group_b), 1), source=b)
+    return PackedWeight(buf, N, K, granularity, mode, p, config, max(int(group_b), 1), source=b,
+                        k_segment=kseg)
 
 
 @torch.no_grad()
@@ -232,12 +242,13 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
         return t.contiguous()
     a3 = _operand(a3)
     if packed is not None:
-        if chunk_d or k_segment:
-            raise ValueError("a prepacked b runs without chunk_d / k_segment")
+        if chunk_d:
+            raise ValueError("a prepacked b runs without chunk_d")
+        kseg_call = int(k_segment) if 0 < int(k_segment) < K else 0
         if not packed.matches(granularity=granularity, mode=mode, sc_prec=p, config=config,
-                              group_b=group_b):
+                              group_b=group_b, k_segment=kseg_call):
             raise ValueError("prepacked b was built with other granularity / mode / sc_prec / "
-                             "config / group_b")
+                             "config / group_b / k_segment")
     else:
         b3 = _operand(b3)
     if chunk_d and 0 < int(chunk_d) < K and mode == "bipolar":

@@ -184,3 +184,56 @@ def test_fp4_narrow_window_chunk_shortcuts(cuda_device, temp):
     np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
     y, y_ref = _run(cuda_device, attn, vt, 8, 256)
     np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=1e-30)
+
+
+# ------------------------------------------------------------- K segments
+# Segmented K (head-aligned compensation, chunk-D sums) runs on one-accumulator
+# pair tiles (<= 240 columns, fp32 running sums in tensor memory next to the
+# accumulator): each segment quantised and rescaled on its own, the fp32
+# segment results summed in segment order, then the bias.
+
+@pytest.mark.parametrize("M,N,K,kseg,p,L", [
+    (600, 1024, 1024, 64, 8, 256),   # the compensation shape: 16 heads of 64, 5 tiles of 208
+    (1000, 300, 512, 64, 8, 192),    # early termination, ragged a rows and b columns
+    (513, 250, 256, 32, 7, 128),     # Lp = 128, 8 segments, one-row a tail
+    (257, 1040, 128, 64, 8, 256),    # two segments, wide b
+    (128, 40, 192, 16, 8, 256),      # narrow b, 12 segments of 16
+])
+def test_segments_on_pairs(cuda_device, M, N, K, kseg, p, L):
+    dev = cuda_device
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    bias = torch.randn(N, generator=g)
+    random.seed(kseg + p)
+    cfg = ch.make_lfsr_config(kseg, kseg, p, seed=M)
+    y = sc_matmul(a.to(dev), b.to(dev), sc_prec=p, config=cfg, stoc_len=L, k_segment=kseg,
+                  bias=bias.to(dev), engine="tcgen05")
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    _, y_ref = sc_oracle.sc_matmul_segments_ref(a.numpy(), b.numpy(), kseg, sc_prec=p,
+                                                pool=cfg["table"], stoc_len=L, bias=bias.numpy())
+    np.testing.assert_allclose(y.cpu().numpy(), y_ref[0], rtol=RTOL, atol=1e-30)
+
+
+def test_segments_on_pairs_per_row_lengths_and_batches(cuda_device):
+    """Per-row stream lengths (0 = pruned row, bias only) across segments, and
+    batched slices with their own b."""
+    dev = cuda_device
+    g = torch.Generator().manual_seed(77)
+    BH, M, N, K, kseg = 3, 300, 176, 256, 64
+    a = torch.randn(BH, M, K, generator=g)
+    b = torch.randn(BH, N, K, generator=g) * 0.05
+    rowL = np.random.default_rng(1).choice([0, 160, 256], BH * M).astype(np.int32)
+    random.seed(3)
+    cfg = ch.make_sobol_simple_config(kseg, kseg, 8)
+    y = sc_matmul(a.to(dev), b.to(dev), sc_prec=8, config=cfg, k_segment=kseg,
+                  row_stoc_len=torch.from_numpy(rowL), engine="tcgen05")
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    Lc = np.where(rowL > 0, rowL, 1).astype(np.int32)
+    _, y_ref = sc_oracle.sc_matmul_segments_ref(a.numpy(), b.numpy(), kseg, sc_prec=8,
+                                                pool=cfg["table"], L_row=Lc)
+    y_ref = y_ref.reshape(BH * M, N)
+    y_ref[rowL == 0] = 0.0
+    np.testing.assert_allclose(y.cpu().numpy().reshape(BH * M, N), y_ref, rtol=RTOL, atol=1e-30)

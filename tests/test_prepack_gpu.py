@@ -108,3 +108,61 @@ def test_sclinear_cache_follows_the_weight(cuda_device):
         scl.set_weight_prepack(None)
     torch.cuda.synchronize()
     assert _lib.engine_status(reset=True) == 0
+
+
+@pytest.mark.parametrize("M,N,K,kseg,p,L", [
+    (600, 1024, 1024, 64, 8, None),   # the head-aligned compensation shape
+    (300, 250, 256, 32, 7, None),     # ragged b tile, Lp = 128
+    (257, 176, 512, 64, 8, 160),      # L < 2^p: b generated from the packed codes
+])
+def test_segmented_prepack_matches_weight_and_oracle(cuda_device, M, N, K, kseg, p, L):
+    """A weight packed for segmented calls (per-segment quantisation, pool rows
+    per index inside the segment) gives the weight's own results bit for bit,
+    and the oracle's segment sums."""
+    dev = cuda_device
+    g = torch.Generator().manual_seed(M + N)
+    a = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.02
+    bias = torch.randn(N, generator=g)
+    cfg = ch.make_lfsr_config(kseg, kseg, p, seed=N)
+    kw = dict(sc_prec=p, config=cfg, stoc_len=L, k_segment=kseg, bias=bias.to(dev))
+    y1 = sc_matmul(a.to(dev), w.to(dev), **kw)
+    pk = prepack_b(w.to(dev), sc_prec=p, config=cfg, k_segment=kseg)
+    y2 = sc_matmul(a.to(dev), pk, **kw)
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    assert torch.equal(y1, y2)
+    _, y_ref = sc_oracle.sc_matmul_segments_ref(a.numpy(), w.numpy(), kseg, sc_prec=p,
+                                                pool=cfg["table"], stoc_len=L, bias=bias.numpy())
+    np.testing.assert_allclose(y2.cpu().numpy(), y_ref[0], rtol=1e-5, atol=1e-30)
+    with pytest.raises(ValueError, match="k_segment"):
+        sc_matmul(a.to(dev), pk, sc_prec=p, config=cfg, stoc_len=L)
+
+
+def test_head_aligned_keeps_its_packed_weight(cuda_device):
+    """With prepacking forced on, HeadAlignedSCLinear packs its weight once per
+    weight version; results equal the generated path bit for bit."""
+    from scmp_vit_b200.head_aligned_comp import HeadAlignedSCLinear
+    dev = cuda_device
+    lin = nn.Linear(256, 96).to(dev)
+    cfg = ch.make_lfsr_config(64, 64, 8, seed=3)
+    m = HeadAlignedSCLinear(lin, 8, n_heads=4, cfg_override=cfg)
+    x = torch.randn(700, 256, generator=torch.Generator().manual_seed(2)).to(dev)
+    y0 = m(x)  # default: b generated in the kernel
+    assert getattr(m, "_packed", None) is None
+    scl.set_weight_prepack(True)
+    try:
+        y1 = m(x)
+        assert m._packed is not None and m._packed.k_segment == 64
+        packed = m._packed
+        y2 = m(x)
+        assert m._packed is packed  # cached
+        with torch.no_grad():
+            lin.weight.mul_(0.5)  # in place: the cache notices the new version
+        y3 = m(x)
+        assert m._packed is not packed
+    finally:
+        scl.set_weight_prepack(None)
+    y4 = m(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1) and torch.equal(y1, y2) and torch.equal(y3, y4)
