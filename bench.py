@@ -56,7 +56,7 @@ def parse():
     p.add_argument("--engine", default="auto")
     p.add_argument("--fp-glue", choices=["fp32", "bf16"], default="fp32",
                    help="dtype of the FP ops around the SC matmuls (fp32 = the reference's)")
-    p.add_argument("--e2e-steps", type=int, default=5,
+    p.add_argument("--e2e-steps", type=int, default=3,
                    help="steps of the end-to-end leg (at most --steps)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")

@@ -38,7 +38,7 @@ from .sc import sc_matmul
 
 __all__ = ["SCLinear", "set_noise_model", "set_vit_timestep", "get_vit_timestep",
            "_sc_linear", "_sc_linear_mp", "_mm_one_bucket", "_get_config", "_CFG_CACHE",
-           "sc_linear_rows"]
+           "sc_linear_rows", "PackedWeights"]
 
 # Read at call time through the module (``sc_linear.USE_NOISE_MODEL``).
 USE_NOISE_MODEL = False
@@ -128,7 +128,8 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
                    levels: Iterable[int], mode: str, *, bias: Optional[torch.Tensor] = None,
                    out: Optional[torch.Tensor] = None, chunk_d: int = 0,
                    cfg_for: Optional[Callable[[int, int], dict]] = None,
-                   host_counts: Optional[dict] = None) -> torch.Tensor:
+                   host_counts: Optional[dict] = None,
+                   packed_for: Optional[Callable[[int, dict], object]] = None) -> torch.Tensor:
     """Per-row stream lengths in grouped launches: one engine call per
     distinct precision among ``levels`` (the host-known set of values that
     ``row_L`` may hold; 0 = pruned row -> bias only).
@@ -136,7 +137,9 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
     With ``host_counts`` (rows per level, known without a device sync for
     quantile splits) the rows are sorted by level once and every call runs
     on its own contiguous rows only; otherwise every call spans all rows and
-    skips the others (``row_stoc_len = -1``)."""
+    skips the others (``row_stoc_len = -1``).  ``packed_for(p, config)``, if
+    given, returns the weight prepacked for precision ``p`` (or None): the
+    per-row calls then load its operand bytes instead of generating them."""
     M, K = x2.shape
     N = w.shape[0]
     if out is None:
@@ -166,7 +169,8 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
             if n_rows == 0:
                 continue
             cfg = cfg_for(chunk_d if use_chunk else K, p)
-            sc_matmul(xs[start:start + n_rows], w, granularity="per_row", mode=mode, sc_prec=p,
+            b = _packed_or(w, packed_for, p, cfg, use_chunk)
+            sc_matmul(xs[start:start + n_rows], b, granularity="per_row", mode=mode, sc_prec=p,
                       config=cfg, chunk_d=chunk_d if use_chunk else 0, bias=bias,
                       row_stoc_len=Ls[start:start + n_rows], out=ys[start:start + n_rows])
             start += n_rows
@@ -181,10 +185,47 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
             mask |= row_L <= 0  # the first launch writes the pruned rows
         sel = torch.where(mask, row_L.clamp(min=0), torch.full_like(row_L, -1))
         cfg = cfg_for(chunk_d if use_chunk else K, p)
-        sc_matmul(x2, w, granularity="per_row", mode=mode, sc_prec=p, config=cfg,
-                  chunk_d=chunk_d if use_chunk else 0, bias=bias, row_stoc_len=sel, out=out)
+        sc_matmul(x2, _packed_or(w, packed_for, p, cfg, use_chunk), granularity="per_row",
+                  mode=mode, sc_prec=p, config=cfg, chunk_d=chunk_d if use_chunk else 0,
+                  bias=bias, row_stoc_len=sel, out=out)
         first = False
     return out
+
+
+def _packed_or(w, packed_for, p: int, cfg: dict, chunked: bool):
+    """The prepacked weight for precision ``p`` if one applies, else ``w``."""
+    if packed_for is None or chunked:
+        return w
+    pk = packed_for(p, cfg)
+    return w if pk is None else pk
+
+
+class PackedWeights:
+    """A weight's prepacked SC operands, one per (precision, pool), rebuilt
+    when the weight's storage or version counter changes (mixed-precision
+    linears run one call per precision class, each of which can load packed
+    bytes instead of generating them)."""
+
+    def __init__(self, weight: torch.Tensor, mode: str):
+        self.weight = weight
+        self.mode = mode
+        self._cache: dict = {}
+        self._key = None
+
+    def __call__(self, p: int, cfg: dict):
+        if not _prepack_applies(self.weight, p, self.mode, None, 0):
+            return None
+        from .sc import prepack_b
+        w = self.weight
+        key = (w.data_ptr(), w._version, w.dtype, str(w.device))
+        if key != self._key:
+            self._cache.clear()
+            self._key = key
+        ck = (p, cfg["uid"])
+        if ck not in self._cache:
+            self._cache[ck] = prepack_b(w.detach(), granularity="per_row", mode=self.mode,
+                                        sc_prec=p, config=cfg, group_b=1)
+        return self._cache[ck]
 
 
 def _record_budget(operator, row_L: torch.Tensor, M: int, D_out: int, max_sl: int):
@@ -198,7 +239,8 @@ def _sc_linear_mp(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int, mod
                   range_entries: list[DispatchEntry] | None = None,
                   mp_cfg: MPConfig | None = None,
                   adaptive_mp_cfg: AdaptiveMPConfig | None = None,
-                  operator: str | None = None, chunk_d: int = 0) -> torch.Tensor:
+                  operator: str | None = None, chunk_d: int = 0,
+                  packed_for=None) -> torch.Tensor:
     """MP-aware SC linear (reference ``sc_linear.py:183-288``): per-row levels
     from fixed or adaptive MP (adaptive wins), per-output-group levels from
     range MP, ``min(row_sl, group_sl)`` when combined."""
@@ -247,7 +289,8 @@ def _sc_linear_mp(x: torch.Tensor, weight: torch.Tensor, bias, sc_prec: int, mod
 
     if range_entries is None:
         result = sc_linear_rows(x_flat, w, row_L, levels, mode, bias=bias, chunk_d=chunk_d,
-                                host_counts=None if assign is None else assign.host_counts)
+                                host_counts=None if assign is None else assign.host_counts,
+                                packed_for=packed_for)
     else:
         result = torch.empty(M, D_out, dtype=torch.float32, device=x.device)
         for e in range_entries:
@@ -348,10 +391,12 @@ class SCLinear(nn.Module):
             return _sc_linear(x, self.weight, self.bias, self.sc_prec, mode=self.mode,
                               cfg_override=self.cfg_override, stoc_len=self.stoc_len,
                               chunk_d=self.chunk_d, packed=packed)
+        if getattr(self, "_packed_levels", None) is None:
+            self._packed_levels = PackedWeights(self.weight, self.mode)
         return _sc_linear_mp(x, self.weight, self.bias, self.sc_prec, self.mode,
                              range_entries=self.range_entries, mp_cfg=self.mp_cfg,
                              adaptive_mp_cfg=self.adaptive_mp_cfg, operator=self.operator,
-                             chunk_d=self.chunk_d)
+                             chunk_d=self.chunk_d, packed_for=self._packed_levels)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "

@@ -25,7 +25,7 @@ import torch.nn.functional as F
 from .attention import make_sc_attention_forward
 from .head_aligned_comp import HeadAlignedSCLinear
 from .mp import SeededRandomMPConfig, quantile_counts, set_current_block_idx
-from .sc_linear import SCLinear, _get_config, sc_linear_rows
+from .sc_linear import PackedWeights, SCLinear, _get_config, sc_linear_rows
 
 
 class Mlp(nn.Module):
@@ -156,15 +156,19 @@ class _RowMPLinear(nn.Module):
         self.salt = salt
         self.cfg_for = cfg_for
         self.calls = 0
+        self.packed = PackedWeights(self.weight, "bipolar")  # one per precision class
 
     def forward(self, x):
         shp = x.shape
-        x2 = x.reshape(-1, shp[-1]).float()
+        x2 = x.reshape(-1, shp[-1])
+        if x2.dtype not in (torch.float32, torch.bfloat16):
+            x2 = x2.float()
         row_L = self.cfg.assign(x2.shape[0], x2.device, salt=(self.salt << 16) + self.calls)
         self.calls += 1
         counts = quantile_counts(x2.shape[0], self.cfg.stoc_len_levels, self.cfg.level_fractions)
-        y = sc_linear_rows(x2, self.weight.float(), row_L, self.cfg.stoc_len_levels, "bipolar",
-                           bias=self.bias, cfg_for=self.cfg_for, host_counts=counts)
+        y = sc_linear_rows(x2, self.weight, row_L, self.cfg.stoc_len_levels, "bipolar",
+                           bias=self.bias, cfg_for=self.cfg_for, host_counts=counts,
+                           packed_for=self.packed)
         return y.to(x.dtype).reshape(*shp[:-1], -1)
 
 

@@ -166,3 +166,31 @@ def test_head_aligned_keeps_its_packed_weight(cuda_device):
     y4 = m(x)
     torch.cuda.synchronize()
     assert torch.equal(y0, y1) and torch.equal(y1, y2) and torch.equal(y3, y4)
+
+
+def test_mixed_precision_linears_use_packed_weights(cuda_device):
+    """Mixed-precision linears run one call per precision class; each loads
+    the weight prepacked for its precision (SCLinear with an MP config, and
+    the benchmark's seeded-random MP linear), bit-identical to generating b."""
+    from scmp_vit_b200.mp import MPConfig, SeededRandomMPConfig
+    from scmp_vit_b200.vit import _RowMPLinear
+    dev = cuda_device
+    g = torch.Generator().manual_seed(11)
+    lin = nn.Linear(256, 300).to(dev)
+    x = torch.randn(2, 257, 256, generator=g).to(dev)
+    scl._CFG_CACHE.clear()
+    random.seed(4)
+    m = scl.SCLinear(lin, 8, mp_cfg=MPConfig([128, 192, 256]), operator="mlp_fc1")
+    r = _RowMPLinear(lin, SeededRandomMPConfig([128, 192, 256], None, seed=0), 5, scl._get_config)
+    ys = []
+    for prepack in (None, False):
+        scl.set_weight_prepack(prepack)
+        try:
+            r.calls = 0
+            ys.append((m(x), r(x)))
+        finally:
+            scl.set_weight_prepack(None)
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    assert len(m._packed_levels._cache) == 2 and len(r.packed._cache) == 2  # p = 7 and 8
+    assert torch.equal(ys[0][0], ys[1][0]) and torch.equal(ys[0][1], ys[1][1])
