@@ -111,6 +111,8 @@ struct Plan {
   size_t pool_comp = 0;
   int64_t pool_comp_rows = 0;
   int64_t ldk = 0;
+  size_t split = 0;  // int32 [ksplit, batch, M, N] partial counts (ksplit > 1)
+  int ksplit = 1;
   size_t total = 0;
 };
 
@@ -216,6 +218,45 @@ PackPlan make_pack_plan(const scmp_matmul_args *x) {
   return p;
 }
 
+// The fields of GemmProblem that the tensor-core routing reads, from the
+// arguments alone (sizing precedes any pointer; the carved code planes are
+// 256-byte aligned, as the routing requires).
+GemmProblem routing_problem(const scmp_matmul_args *x, int64_t ldk) {
+  GemmProblem P{};
+  const int64_t kseg = seg_len(x);
+  P.batch = x->batch;
+  P.batch_b = x->batch_b;
+  P.M = x->M;
+  P.N = x->N;
+  P.K = x->K;
+  P.ldk = ldk;
+  P.kseg = kseg;
+  P.nseg = (int)(x->K / kseg);
+  P.mode = x->mode;
+  P.prec = x->sc_prec;
+  P.stoc_len = x->stoc_len;
+  P.pool_dims = x->pool_dims;
+  static const int32_t marker = 0;
+  P.row_L = x->row_stoc_len ? &marker : nullptr;
+  P.slice_L = x->slice_stoc_len ? &marker : nullptr;
+  P.acc_out = x->acc_out;
+  if (x->io_flags & SCMP_IO_B_PACKED) {
+    const PackPlan pk = make_pack_plan(x);
+    static const uint8_t packed_marker = 0;
+    P.b_streams = &packed_marker;
+    P.b_e2m1 = pk.e2m1 ? 1 : 0;
+  }
+  return P;
+}
+
+// K splits the engine will use for these arguments (tensor-core route only).
+int plan_ksplit(const scmp_matmul_args *x, int64_t ldk) {
+  if (x->engine == SCMP_ENGINE_POPC || x->batch == 0 || x->M == 0 || x->N == 0) return 1;
+  const GemmProblem P = routing_problem(x, ldk);
+  if (!tc_supported(P)) return 1;
+  return tc_ksplit(P, tc_rows(x->M, 256), tc_rows(x->N, tc_tile_n(P, x->N)));
+}
+
 Plan make_plan(const scmp_matmul_args *x) {
   Plan p;
   Carver c;
@@ -233,6 +274,9 @@ Plan make_plan(const scmp_matmul_args *x) {
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
   p.pool_comp_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
   p.pool_comp = c.take((size_t)p.pool_comp_rows * T);
+  p.ksplit = plan_ksplit(x, p.ldk);
+  if (p.ksplit > 1)
+    p.split = c.take(sizeof(int32_t) * (size_t)p.ksplit * (size_t)(x->batch * x->M * x->N));
   p.total = c.off;
   return p;
 }
@@ -460,6 +504,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.m_hi = x.M;
   P.n_lo = 0;
   P.n_hi = x.N;
+  P.split_part = plan.ksplit > 1 ? reinterpret_cast<int32_t *>(ws + plan.split) : nullptr;
 
   bool use_tc = false;
   if (x.engine == SCMP_ENGINE_TCGEN05) {
@@ -485,9 +530,10 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
         return cuda_fail(e, "pool_complement launch");
       count_launches(1);
     }
-    if ((e = launch_gemm_tc(P, m_tc, n_tc, err, s)) != cudaSuccess)
+    int launched = 0;
+    if ((e = launch_gemm_tc(P, m_tc, n_tc, err, s, &launched)) != cudaSuccess)
       return cuda_fail(e, "gemm_tc launch");
-    count_launches(1);
+    count_launches((uint64_t)launched);
   }
   // CUDA-core engine: everything (no tensor-core path) or the ragged strips
   // the tensor-core tiles leave (rows >= m_tc; columns >= n_tc of rows < m_tc).

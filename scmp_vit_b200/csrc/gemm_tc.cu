@@ -86,7 +86,34 @@ struct TcParams {
   uint32_t rep;          // 0x01010101
   uint32_t stage_bytes;  // TcCfg<BN>::kStage
   int ncols;             // e2m1 CTA pairs: b rows (accumulator columns) per tile
+  // K splits (e2m1 pairs, one segment): prm.tiles = ksplit x tiles_split;
+  // split s covers macro steps (8 reduction indices each) [s msplit,
+  // min((s + 1) msplit, ldk / 8)) and its tiles write exact int32 counts to
+  // part + s part_stride ([batch, M, N]); a reduce kernel rescales their sum.
+  int ksplit;
+  int msplit;
+  int64_t tiles_split;
+  int32_t *part;
+  int64_t part_stride;
 };
+
+// Position of a tile in the launch: its K split, slice and (m, n) block.
+struct TileCoord {
+  int64_t split, slice, rem;
+  int mc0, mc1;  // macro steps of the split
+};
+template <bool kSplit>
+__device__ __forceinline__ TileCoord tile_coord(const TcParams &prm, int64_t tile) {
+  TileCoord t;
+  const int nmacro = (int)(prm.P.ldk >> 3);
+  const int64_t t2 = kSplit ? tile % prm.tiles_split : tile;
+  t.split = kSplit ? tile / prm.tiles_split : 0;
+  t.slice = t2 / (prm.tiles_m * prm.tiles_n);
+  t.rem = t2 % (prm.tiles_m * prm.tiles_n);
+  t.mc0 = kSplit ? (int)t.split * prm.msplit : 0;
+  t.mc1 = kSplit ? min(t.mc0 + prm.msplit, nmacro) : nmacro;
+  return t;
+}
 
 // ------------------------------------------------------------ PTX helpers
 
@@ -117,14 +144,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false when it gave up (timeout or another thread aborted).
+// The limit is re-read on every slow iteration rather than held in registers
+// across the loop (waits sit where the producers hold the most live state).
+__device__ __forceinline__ unsigned long long wait_limit() {
+  return *reinterpret_cast<volatile unsigned long long *>(&g_wait_limit_ns);
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
-  const unsigned long long lim = g_wait_limit_ns;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (now_ns() - t0 > lim) {
+    if (now_ns() - t0 > wait_limit()) {
       *abort = 1;
       return false;
     }
@@ -144,10 +175,9 @@ __device__ __forceinline__ void mbar_wait_own(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool producers_released(volatile int *abort) {
   if (!*reinterpret_cast<volatile int *>(&g_hold_producers)) return true;
   const unsigned long long t0 = now_ns();
-  const unsigned long long lim = g_wait_limit_ns;
   while (!*reinterpret_cast<volatile int *>(&g_hold_release)) {
     if (*abort) return false;
-    if (now_ns() - t0 > lim) {
+    if (now_ns() - t0 > wait_limit()) {
       *abort = 1;
       return false;
     }
@@ -210,11 +240,10 @@ __device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity)
 __device__ __forceinline__ bool mbar_wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort) {
   if (mbar_try_wait_cl(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
-  const unsigned long long lim = g_wait_limit_ns;
   while (true) {
     if (mbar_try_wait_cl(bar, parity)) return true;
     if (*abort) return false;
-    if (now_ns() - t0 > lim) {
+    if (now_ns() - t0 > wait_limit()) {
       *abort = 1;
       return false;
     }
@@ -1129,11 +1158,14 @@ __device__ __forceinline__ uint32_t stream_word_e2m1(uint32_t u, uint32_t rep, u
 // pool rows restart at every segment, and after each non-final segment the
 // producers fold its counts into the running sums (segment_drain_pair, which
 // needs tmem_base, warp and the tile's first b row n0_tile).
+// mc_begin / mc_end: the macro steps (8 reduction indices each) of a K split
+// (mc_end < 0: to the end of K).
 template <int LG, int NS, bool kNoB, bool kOneAcc, bool kSkipA = false, bool kSeg = false>
 __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &st,
                                  uint32_t smem_s, uint32_t stage_a_bytes, int lane, int64_t slice,
                                  int64_t slice_b, int64_t m0, int64_t n0, int nb,
-                                 uint32_t tmem_base = 0, int warp = 0, int64_t n0_tile = 0) {
+                                 uint32_t tmem_base = 0, int warp = 0, int64_t n0_tile = 0,
+                                 int mc_begin = 0, int mc_end = -1) {
   static_assert(LG == 7 || LG == 8, "e2m1 producers take Lp = 128 or 256");
   static_assert(!kSeg || kOneAcc, "segments run on one-accumulator tiles");
   if (!producers_released(b.abort)) return false;  // give-up path test hook
@@ -1180,7 +1212,7 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
   const uint32_t rep = prm.rep;
   const int prec = P.prec;
   const int shift = prm.shift_pool;
-  const int nmacro = (int)(P.ldk >> 3);
+  const int nmacro = mc_end < 0 ? (int)(P.ldk >> 3) : mc_end;
   // pool complement: k-block j of a macro step starts 256 bytes after j - 1;
   // this thread's 64 positions are 64 bytes at 32 cB0 into it
   const uint8_t *pc_thr = P.pool_comp + 32 * cB0;
@@ -1189,10 +1221,10 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
     if (lane < LPB / 16 && prow < prow_lim)
       prefetch_l1(P.pool_comp + (size_t)prow * LPB + 128 * lane);
   };
-  int pbase = 0;
+  int pbase = 8 * mc_begin;  // pool row of the macro step's first reduction index
   const int msteps_seg = kSeg ? prm.kseg >> 3 : 0;  // macro steps per segment
   int mseg = 0;                                     // macro steps done in the segment
-  uint4 ca_n = ld_stream_v4(pa), cb_n = make_uint4(0, 0, 0, 0);
+  uint4 ca_n = ld_stream_v4(pa + mc_begin), cb_n = make_uint4(0, 0, 0, 0);
   // One-accumulator tiles (8 a words per thread) have the registers to load
   // the next stage's pool complement words one stage ahead, keeping their
   // latency off each stage's acquire -> store -> publish chain; the others
@@ -1203,19 +1235,19 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
   uint4 qn0 = make_uint4(0, 0, 0, 0), qn1 = qn0, qn2 = qn0, qn3 = qn0;
   if constexpr (!kNoB) {
     if (doB) {
-      cb_n = ld_stream_v4(pb);
+      cb_n = ld_stream_v4(pb + mc_begin);
       if constexpr (kAheadPC) {
-        const uint4 *pc = reinterpret_cast<const uint4 *>(pc_thr);
+        const uint4 *pc = reinterpret_cast<const uint4 *>(pc_thr + (size_t)pbase * LPB);
         qn0 = __ldg(pc);
         qn1 = __ldg(pc + 1);
         qn2 = __ldg(pc + 2);
         qn3 = __ldg(pc + 3);
       }
     }
-    prefetch_macro(0);
+    prefetch_macro(pbase);
   }
 #pragma unroll 1
-  for (int mc = 0; mc < nmacro; ++mc) {
+  for (int mc = mc_begin; mc < nmacro; ++mc) {
     const uint4 ca = ca_n, cb = cb_n;
     if (mc + 1 < nmacro) {
       ca_n = ld_stream_v4(pa + mc + 1);
@@ -1320,10 +1352,13 @@ __device__ bool produce_rows_fp4(const TcParams &prm, const Bars &b, ProdState &
 // prm.ncols are not part of the tile.  kOneAcc: one accumulator of 128 a rows
 // (lanes) x prm.ncols columns; warp pw takes the 32-column chunks pw / 4,
 // pw / 4 + 4, ...
+// part != NULL (a K split): store the tile's exact int32 counts there
+// ([batch, M, N] layout) instead of rescaled outputs.
 template <int BN, bool kSeg, bool kPair = false, bool kF32 = false, bool kOneAcc = false>
 __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
                               unsigned char *smem, uint32_t tmem_base, int warp, int lane,
-                              int64_t slice, int64_t slice_b, int64_t m0, int64_t n0, int64_t it) {
+                              int64_t slice, int64_t slice_b, int64_t m0, int64_t n0, int64_t it,
+                              int32_t *part = nullptr) {
   static_assert(!kOneAcc || kF32, "one-accumulator tiles are e2m1 pair tiles");
   const GemmProblem &P = prm.P;
   const int ncols = kF32 ? prm.ncols : BN;
@@ -1424,6 +1459,10 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         const int4 rp = rowp[r];  // broadcast
         if (!col_ok || rp.x < 0) continue;
         const int32_t a = rp.x > 0 ? __float_as_int(stg[r * 33 + lane]) : 0;
+        if (!kSeg && part) {
+          part[(grow0 + r) * P.N + gn] = a;
+          continue;
+        }
         float y = 0.0f;
         if constexpr (kSeg) {
           if (rp.x > 0) y = stg[r * 33 + lane];
@@ -1951,9 +1990,11 @@ constexpr int kSegPairStages = 4;
 // producers' drain of the previous one (tempty); the fp32 running sums live in
 // TMEM columns [ncols, 2 ncols) (ncols <= 240).  Two accumulators would leave
 // room for 112 columns only and measured slower on the compensation shape.
-template <int LG, bool kPackedB, bool kOneAcc, bool kSeg = false>
+// kSplit: the tiles of prm.ksplit K splits (see TcParams), counts to prm.part.
+template <int LG, bool kPackedB, bool kOneAcc, bool kSeg = false, bool kSplit = false>
 __global__ void __launch_bounds__(kThreads + 32, 1)
     gemm_tc_pair_fp4_kernel(const TcParams prm, const __grid_constant__ CUtensorMap tmap) {
+  static_assert(!(kSeg && kSplit), "segmented K is not split");
   static_assert(!kSeg || kOneAcc, "segments run on one-accumulator tiles");
   using Cfg = Fp4PairCfg<kOneAcc, kSeg ? kSegPairStages : kPairStages>;
   constexpr uint32_t kTmemAlloc = 512;
@@ -2032,8 +2073,10 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       bool ok = true;
       int64_t g = 0;  // one per (tile, segment), as on the producer side
       const int nseg = kSeg ? prm.nseg : 1;
-      const int64_t nkb_seg = kSeg ? prm.nkb_seg : prm.nkb;
+      constexpr int G = (8 << LG) / 256;  // k-blocks per macro step
       for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters) {
+        const TileCoord tc = tile_coord<kSplit>(prm, tile);
+        const int64_t nkb_seg = kSeg ? prm.nkb_seg : (int64_t)(tc.mc1 - tc.mc0) * G;
         for (int seg = 0; seg < nseg && ok; ++seg, ++g) {
           if (g > 0) ok = mbar_wait_cl(b.tempty, (uint32_t)((g - 1) & 1), b.abort);
           if (!ok) break;
@@ -2073,8 +2116,11 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      constexpr int G = (8 << LG) / 256;
       for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters) {
-        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+        const TileCoord tc = tile_coord<kSplit>(prm, tile);
+        const int64_t nkb = (int64_t)(tc.mc1 - tc.mc0) * G;
+        for (int64_t kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
           mbar_arrive_cluster(b.pfull_cl + 8u * (uint32_t)stage);
           if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
@@ -2092,19 +2138,23 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
       uint32_t phase = 0;
       bool ok = true;
       int64_t it = 0;
+      constexpr int G = (8 << LG) / 256;
       for (int64_t tile = cluster; tile < prm.tiles && ok; tile += nclusters, ++it) {
-        const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+        const TileCoord tc = tile_coord<kSplit>(prm, tile);
+        const int64_t rem = tc.rem;
+        const int kb0 = tc.mc0 * G;
+        const int64_t nkb = (int64_t)(tc.mc1 - tc.mc0) * G;
         const int nb0 = (int)((rem / prm.tiles_m) * ncols + (int64_t)rank * (ncols / 2));
         // the previous tile's epilogue stages its transpose in the ring (the
         // epi barrier completes once per segment: the epilogue is the tile's
         // last completion)
         const int64_t epi_done = it * (kSeg ? prm.nseg : 1) - 1;
         if (it > 0 && !mbar_wait(b.epi, (uint32_t)(epi_done & 1), b.abort)) break;
-        for (int64_t kb = 0; kb < prm.nkb; ++kb) {
+        for (int64_t kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&b.empty[stage], phase ^ 1, b.abort)) { ok = false; break; }
           mbar_arrive_expect_tx(&b.full[stage], bytes);
-          tma_load_2d(smem0 + stage * Cfg::kStage + Cfg::kStageA, &tmap, (int)(kb * kKB), nb0,
-                      &b.full[stage]);
+          tma_load_2d(smem0 + stage * Cfg::kStage + Cfg::kStageA, &tmap,
+                      (int)((kb0 + kb) * kKB), nb0, &b.full[stage]);
           if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
         }
       }
@@ -2117,18 +2167,21 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     int64_t it = 0;
     const int half = ncols / 2;
     for (int64_t tile = cluster; tile < prm.tiles; tile += nclusters, ++it) {
-      const int64_t slice = tile / (prm.tiles_m * prm.tiles_n);
-      const int64_t rem = tile % (prm.tiles_m * prm.tiles_n);
+      const TileCoord tc = tile_coord<kSplit>(prm, tile);
+      const int64_t slice = tc.slice;
+      const int64_t rem = tc.rem;
       constexpr int64_t kRowsA = kOneAcc ? 128 : 256;  // a rows per CTA
       const int64_t m0 = (rem % prm.tiles_m) * (2 * kRowsA) + (int64_t)rank * kRowsA;
       const int64_t n0 = (rem / prm.tiles_m) * ncols;
       const int64_t slice_b = prm.P.batch_b == 1 ? 0 : slice;
       if (!produce_rows_fp4<LG, Cfg::kStages, kPackedB, kOneAcc, false, kSeg>(
               prm, b, st, smem_s, Cfg::kStageA, lane, slice, slice_b, m0,
-              n0 + (int64_t)rank * half, half, tmem_base, warp, n0))
+              n0 + (int64_t)rank * half, half, tmem_base, warp, n0, kSplit ? tc.mc0 : 0,
+              kSplit ? tc.mc1 : -1))
         break;
+      int32_t *part = kSplit ? prm.part + tc.split * prm.part_stride : nullptr;
       if (!tile_epilogue<256, kSeg, true, true, kOneAcc>(prm, b, st, smem, tmem_base, warp, lane,
-                                                         slice, slice_b, m0, n0, it))
+                                                         slice, slice_b, m0, n0, it, part))
         break;
     }
   }
@@ -2296,6 +2349,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
                  "r"(kTmemAlloc));
   }
   if (threadIdx.x == 0 && *b.abort) atomicOr(prm.error, 1u);
+}
+
+// ---------------------------------------------------------------------------
+// Sum of the K splits' exact int32 partial counts, rescaled as the tile
+// epilogue would (per-row factor, row and column scales, bias, output type).
+__global__ void split_reduce_kernel(const GemmProblem P, const int32_t *__restrict__ part,
+                                    int ksplit, int64_t stride, int64_t m_rows, int64_t n_rows) {
+  const int64_t per_slice = m_rows * n_rows;
+  const int64_t total = P.batch * per_slice;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t slice = i / per_slice, r = i % per_slice;
+    const int64_t m = r / n_rows, n = r % n_rows;
+    const int64_t grow = slice * P.M + m;
+    const int L = row_stream_len(P, slice, grow);
+    if (L < 0) continue;  // the row belongs to another call
+    const int64_t o = grow * P.N + n;
+    int32_t acc = 0;
+    for (int sp = 0; sp < ksplit; ++sp) acc += part[sp * stride + o];
+    float y = 0.0f;
+    if (L > 0) {
+      const int64_t rb = (P.batch_b == 1 ? 0 : slice) * P.N + n;
+      y = sc_rescale_f(P.mode, sc_rescale_factor(P.mode, P.prec, L), acc, P.K, P.qa.scale[grow],
+                       P.qa.zero[grow], P.qa.rowsum[grow], P.qb.scale[rb], P.qb.zero[rb],
+                       P.qb.rowsum[rb]);
+    } else {
+      acc = 0;
+    }
+    if (P.bias) y = __fadd_rn(y, P.bias[n]);
+    store_out(P, o, y);
+    if (P.acc_out) P.acc_out[o] = acc;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -2479,10 +2564,10 @@ int fp4_tile_cols(int64_t n_rows, bool one_acc, bool seg = false) {
   return best;
 }
 
-template <int LG, bool kPackedB, bool kOneAcc, bool kSeg = false>
+template <int LG, bool kPackedB, bool kOneAcc, bool kSeg = false, bool kSplit = false>
 cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &tmap,
                               cudaStream_t s) {
-  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB, kOneAcc, kSeg>;
+  auto kern = gemm_tc_pair_fp4_kernel<LG, kPackedB, kOneAcc, kSeg, kSplit>;
   constexpr size_t kSmem = Fp4PairCfg<kOneAcc, kSeg ? kSegPairStages : kPairStages>::kSmem;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
@@ -2514,7 +2599,7 @@ cudaError_t launch_pair_fp4_v(const TcParams &prm, int dev, const CUtensorMap &t
 }
 
 template <int LG, bool kOneAcc>
-cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
+cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s, int ksplit) {
   prm.rep = 0x01010101u;
   prm.stage_bytes = Fp4PairCfg<kOneAcc>::kStage;
   prm.ncols = fp4_tile_cols(prm.n_rows, kOneAcc);
@@ -2524,6 +2609,15 @@ cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
   prm.tiles_m = (prm.m_rows + rows_tile - 1) / rows_tile;
   prm.tiles_n = (prm.n_rows + prm.ncols - 1) / prm.ncols;
   prm.tiles = prm.P.batch * prm.tiles_m * prm.tiles_n;
+  if (ksplit > 1) {
+    const int nmacro = (int)(prm.P.ldk >> 3);
+    prm.msplit = (nmacro + ksplit - 1) / ksplit;
+    prm.ksplit = (nmacro + prm.msplit - 1) / prm.msplit;
+    prm.tiles_split = prm.tiles;
+    prm.tiles *= prm.ksplit;
+    prm.part = prm.P.split_part;
+    prm.part_stride = prm.P.batch * prm.P.M * prm.P.N;
+  }
   CUtensorMap tmap;
   memset(&tmap, 0, sizeof(tmap));
   // prepacked e2m1 b (positions laid out at Lp = 2^prec) serves calls whose
@@ -2541,11 +2635,14 @@ cudaError_t launch_pair_fp4(TcParams prm, int dev, cudaStream_t s) {
                              const_cast<uint8_t *>(P.b_streams), gdim, gstride, box, estride,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-      if (r == CUDA_SUCCESS) return launch_pair_fp4_v<LG, true, kOneAcc>(prm, dev, tmap, s);
+      if (r == CUDA_SUCCESS)
+        return prm.ksplit > 1 ? launch_pair_fp4_v<LG, true, kOneAcc, false, true>(prm, dev, tmap, s)
+                              : launch_pair_fp4_v<LG, true, kOneAcc>(prm, dev, tmap, s);
     }
     // no encoder or a rejected map: generate b from the packed codes instead
   }
-  return launch_pair_fp4_v<LG, false, kOneAcc>(prm, dev, tmap, s);
+  return prm.ksplit > 1 ? launch_pair_fp4_v<LG, false, kOneAcc, false, true>(prm, dev, tmap, s)
+                        : launch_pair_fp4_v<LG, false, kOneAcc>(prm, dev, tmap, s);
 }
 
 // Segmented K on the e2m1 pairs (head-aligned compensation, chunk-D): one
@@ -2718,14 +2815,37 @@ bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows) {
   return (P.b_streams == nullptr || P.b_e2m1) && (P.ldk << lg) < (1LL << 24);
 }
 
+int tc_ksplit(const GemmProblem &P, int64_t m_rows, int64_t n_rows) {
+  if (m_rows <= 0 || n_rows <= 128 || P.nseg != 1 || P.batch <= 0) return 1;
+  if (!tc_supported(P) || !tc_nibble_pairs(P, m_rows, n_rows)) return 1;
+  const bool two = m_rows > kBM;
+  const int ncols = fp4_tile_cols(n_rows, !two);
+  const int64_t rows_tile = two ? 2 * kBM : kBM;
+  const int64_t tiles =
+      P.batch * ((m_rows + rows_tile - 1) / rows_tile) * ((n_rows + ncols - 1) / ncols);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t pairs = sms / 2;
+  if (2 * tiles > pairs) return 1;  // the output tiles already fill half of the pairs
+  const int64_t nmacro = P.ldk >> 3;
+  int64_t ks = pairs / tiles;
+  if (ks > nmacro / 4) ks = nmacro / 4;  // at least 32 reduction indices per split
+  if (ks < 2) return 1;
+  const int64_t msplit = (nmacro + ks - 1) / ks;
+  return (int)((nmacro + msplit - 1) / msplit);
+}
+
 int tc_tile_n(const GemmProblem &P, int64_t N) {
   const int bn = tc_block_n(N);
   return (P.nseg > 1 && bn > 128) ? 128 : bn;
 }
 
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
-                           unsigned int *error, cudaStream_t s) {
+                           unsigned int *error, cudaStream_t s, int *launches) {
+  *launches = 0;
   if (P.M == 0 || P.N == 0 || P.batch == 0 || m_rows == 0 || n_rows == 0) return cudaSuccess;
+  *launches = 1;
   TcParams prm{};
   prm.P = P;
   const int lg = padded_stream_log2(P);
@@ -2762,11 +2882,23 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
         if (bn == 64) return launch_fp4_narrow<64>(prm, sms, s);
         return launch_fp4_narrow<128>(prm, sms, s);
       }
-      // two accumulators (512-row tiles) when both sides are wide
+      // two accumulators (512-row tiles) when both sides are wide; K splits
+      // (with their reduce) when the tiles would leave most pairs idle
       const bool two = m_rows > kBM && n_rows > 128;
-      if (lg == 7) return two ? launch_pair_fp4<7, false>(prm, dev, s)
-                              : launch_pair_fp4<7, true>(prm, dev, s);
-      return two ? launch_pair_fp4<8, false>(prm, dev, s) : launch_pair_fp4<8, true>(prm, dev, s);
+      const int ks = P.split_part ? tc_ksplit(P, m_rows, n_rows) : 1;
+      cudaError_t e;
+      if (lg == 7)
+        e = two ? launch_pair_fp4<7, false>(prm, dev, s, ks) : launch_pair_fp4<7, true>(prm, dev, s, ks);
+      else
+        e = two ? launch_pair_fp4<8, false>(prm, dev, s, ks) : launch_pair_fp4<8, true>(prm, dev, s, ks);
+      if (e != cudaSuccess || ks <= 1) return e;
+      const int64_t total = P.batch * m_rows * n_rows;
+      int64_t blocks = (total + 255) / 256;
+      if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+      split_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(P, P.split_part, ks,
+                                                           P.batch * P.M * P.N, m_rows, n_rows);
+      *launches = 2;
+      return cudaGetLastError();
     }
     if (P.nseg == 1 && bn == 256 && m_rows > kBM) {
       if (lg == 6) return launch_pair<6>(prm, dev, s);

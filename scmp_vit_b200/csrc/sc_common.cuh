@@ -67,6 +67,9 @@ struct GemmProblem {
   int b_e2m1;
   // window of (a row, b row) pairs per slice this launch computes
   int64_t m_lo, m_hi, n_lo, n_hi;
+  // nullable int32 [ksplit, batch, M, N]: partial counts of K splits (the
+  // workspace region sized by tc_ksplit; no split without it)
+  int32_t *split_part;
 };
 
 // Per-row stream length in the engine's convention (see scmp_matmul_args).
@@ -153,8 +156,14 @@ int tc_stream_log2(const GemmProblem &P);
 // true when launch_gemm_tc runs the e2m1 CTA-pair kernel on this window (its
 // pool complement is laid out with nibble_pairs)
 bool tc_nibble_pairs(const GemmProblem &P, int64_t m_rows, int64_t n_rows);
+// *launches: kernels launched (the tile kernel, plus the reduce of K splits)
 cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
-                           unsigned int *error, cudaStream_t s);
+                           unsigned int *error, cudaStream_t s, int *launches);
+// K splits the tensor-core engine uses for this window (1 = none): problems
+// whose e2m1 pair tiles would fill less than half of the SM pairs (e.g. one
+// image's linear) split K so that every pair works; each split writes exact
+// int32 partial counts and one reduce kernel rescales their sum.
+int tc_ksplit(const GemmProblem &P, int64_t m_rows, int64_t n_rows);
 
 // Message of the last failure on this thread (capi.cu).
 void set_last_error(const char *msg);
