@@ -168,7 +168,7 @@ int check_packable(const scmp_matmul_args *x) {
   if (x->k_segment > 0 && x->k_segment != x->K) {
     if (x->sc_prec < 7 || (x->k_segment % 8) != 0)
       return fail(SCMP_EUNSUPPORTED,
-                  "prepacked segmented b needs sc_prec 7 or 8 and k_segment % 8 == 0");
+                  "prepacked segmented b needs sc_prec 7 or 8 and k_segment a multiple of 8");
     if (x->pool_dims < x->k_segment)
       return fail(SCMP_EINVAL, "prepacked b needs pool_dims >= k_segment");
   } else if (x->pool_dims < x->K) {

@@ -218,46 +218,63 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
 }
 
 // Thin windows with a short reduction (K <= 512, e.g. the 257th row / column
-// of Q@K^T and Attn@V): one thread per output walks all K indices, so no
-// lanes idle on a short K and the rescale runs on every lane.  Consecutive
-// threads take consecutive columns of a row (the a codes are shared).
-template <int LW>
+// of Q@K^T and Attn@V): G lanes per output (G = 8 for K <= 128, else 32)
+// split the reduction indices (lane j of a group takes d = j, j + G, ...),
+// so each lane walks K / G dependent table loads instead of K; the group's
+// signed counts are summed with shuffles and its first lane rescales and
+// stores.  Consecutive groups take consecutive columns of a row.
+template <int LW, int G>
 __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P) {
+  static_assert(G == 8 || G == 32, "lane groups of 8 or 32");
   const int64_t wm = P.m_hi - P.m_lo, wn = P.n_hi - P.n_lo;
   const int64_t total = P.batch * wm * wn;
   const int T = 1 << P.prec;
   const int WT = T >= 32 ? T / 32 : 1;
   const int pd = P.pool_dims;
   const int K = (int)P.K;
-  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t slice = o / (wm * wn);
-    const int64_t r = o % (wm * wn);
+  const int lane = threadIdx.x & 31;
+  const int j = lane & (G - 1);
+  constexpr int kGroupsPerWarp = 32 / G;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // the loop runs over warp-uniform bases, so every lane of a warp reaches
+  // the shuffles below; groups past the end compute a copy of the last output
+  // and store nothing
+  for (int64_t ow = gw * kGroupsPerWarp; ow < total; ow += nw * kGroupsPerWarp) {
+    const int64_t o = ow + lane / G;
+    const bool valid = o < total;
+    const int64_t oc = valid ? o : total - 1;
+    const int64_t slice = oc / (wm * wn);
+    const int64_t r = oc % (wm * wn);
     const int64_t gm = P.m_lo + r / wn, gn = P.n_lo + r % wn;
     const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
     const int64_t grow = slice * P.M + gm, brow = slice_b * P.N + gn;
     const int L = row_stream_len(P, slice, grow);
-    if (L < 0) continue;
     int acc = 0;
     if (L > 0) {
       const int16_t *ca = P.qa.code + grow * P.ldk;
       const int16_t *cb = P.qb.code + brow * P.ldk;
-      int dm = 0;  // d mod pool_dims
-      // one reduction index: window of a, stream word(s) of b from the table
-      auto step = [&](int a, int b) {
+      int dm = j % pd;  // pool row d mod pool_dims, advanced without a division
+      for (int d = j; d < K; d += G) {
+        const int a = ca[d], b = cb[d];
         const int k = ((a < 0 ? -a : a) * L) >> P.prec;
         const uint32_t *st = P.stream_table + ((int64_t)dm * (T + 1) + (b < 0 ? -b : b)) * WT;
-        if (++dm == pd) dm = 0;
+        dm += G;
+        while (dm >= pd) dm -= pd;
         int cnt = 0;
-        if (LW == 4 && WT == 4) {  // the four words of a 128-position stream in one load
-          const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(st));
-          const uint32_t sw[4] = {w4.x, w4.y, w4.z, w4.w};
+        if (LW % 4 == 0 && WT == LW) {
+          // whole streams of 128 / 256 positions: 16-byte loads (table rows
+          // are WT words, so entries start on 16 bytes), and the window word
+          // as one funnel shift of the low max(k - 32 w, 0) bits (clamped at 32)
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const int lo = 32 * w;
-            const uint32_t win =
-                k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
-            cnt += __popc(win & sw[w]);
+          for (int q = 0; q < LW / 4; ++q) {
+            const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(st) + q);
+            const uint32_t sw[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const uint32_t sh = (uint32_t)__viaddmax_s32(k, -32 * (4 * q + w), 0);
+              cnt += __popc(__funnelshift_lc(0xffffffffu, 0u, sh) & sw[w]);
+            }
           }
         } else {
 #pragma unroll
@@ -269,24 +286,11 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
           }
         }
         acc += ((a < 0) != (b < 0) ? -cnt : cnt);
-      };
-      int d = 0;
-      if ((P.ldk & 7) == 0) {
-        // codes 8 at a time: rows of ldk int16 codes start on 16 bytes
-        const uint4 *ca4 = reinterpret_cast<const uint4 *>(ca);
-        const uint4 *cb4 = reinterpret_cast<const uint4 *>(cb);
-        for (; d + 8 <= K; d += 8) {
-          const uint4 va = __ldg(ca4 + (d >> 3)), vb = __ldg(cb4 + (d >> 3));
-          const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            step((int)(int16_t)(wa[j] & 0xFFFFu), (int)(int16_t)(wb[j] & 0xFFFFu));
-            step((int)wa[j] >> 16, (int)wb[j] >> 16);
-          }
-        }
       }
-      for (; d < K; ++d) step(ca[d], cb[d]);
     }
+#pragma unroll
+    for (int off = G / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (!valid || j != 0 || L < 0) continue;
     float y = 0.0f;
     if (L > 0)
       y = sc_rescale(P.mode, P.prec, L, acc, P.K, P.qa.scale[grow], P.qa.zero[grow],
@@ -300,9 +304,13 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
 template <int LW>
 cudaError_t launch_thin_lane(const GemmProblem &P, cudaStream_t s) {
   const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
-  int64_t blocks = (total + 255) / 256;
+  const int G = P.K <= 128 ? 8 : 32;
+  int64_t blocks = (total * G + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  gemm_popc_thin_lane_kernel<LW><<<(unsigned)blocks, 256, 0, s>>>(P);
+  if (G == 8)
+    gemm_popc_thin_lane_kernel<LW, 8><<<(unsigned)blocks, 256, 0, s>>>(P);
+  else
+    gemm_popc_thin_lane_kernel<LW, 32><<<(unsigned)blocks, 256, 0, s>>>(P);
   return cudaGetLastError();
 }
 

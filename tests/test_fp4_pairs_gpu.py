@@ -237,3 +237,61 @@ def test_segments_on_pairs_per_row_lengths_and_batches(cuda_device):
     y_ref = y_ref.reshape(BH * M, N)
     y_ref[rowL == 0] = 0.0
     np.testing.assert_allclose(y.cpu().numpy().reshape(BH * M, N), y_ref, rtol=RTOL, atol=1e-30)
+
+
+# ----------------------------------------------------------------- K splits
+# Problems whose output tiles would leave most SM pairs idle (one image's
+# linear) split K across pairs: each split writes exact int32 partial counts
+# and a reduce kernel rescales their sum, so results are those of one pass.
+
+@pytest.mark.parametrize("prepacked", [False, True])
+def test_k_splits_match_oracle_with_row_lengths(cuda_device, prepacked):
+    from scmp_vit_b200.sc import prepack_b
+    dev = cuda_device
+    g = torch.Generator().manual_seed(5)
+    M, N, K, p = 250, 1024, 768, 8
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    bias = torch.randn(N, generator=g)
+    rowL = np.random.default_rng(2).choice([-1, 0, 64, 200, 256], M).astype(np.int32)
+    random.seed(7)
+    cfg = ch.make_sobol_simple_config(K, K, p)
+    bd = b.to(dev)
+    bb = prepack_b(bd, sc_prec=p, config=cfg) if prepacked else bd
+    out = torch.full((M, N), 7.0, device=dev)
+    acc = torch.full((M * N,), -9, dtype=torch.int32, device=dev)
+    l0 = _lib.kernel_launches()
+    sc_matmul(a.to(dev), bb, sc_prec=p, config=cfg, bias=bias.to(dev), out=out, acc_out=acc,
+              row_stoc_len=torch.from_numpy(rowL), engine="tcgen05")
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    Lc = np.where(rowL > 0, rowL, 1).astype(np.int32)
+    acc_ref, y_ref = sc_oracle.sc_matmul_ref(a.numpy(), b.numpy(), sc_prec=p, pool=cfg["table"],
+                                             bias=bias.numpy(), L_row=Lc)
+    y = out.cpu().numpy()
+    accg = acc.view(M, N).cpu().numpy()
+    keep, pruned = rowL > 0, rowL == 0
+    np.testing.assert_array_equal(accg[keep], acc_ref[0][keep])
+    np.testing.assert_allclose(y[keep], y_ref[0][keep], rtol=RTOL, atol=1e-30)
+    np.testing.assert_array_equal(accg[pruned], 0)
+    np.testing.assert_array_equal(y[pruned], np.broadcast_to(bias.numpy(), y[pruned].shape))
+    np.testing.assert_array_equal(y[rowL < 0], 7.0)  # rows of another call: untouched
+    np.testing.assert_array_equal(accg[rowL < 0], -9)
+    assert _lib.kernel_launches() - l0 >= 3  # quantise, tiles, reduce (at least)
+
+
+def test_k_splits_bf16_output(cuda_device):
+    dev = cuda_device
+    g = torch.Generator().manual_seed(6)
+    a = torch.randn(257, 1024, generator=g)
+    b = torch.randn(3072, 1024, generator=g) * 0.02
+    random.seed(1)
+    cfg = ch.make_sobol_simple_config(1024, 1024, 7)
+    y32 = sc_matmul(a.to(dev), b.to(dev), granularity="per_tensor", sc_prec=7, config=cfg,
+                    stoc_len=128)
+    y16 = sc_matmul(a.to(dev), b.to(dev), granularity="per_tensor", sc_prec=7, config=cfg,
+                    stoc_len=128, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert _lib.engine_status(reset=True) == 0
+    assert torch.equal(y16, y32.to(torch.bfloat16))
+
