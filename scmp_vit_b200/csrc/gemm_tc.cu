@@ -86,6 +86,11 @@ struct TcParams {
   uint32_t rep;          // 0x01010101
   uint32_t stage_bytes;  // TcCfg<BN>::kStage
   int ncols;             // e2m1 CTA pairs: b rows (accumulator columns) per tile
+  // e2m1 kernels: MMA k-steps (64 positions each) per 256-position stage that
+  // can meet a nonzero window; fewer than 4 when one stream length L < 2^p
+  // holds for every row at Lp = 256 (windows end before position
+  // ((2^p - 1) L) >> p, e.g. 3 steps at L = 192), so the rest are skipped
+  int mma_ksteps;
   // K splits (e2m1 pairs, one segment): prm.tiles = ksplit x tiles_split;
   // split s covers macro steps (8 reduction indices each) [s msplit,
   // min((s + 1) msplit, ldk / 8)) and its tiles write exact int32 counts to
@@ -2092,6 +2097,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             const uint32_t b0 = a0 + Cfg::kStageA;
 #pragma unroll
             for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
+              if (kk >= prm.mma_ksteps) break;  // past every window of the launch
               const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
 #pragma unroll
               for (int j = 0; j < kAcc; ++j) {
@@ -2304,6 +2310,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
           const uint32_t b0 = a0 + Cfg::kStageA;
 #pragma unroll
           for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
+            if (kk >= prm.mma_ksteps) break;  // past every window of the launch
             const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -2859,6 +2866,13 @@ cudaError_t launch_gemm_tc(const GemmProblem &P, int64_t m_rows, int64_t n_rows,
   prm.nkb_seg = P.nseg > 1 ? ((P.kseg << lg) / kKB) : prm.nkb;
   prm.m_rows = m_rows;
   prm.n_rows = n_rows;
+  prm.mma_ksteps = 4;
+  if (lg == 8 && !P.row_L && !P.slice_L) {
+    // the longest window of the launch: |code| <= 2^p - 1 at L = stoc_len
+    const int64_t kmax = ((((int64_t)1 << P.prec) - 1) * P.stoc_len) >> P.prec;
+    const int steps = (int)((kmax + 63) / 64);
+    prm.mma_ksteps = steps < 1 ? 1 : (steps > 4 ? 4 : steps);
+  }
   const int bn = tc_tile_n(P, n_rows);
   prm.tiles_m = (m_rows + kBM - 1) / kBM;
   prm.tiles_n = (n_rows + bn - 1) / bn;

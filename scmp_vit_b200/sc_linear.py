@@ -136,7 +136,7 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
 
     With ``host_counts`` (rows per level, known without a device sync for
     quantile splits) the rows are sorted by level once and every call runs
-    on its own contiguous rows only; otherwise every call spans all rows and
+    on its own contiguous rows only, one call per level; otherwise every call spans all rows and
     skips the others (``row_stoc_len = -1``).  ``packed_for(p, config)``, if
     given, returns the weight prepacked for precision ``p`` (or None): the
     per-row calls then load its operand bytes instead of generating them."""
@@ -159,21 +159,26 @@ def sc_linear_rows(x2: torch.Tensor, w: torch.Tensor, row_L: torch.Tensor,
         # rows ordered by level: pruned first, then each precision's levels
         order = torch.sort(row_L, stable=True).indices
         xs = x2.index_select(0, order)
-        Ls = row_L.index_select(0, order)
         ys = torch.empty(M, N, dtype=torch.float32, device=x2.device)
         start = sum(c for L, c in host_counts.items() if int(L) <= 0)
         if start:
             ys[:start] = 0.0 if bias is None else bias.float()
         for p, Lset in by_prec.items():
-            n_rows = sum(host_counts.get(L, 0) for L in Lset)
-            if n_rows == 0:
+            if sum(host_counts.get(L, 0) for L in Lset) == 0:
                 continue
             cfg = cfg_for(chunk_d if use_chunk else K, p)
             b = _packed_or(w, packed_for, p, cfg, use_chunk)
-            sc_matmul(xs[start:start + n_rows], b, granularity="per_row", mode=mode, sc_prec=p,
-                      config=cfg, chunk_d=chunk_d if use_chunk else 0, bias=bias,
-                      row_stoc_len=Ls[start:start + n_rows], out=ys[start:start + n_rows])
-            start += n_rows
+            # one call per level: with a single stream length the engine runs
+            # only the stream positions a window can reach (L = 192 at p = 8:
+            # three quarters of each 256-position stage)
+            for L in Lset:
+                n_rows = host_counts.get(L, 0)
+                if n_rows == 0:
+                    continue
+                sc_matmul(xs[start:start + n_rows], b, granularity="per_row", mode=mode,
+                          sc_prec=p, config=cfg, chunk_d=chunk_d if use_chunk else 0, bias=bias,
+                          stoc_len=L, out=ys[start:start + n_rows])
+                start += n_rows
         out.index_copy_(0, order, ys)
         return out
     first = True

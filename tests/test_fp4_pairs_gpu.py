@@ -60,6 +60,13 @@ def _run(dev, a, b, p, L, *, mode="bipolar", granularity="per_row", bias=None, r
     (513, 257, 72, 7, 128),     # 257th a row and b column on the CUDA-core strips
     (4096, 2560, 16, 7, 128),   # many tiles per cluster
     (600, 640, 257, 7, 128),    # K = 257: codes padded to 264
+    # one stream length below 2^p at Lp = 256: the MMAs stop at the last
+    # 64-position step a window can reach (3 of 4 at L = 192 and 160, 3 at
+    # 129 -> windows up to 128 positions need only 2)
+    (512, 272, 24, 8, 192),     # two accumulators
+    (300, 300, 32, 8, 129),
+    (256, 1000, 64, 8, 160),    # one accumulator
+    (257, 64, 257, 8, 192),     # narrow tiles (Attn@V shape)
 ])
 def test_fp4_pair_shapes(cuda_device, M, N, K, p, L):
     g = torch.Generator().manual_seed(M * 7 + N * 3 + K)

@@ -54,6 +54,7 @@ def _same(dev, a, w, p, L=None, mode="bipolar", granularity="per_row", bias=None
     (600, 1024, 64, 7, None),
     (520, 3072, 32, 7, None),
     (700, 520, 48, 8, 256),
+    (600, 1024, 64, 8, 192),     # TMA b, three of the four MMA steps per stage
 ])
 def test_prepacked_equals_weight(cuda_device, M, N, K, p, L):
     g = torch.Generator().manual_seed(M + N + K)
