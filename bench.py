@@ -353,17 +353,24 @@ def measured_peaks() -> dict:
                 "source": "of fallback: 1.59 (burst) / 1.4 (sustained) PFLOP/s bf16 x4"}
 
 
-# DRAM bytes (read + write) of one qkv_proj e2m1 pair-kernel launch per image
-# at p = 7 (prepacked weight), from the ncu capture of 64 images
-# (profiles/gemm_tc_pair_fp4_vit_l14_qkv_b64.md): the activation and output
-# traffic grows with the images, the weight re-reads with the waves.
+# DRAM bytes (read + write) of one qkv_proj e2m1 pair-kernel launch
+# (prepacked weight): at p = 7 from the ncu capture of 64 images
+# (profiles/gemm_tc_pair_fp4_vit_l14_qkv_b64.md), scaled per image; at p = 8
+# the two-point fit of captures at 128 and 512 images
+# (profiles/gemm_tc_pair_fp4_qkv_p8_prepacked_dram.md): traffic is linear in
+# the images with a fixed part (the weight's reads).
 QKV_DRAM_BYTES_PER_IMAGE = (585.3e6 + 77.1e6) / 64
 QKV_DRAM_SOURCE = ("ncu dram__bytes_read+write of the e2m1 pair kernel at 64 images (p=7), "
                    "scaled per image; an estimate: weight re-reads do not scale with images")
+QKV_P8_DRAM_FIXED = 759_570_048
+QKV_P8_DRAM_PER_IMAGE = 17_689_163
+QKV_P8_DRAM_SOURCE = ("ncu dram__bytes_read+write of the prepacked e2m1 pair kernel (p=8) at 128 "
+                      "and 512 images: 3.02e9 and 9.82e9 B; linear fit 0.760 GB + 17.69 MB per "
+                      "image, evaluated at this launch's images")
 
 
 def roofline(kind: str, ms: float, bitops: float, peaks: dict, peak_i8: float, peak_popc: float,
-             images: int | None, sc_prec: int) -> dict:
+             images: int | None, sc_prec: int, uniform: bool = True) -> dict:
     """Roofline of one SC matmul kind.  One SC bit-product is one multiply-add
     on the tensor-core engine (2 ops: e2m1 operands with unit block scales)."""
     ach = 2 * bitops / (ms * 1e-3) / 1e12 if ms and ms > 0 else None
@@ -380,6 +387,10 @@ def roofline(kind: str, ms: float, bitops: float, peaks: dict, peak_i8: float, p
     if images and kind.startswith("sc_matmul qkv_proj") and sc_prec == 7:
         out["traffic"] = QKV_DRAM_BYTES_PER_IMAGE * images
         out["traffic_source"] = QKV_DRAM_SOURCE
+    elif (images and uniform and sc_prec == 8
+          and kind.startswith("sc_matmul qkv_proj (SCLinear, prepacked")):
+        out["traffic"] = float(QKV_P8_DRAM_FIXED + QKV_P8_DRAM_PER_IMAGE * images)
+        out["traffic_source"] = QKV_P8_DRAM_SOURCE
     else:
         out["traffic"] = None
     return out
@@ -699,7 +710,7 @@ def main():
     peak_i8 = int8_tensor_peak(dev)
     peaks = measured_peaks()
     roof = roofline("sc_matmul qkv_proj (SCLinear, prepacked weight by TMA)", qkv_ms, qkv_bitops,
-                    peaks, peak_i8, peak_popc, bl, p)
+                    peaks, peak_i8, peak_popc, bl, p, uniform=args.config != 4)
     if comp_d:
         roof["comp_head_aligned"] = {
             "per_launch_ms": comp_ms, "vs_out_proj": comp_ms / out_ms if out_ms else None,
