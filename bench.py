@@ -383,6 +383,13 @@ def roofline(kind: str, ms: float, bitops: float, peaks: dict, peak_i8: float, p
            "frac_of_int8_cublas_x2": ach / (2 * peak_i8 / 1e12) if (ach and peak_i8) else None,
            "x_int_pipe_roofline": (bitops / (ms * 1e-3)) / peak_popc if (ms and peak_popc)
            else None,
+           # the e2m1 MMA itself (scmp_probe_int_peak kind 3: M128 x N256 x K64
+           # kind::mxf4, back to back on every SM) runs faster than 4 x the
+           # bf16 GEMM; this is the fraction of that raw issue rate
+           "frac_of_mxf4_probe": (ach / (2 * peaks["mxf4_probe"] / 1e12)
+                                  if (ach and peaks.get("mxf4_probe")) else None),
+           "mxf4_probe_tops": (2 * peaks["mxf4_probe"] / 1e12 if peaks.get("mxf4_probe")
+                               else None),
            "int_pipe_peak_tbitops": peak_popc / 1e12 if peak_popc else None}
     if images and kind.startswith("sc_matmul qkv_proj") and sc_prec == 7:
         out["traffic"] = QKV_DRAM_BYTES_PER_IMAGE * images
@@ -709,6 +716,7 @@ def main():
     peak_popc = _lib.probe_int_peak(0)
     peak_i8 = int8_tensor_peak(dev)
     peaks = measured_peaks()
+    peaks["mxf4_probe"] = _lib.probe_int_peak(3)
     roof = roofline("sc_matmul qkv_proj (SCLinear, prepacked weight by TMA)", qkv_ms, qkv_bitops,
                     peaks, peak_i8, peak_popc, bl, p, uniform=args.config != 4)
     if comp_d:

