@@ -388,6 +388,16 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
+// The descriptor of addr + bytes from that of addr: the start-address field
+// holds (addr & 0x3FFFF) >> 4 in 14 bits, so adding bytes >> 4 is exact while
+// addr + bytes stays below 256 KB and bytes is a multiple of 16 (every tile
+// offset here).  One 64-bit add instead of rebuilding the descriptor: the
+// MMA thread shares its SM sub-partition with busy producer warps, and its
+// instructions per stage are on the tensor pipe's critical path.
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t bytes) {
+  return desc + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = BN.
 template <int BN>
 __host__ __device__ constexpr uint32_t idesc_i8() {
@@ -2080,6 +2090,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     // ====================================== MMA issuer (even CTA, lane 0)
     if (rank == 0 && lane == 0) {
       const uint32_t smem0 = smem_u32(smem);
+      const uint64_t desc0 = smem_desc_sw128(smem0);
       const uint32_t idesc = idesc_mxf4_pair(ncols);
       const uint32_t sf = tmem_base + kFp4SfCol;
       int stage = 0;
@@ -2102,18 +2113,18 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a0 = smem0 + stage * Cfg::kStage;
-            const uint32_t b0 = a0 + Cfg::kStageA;
+            const uint64_t dst = desc_add(desc0, (uint32_t)stage * Cfg::kStage);
+            const uint32_t acc0 = kb > 0 ? 1u : 0u;
 #pragma unroll
             for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
               if (kk >= prm.mma_ksteps) break;  // past every window of the launch
-              const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+              const uint64_t bdesc = desc_add(dst, Cfg::kStageA + kk * 32);
 #pragma unroll
               for (int j = 0; j < kAcc; ++j) {
-                const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+                const uint64_t adesc = desc_add(dst, j * (128 * kKB) + kk * 32);
                 // a and b read their (all-equal) scale factors from the same columns
                 tc_mma_mxf4_pair(tmem_base + (uint32_t)(j * ncols), adesc, bdesc, idesc, sf, sf,
-                                 (kb > 0 || kk > 0) ? 1u : 0u);
+                                 kk > 0 ? 1u : acc0);
               }
             }
             tc_commit_pair_both(&b.empty[stage]);
@@ -2306,6 +2317,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_mxf4_m128(BN);
       const uint32_t smem0 = smem_u32(smem);
+      const uint64_t desc0 = smem_desc_sw128(smem0);
       const uint32_t sf = tmem_base + kFp4SfCol;
       int stage = 0;
       uint32_t phase = 0;
@@ -2318,17 +2330,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_fp4_narrow_kernel(const T
         for (int64_t kb = 0; kb < prm.nkb; ++kb) {
           if (!mbar_wait(&b.full[stage], phase, b.abort)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = smem0 + stage * Cfg::kStage;
-          const uint32_t b0 = a0 + Cfg::kStageA;
+          const uint64_t dst = desc_add(desc0, (uint32_t)stage * Cfg::kStage);
+          const uint32_t acc0 = kb > 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < kKB / 32; ++kk) {  // 32 bytes = 64 positions per MMA
             if (kk >= prm.mma_ksteps) break;  // past every window of the launch
-            const uint64_t bdesc = smem_desc_sw128(b0 + kk * 32);
+            const uint64_t bdesc = desc_add(dst, Cfg::kStageA + kk * 32);
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-              const uint64_t adesc = smem_desc_sw128(a0 + j * (128 * kKB) + kk * 32);
+              const uint64_t adesc = desc_add(dst, j * (128 * kKB) + kk * 32);
               tc_mma_mxf4(tmem_base + (uint32_t)(j * BN), adesc, bdesc, idesc, sf,
-                          (kb > 0 || kk > 0) ? 1u : 0u);
+                          kk > 0 ? 1u : acc0);
             }
           }
           tc_commit(&b.empty[stage]);
