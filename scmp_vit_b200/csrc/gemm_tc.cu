@@ -90,7 +90,7 @@ struct TcParams {
   // can meet a nonzero window; fewer than 4 when one stream length L < 2^p
   // holds for every row at Lp = 256 (windows end before position
   // ((2^p - 1) L) >> p, e.g. 3 steps at L = 192), so the rest are skipped
-  int mma_ksteps;
+  int mma_ksteps = 4;
   // K splits (e2m1 pairs, one segment): prm.tiles = ksplit x tiles_split;
   // split s covers macro steps (8 reduction indices each) [s msplit,
   // min((s + 1) msplit, ldk / 8)) and its tiles write exact int32 counts to
