@@ -1420,6 +1420,11 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
     __syncwarp();
     const int64_t grow0 = slice * P.M + mrow0;
     const int myL = rowp[lane].x;  // stream length of this lane's row
+    // Bipolar outputs without counts to keep: the rescale ((acc * sa) * (sb *
+    // F), the oracle's order) is split at its first product, taken while a
+    // lane holds a row; after the transpose each element costs two multiplies.
+    const bool fast = !kSeg && P.mode == SCMP_BIPOLAR && part == nullptr && P.acc_out == nullptr;
+    const uint32_t skip_rows = __ballot_sync(0xffffffffu, myL < 0);  // rows of another call
 #pragma unroll 1
     for (int cc = cc_begin; cc < cc_end; cc += cc_step) {
       if (kF32 && cc * 32 >= ncols) break;  // warp-uniform
@@ -1458,10 +1463,21 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc_j * ncols + cc * 32),
                   v);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (fast) {
+          // count * sa of this lane's row (pruned rows: 0); e2m1 counts are
+          // exact integers in fp32, so (float)acc is the loaded value
+          const float sa_l = myL > 0 ? __int_as_float(rowp[lane].y) : 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)  // int32 counts as their bit patterns
-          stg[lane * 33 + i] =
-              kF32 ? __int_as_float(__float2int_rn(__uint_as_float(v[i]))) : __uint_as_float(v[i]);
+          for (int i = 0; i < 32; ++i) {
+            const float cnt = kF32 ? __uint_as_float(v[i]) : (float)(int32_t)v[i];
+            stg[lane * 33 + i] = myL > 0 ? __fmul_rn(cnt, sa_l) : 0.0f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)  // int32 counts as their bit patterns
+            stg[lane * 33 + i] = kF32 ? __int_as_float(__float2int_rn(__uint_as_float(v[i])))
+                                      : __uint_as_float(v[i]);
+        }
       }
       __syncwarp();
       // lane = column now
@@ -1476,6 +1492,19 @@ __device__ bool tile_epilogue(const TcParams &prm, const Bars &b, ProdState &st,
         zb = P.qb.zero[brw];
         rsb = P.qb.rowsum[brw];
         if (P.bias) bias = P.bias[gn];
+      }
+      if (!kSeg && fast) {
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          if ((skip_rows >> r) & 1u) continue;  // warp-uniform
+          // sb * F (F = 0 on pruned rows), then (count * sa) * that
+          const float fb = __fmul_rn(sb, rowF[r]);
+          float y = __fmul_rn(stg[r * 33 + lane], fb);
+          if (P.bias) y = __fadd_rn(y, bias);
+          if (col_ok) store_out(P, (grow0 + r) * P.N + gn, y);
+        }
+        __syncwarp();
+        continue;
       }
 #pragma unroll 4
       for (int r = 0; r < 32; ++r) {
