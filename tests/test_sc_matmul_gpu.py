@@ -11,6 +11,7 @@ import pytest
 import torch
 
 from oracle import sc_oracle
+from scmp_vit_b200 import _lib
 from scmp_vit_b200 import config_helpers as ch
 from scmp_vit_b200 import sc_matmul
 from scmp_vit_b200._lib import EngineError
@@ -206,3 +207,21 @@ def test_bad_stoc_len_raises(cuda_device):
     a = torch.randn(3, 4, device=cuda_device)
     with pytest.raises(EngineError, match="stoc_len"):
         sc_matmul(a, a, sc_prec=7, config=_cfg("sobol", 4, 7), stoc_len=129)
+
+
+@pytest.mark.parametrize("shape_a,shape_b", [
+    ((0, 16), (5, 16)),          # no a rows
+    ((7, 16), (0, 16)),          # no b rows
+    ((0, 9, 16), (0, 4, 16)),    # no slices
+    ((3, 0, 16), (4, 16)),       # batched, no rows per slice
+])
+def test_empty_operands_give_empty_outputs(cuda_device, shape_a, shape_b):
+    """Empty inputs (as the reference's torch code produces for an empty
+    batch) return correctly shaped empty outputs without a launch error."""
+    a = torch.randn(*shape_a, device=cuda_device)
+    b = torch.randn(*shape_b, device=cuda_device)
+    y = sc_matmul(a, b, sc_prec=7, config=_cfg("sobol", 16, 7))
+    torch.cuda.synchronize()
+    assert y.shape == (*shape_a[:-1], shape_b[-2])
+    assert y.numel() == 0
+    assert _lib.engine_status(reset=True) == 0
