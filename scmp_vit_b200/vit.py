@@ -28,6 +28,23 @@ from .mp import SeededRandomMPConfig, quantile_counts, set_current_block_idx
 from .sc_linear import PackedWeights, SCLinear, _get_config, sc_linear_rows
 
 
+def _fp_linear(lin: nn.Module, x: torch.Tensor) -> torch.Tensor:
+    """``lin(x)``; a plain ``nn.Linear`` with a bias on a CUDA input runs as a
+    matmul followed by an in-place bias add.  On B200 with fp32 operands that
+    is the same cuBLAS GEMM kernel as ``F.linear`` and the same single
+    rounding of ``acc + bias`` as its bias epilogue (identical bits), without
+    the epilogue's extra pass: ViT-L/14 fc1 at 128 images 5.07 -> 4.72 ms,
+    fc2 4.42 -> 4.33 ms.  CPU inputs keep ``F.linear``, whose ``addmm`` adds
+    the bias inside the GEMM, and so do 16-bit ones (the epilogue adds the
+    bias before the output is rounded)."""
+    if (type(lin) is not nn.Linear or lin.bias is None or not x.is_cuda
+            or x.dtype != torch.float32 or lin.weight.dtype != torch.float32):
+        return lin(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    y = torch.mm(x2, lin.weight.t()).add_(lin.bias)
+    return y.reshape(*x.shape[:-1], y.shape[-1])
+
+
 class Mlp(nn.Module):
     def __init__(self, dim: int, hidden: int):
         super().__init__()
@@ -36,7 +53,7 @@ class Mlp(nn.Module):
         self.fc2 = nn.Linear(hidden, dim)
 
     def forward(self, x):
-        return self.fc2(self.act(self.fc1(x)))
+        return _fp_linear(self.fc2, self.act(_fp_linear(self.fc1, x)))
 
 
 class Attention(nn.Module):

@@ -150,3 +150,19 @@ def test_vit_forward_small(cuda_device):
     assert torch.isfinite(y_sc).all()
     rel = (y_sc - y_fp).norm() / y_fp.norm()
     assert rel < 0.2, float(rel)
+
+
+@pytest.mark.parametrize("rows,d_in,d_out", [(514, 1024, 4096), (514, 4096, 1024), (77, 96, 40)])
+def test_fp_mlp_linear_matches_f_linear(cuda_device, rows, d_in, d_out):
+    """The ViT's FP MLP linears (matmul, then the bias added in place) give
+    F.linear's bits on CUDA fp32 (the ViT-L/14 fc1 / fc2 shapes and a ragged
+    one); bf16 inputs keep F.linear itself."""
+    from scmp_vit_b200 import vit
+    torch.backends.cuda.matmul.allow_tf32 = False
+    lin = _linear(d_in, d_out, rows).to(cuda_device)
+    x = torch.randn(2, rows // 2, d_in, generator=torch.Generator().manual_seed(d_in)).to(cuda_device)
+    with torch.no_grad():
+        assert torch.equal(vit._fp_linear(lin, x), nn.functional.linear(x, lin.weight, lin.bias))
+        lb = lin.to(torch.bfloat16)
+        xb = x.to(torch.bfloat16)
+        assert torch.equal(vit._fp_linear(lb, xb), nn.functional.linear(xb, lb.weight, lb.bias))
