@@ -108,6 +108,7 @@ void layout_operand(Carver &c, OperandLayout &o, int64_t K, int64_t ldc) {
 struct Plan {
   OperandLayout A, B;
   size_t table = 0;
+  size_t counts = 0;  // prefix counts of the stream table (thin strips)
   size_t pool_comp = 0;
   int64_t pool_comp_rows = 0;
   int64_t ldk = 0;
@@ -272,6 +273,7 @@ Plan make_plan(const scmp_matmul_args *x) {
   const int T = 1 << x->sc_prec;
   const int WT = T >= 32 ? T / 32 : 1;
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
+  p.counts = c.take(sizeof(uint16_t) * (size_t)x->pool_dims * (WT + 1) * (T + 1));
   p.pool_comp_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
   p.pool_comp = c.take((size_t)p.pool_comp_rows * T);
   p.ksplit = plan_ksplit(x, p.ldk);
@@ -499,6 +501,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.out_bf16 = (x.io_flags & SCMP_IO_OUT_BF16) != 0;
   P.acc_out = x.acc_out;
   P.stream_table = table;
+  P.count_table = reinterpret_cast<const uint16_t *>(ws + plan.counts);
   P.pool_comp = ws + plan.pool_comp;
   P.m_lo = 0;
   P.m_hi = x.M;
@@ -540,7 +543,9 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   const bool strip_m = use_tc && m_tc < x.M;
   const bool strip_n = use_tc && n_tc < x.N && m_tc > 0;
   if (!use_tc || strip_m || strip_n) {
-    if ((e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table, s)) != cudaSuccess)
+    if ((e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table,
+                                 reinterpret_cast<uint16_t *>(ws + plan.counts), s)) !=
+        cudaSuccess)
       return cuda_fail(e, "stream_table launch");
     count_launches(1);
   }

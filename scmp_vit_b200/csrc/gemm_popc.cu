@@ -219,34 +219,40 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
 
 // Thin windows with a short reduction (K <= 512, e.g. the 257th row / column
 // of Q@K^T and Attn@V): G lanes per output (G = 8 for K <= 128, else 32)
-// split the reduction indices (lane j of a group takes d = j, j + G, ...),
-// so each lane walks K / G dependent table loads instead of K; the group's
-// signed counts are summed with shuffles and its first lane rescales and
-// stores.  Consecutive groups take consecutive columns of a row.
-template <int LW, int G>
+// split the reduction indices (lane j of a group takes d = j, j + G, ...);
+// the group's signed counts are summed with shuffles and its first lane
+// rescales and stores.  Consecutive groups take consecutive columns of a row.
+// The count of index d is one prefix-count lookup and one masked stream word:
+//   #{t < k : R[d'][t] < v} = CT[d'][k / 32][v] + popc(ST[d'][v][k / 32] & (2^(k % 32) - 1))
+// (the word is not read past the stream: k = 2^p has no partial word).  Index
+// math is 32-bit: the host launches this kernel when batch x strip < 2^31.
+template <int G>
 __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P) {
   static_assert(G == 8 || G == 32, "lane groups of 8 or 32");
-  const int64_t wm = P.m_hi - P.m_lo, wn = P.n_hi - P.n_lo;
-  const int64_t total = P.batch * wm * wn;
+  const uint32_t wm = (uint32_t)(P.m_hi - P.m_lo), wn = (uint32_t)(P.n_hi - P.n_lo);
+  const uint32_t wmn = wm * wn;
+  const uint32_t total = (uint32_t)P.batch * wmn;
   const int T = 1 << P.prec;
   const int WT = T >= 32 ? T / 32 : 1;
   const int pd = P.pool_dims;
   const int K = (int)P.K;
   const int lane = threadIdx.x & 31;
   const int j = lane & (G - 1);
-  constexpr int kGroupsPerWarp = 32 / G;
-  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  constexpr uint32_t kGroupsPerWarp = 32 / G;
+  const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
   // the loop runs over warp-uniform bases, so every lane of a warp reaches
   // the shuffles below; groups past the end compute a copy of the last output
   // and store nothing
-  for (int64_t ow = gw * kGroupsPerWarp; ow < total; ow += nw * kGroupsPerWarp) {
-    const int64_t o = ow + lane / G;
+  for (uint32_t ow = gw * kGroupsPerWarp; ow < total; ow += nw * kGroupsPerWarp) {
+    const uint32_t o = ow + (uint32_t)lane / G;
     const bool valid = o < total;
-    const int64_t oc = valid ? o : total - 1;
-    const int64_t slice = oc / (wm * wn);
-    const int64_t r = oc % (wm * wn);
-    const int64_t gm = P.m_lo + r / wn, gn = P.n_lo + r % wn;
+    const uint32_t oc = valid ? o : total - 1;
+    const uint32_t sl = oc / wmn;
+    const uint32_t r = oc - sl * wmn;
+    const uint32_t rm = r / wn;
+    const int64_t slice = sl;
+    const int64_t gm = P.m_lo + rm, gn = P.n_lo + (r - rm * wn);
     const int64_t slice_b = P.batch_b == 1 ? 0 : slice;
     const int64_t grow = slice * P.M + gm, brow = slice_b * P.N + gn;
     const int L = row_stream_len(P, slice, grow);
@@ -257,34 +263,17 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
       int dm = j % pd;  // pool row d mod pool_dims, advanced without a division
       for (int d = j; d < K; d += G) {
         const int a = ca[d], b = cb[d];
-        const int k = ((a < 0 ? -a : a) * L) >> P.prec;
-        const uint32_t *st = P.stream_table + ((int64_t)dm * (T + 1) + (b < 0 ? -b : b)) * WT;
+        // (k <= 2^p for every valid stream length; the clamp keeps the
+        // table reads inside their rows whatever the per-row lengths hold)
+        const int k = min(((a < 0 ? -a : a) * L) >> P.prec, T);
+        const int v = b < 0 ? -b : b;
+        const int w = k >> 5;
+        const uint32_t word =
+            __ldg(P.stream_table + (dm * (T + 1) + v) * WT + (w < WT ? w : WT - 1));
+        const int cnt = (int)__ldg(P.count_table + (dm * (WT + 1) + w) * (T + 1) + v) +
+                        __popc(__funnelshift_lc(0xffffffffu, 0u, (uint32_t)(k & 31)) & word);
         dm += G;
         while (dm >= pd) dm -= pd;
-        int cnt = 0;
-        if (LW % 4 == 0 && WT == LW) {
-          // whole streams of 128 / 256 positions: 16-byte loads (table rows
-          // are WT words, so entries start on 16 bytes), and the window word
-          // as one funnel shift of the low max(k - 32 w, 0) bits (clamped at 32)
-#pragma unroll
-          for (int q = 0; q < LW / 4; ++q) {
-            const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(st) + q);
-            const uint32_t sw[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const uint32_t sh = (uint32_t)__viaddmax_s32(k, -32 * (4 * q + w), 0);
-              cnt += __popc(__funnelshift_lc(0xffffffffu, 0u, sh) & sw[w]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int w = 0; w < LW; ++w) {
-            const int lo = 32 * w;
-            const uint32_t win =
-                k >= lo + 32 ? 0xffffffffu : (k > lo ? ((1u << (k - lo)) - 1u) : 0u);
-            cnt += __popc(win & __ldg(st + w));
-          }
-        }
         acc += ((a < 0) != (b < 0) ? -cnt : cnt);
       }
     }
@@ -301,23 +290,22 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
   }
 }
 
-template <int LW>
 cudaError_t launch_thin_lane(const GemmProblem &P, cudaStream_t s) {
   const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
   const int G = P.K <= 128 ? 8 : 32;
   int64_t blocks = (total * G + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (G == 8)
-    gemm_popc_thin_lane_kernel<LW, 8><<<(unsigned)blocks, 256, 0, s>>>(P);
+    gemm_popc_thin_lane_kernel<8><<<(unsigned)blocks, 256, 0, s>>>(P);
   else
-    gemm_popc_thin_lane_kernel<LW, 32><<<(unsigned)blocks, 256, 0, s>>>(P);
+    gemm_popc_thin_lane_kernel<32><<<(unsigned)blocks, 256, 0, s>>>(P);
   return cudaGetLastError();
 }
 
 template <int LW>
 cudaError_t launch_thin(const GemmProblem &P, cudaStream_t s) {
-  if (P.K <= 512) return launch_thin_lane<LW>(P, s);
   const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
+  if (P.K <= 512 && P.count_table && total < ((int64_t)1 << 31)) return launch_thin_lane(P, s);
   int64_t blocks = (total + 7) / 8;  // 8 warps per block, one output per warp
   if (blocks > 148 * 32) blocks = 148 * 32;
   gemm_popc_thin_kernel<LW><<<(unsigned)blocks, 256, 0, s>>>(P);

@@ -58,6 +58,9 @@ struct GemmProblem {
   int32_t *acc_out;
   // stream table ST[pool_dims][2^p + 1][2^p / 32] (bit t of threshold v)
   const uint32_t *stream_table;
+  // prefix counts of the stream table, CT[pool_dims][2^p / 32 + 1][2^p + 1]:
+  // CT[d][w][v] = #{t < 32 w : R[d][t] < v} (the thin strips' counts)
+  const uint16_t *count_table;
   // pool complement PC[pool_dims][2^p] = 0x7F - (R >> shift) (tensor-core
   // row producers; shift = 1 for bipolar p = 8, else 0)
   const uint8_t *pool_comp;
@@ -126,8 +129,10 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
 cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64_t K,
                                  int64_t ldc, int mode, int prec, int16_t *code, float *rscale,
                                  int32_t *rzero, int32_t *rsum, cudaStream_t s);
+// The stream table and, when counts != NULL, its prefix counts (see
+// GemmProblem::count_table), from one pass over the pool.
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
-                                cudaStream_t s);
+                                uint16_t *counts, cudaStream_t s);
 // qkv [B, N, 3, H, D] -> q, k [B, H, N, D], vt [B, H, D, N] (elem_bytes 2 or 4)
 cudaError_t launch_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D,
                              int elem_bytes, void *q, void *k, void *vt, cudaStream_t s);
