@@ -261,20 +261,37 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
       const int16_t *ca = P.qa.code + grow * P.ldk;
       const int16_t *cb = P.qb.code + brow * P.ldk;
       int dm = j % pd;  // pool row d mod pool_dims, advanced without a division
-      for (int d = j; d < K; d += G) {
-        const int a = ca[d], b = cb[d];
-        // (k <= 2^p for every valid stream length; the clamp keeps the
-        // table reads inside their rows whatever the per-row lengths hold)
-        const int k = min(((a < 0 ? -a : a) * L) >> P.prec, T);
-        const int v = b < 0 ? -b : b;
-        const int w = k >> 5;
-        const uint32_t word =
-            __ldg(P.stream_table + (dm * (T + 1) + v) * WT + (w < WT ? w : WT - 1));
-        const int cnt = (int)__ldg(P.count_table + (dm * (WT + 1) + w) * (T + 1) + v) +
-                        __popc(__funnelshift_lc(0xffffffffu, 0u, (uint32_t)(k & 31)) & word);
-        dm += G;
-        while (dm >= pd) dm -= pd;
-        acc += ((a < 0) != (b < 0) ? -cnt : cnt);
+      // four indices per round: their code loads, then their table loads, are
+      // in flight together (indices past K read code 0: an empty window)
+      for (int d = j; d < K; d += 4 * G) {
+        int a[4], b[4], pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int di = d + i * G;
+          a[i] = di < K ? ca[di] : 0;
+          b[i] = di < K ? cb[di] : 0;
+          pr[i] = dm;
+          dm += G;
+          while (dm >= pd) dm -= pd;
+        }
+        int k[4], ct[4];
+        uint32_t word[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          // (k <= 2^p for every valid stream length; the clamp keeps the
+          // table reads inside their rows whatever the per-row lengths hold)
+          k[i] = min(((a[i] < 0 ? -a[i] : a[i]) * L) >> P.prec, T);
+          const int v = b[i] < 0 ? -b[i] : b[i];
+          const int w = k[i] >> 5;
+          word[i] = __ldg(P.stream_table + (pr[i] * (T + 1) + v) * WT + (w < WT ? w : WT - 1));
+          ct[i] = (int)__ldg(P.count_table + (pr[i] * (WT + 1) + w) * (T + 1) + v);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int cnt =
+              ct[i] + __popc(__funnelshift_lc(0xffffffffu, 0u, (uint32_t)(k[i] & 31)) & word[i]);
+          acc += ((a[i] < 0) != (b[i] < 0) ? -cnt : cnt);
+        }
       }
     }
 #pragma unroll

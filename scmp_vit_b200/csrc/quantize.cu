@@ -368,30 +368,46 @@ __global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int6
 }
 
 // ST[d][v][w]: bit j of word w = [R[d][32w+j] < v] for 32w+j < 2^p; with
-// counts, CT[d][w][v] = #{t < 32 w : R[d][t] < v} for w = 0 .. WT (one
-// thread per (d, v) builds both, v fastest, so the CT stores coalesce).
+// counts, CT[d][w][v] = #{t < 32 w : R[d][t] < v} for w = 0 .. WT.  One
+// thread per word; the WT words of a (d, v) sit in adjacent lanes, which
+// scan their popcounts with shuffles (WT divides 32, so a group never spans
+// two warps, and the loop runs over warp-aligned bases so that every lane
+// reaches the shuffles).
 __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_dims, int prec,
                                     uint32_t *__restrict__ table, uint16_t *__restrict__ counts) {
   const int T = 1 << prec;
   const int WT = T >= 32 ? T / 32 : 1;
-  const int64_t total = (int64_t)pool_dims * (T + 1);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int v = (int)(i % (T + 1));
-    const int64_t d = i / (T + 1);
-    const uint8_t *R = pool + d * T;
-    int cnt = 0;
-    for (int w = 0; w < WT; ++w) {
-      uint32_t word = 0;
-      for (int j = 0; j < 32; ++j) {
-        const int t = 32 * w + j;
-        if (t < T && (int)R[t] < v) word |= 1u << j;
-      }
-      table[i * WT + w] = word;
-      if (counts) counts[(d * (WT + 1) + w) * (T + 1) + v] = (uint16_t)cnt;
-      cnt += __popc(word);
+  const int64_t total = (int64_t)pool_dims * (T + 1) * WT;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) << 5; base < total;
+       base += warps << 5) {
+    const int64_t i = base + lane;
+    const bool valid = i < total;
+    const int w = (int)(i % WT);
+    const int64_t dv = i / WT;
+    const int v = (int)(dv % (T + 1));
+    const int64_t d = dv / (T + 1);
+    uint32_t word = 0;
+    if (valid) {
+      const uint8_t *R = pool + d * T + 32 * w;
+#pragma unroll 8
+      for (int j = 0; j < 32; ++j)
+        if (32 * w + j < T && (int)R[j] < v) word |= 1u << j;
+      table[i] = word;
     }
-    if (counts) counts[(d * (WT + 1) + WT) * (T + 1) + v] = (uint16_t)cnt;
+    if (counts) {
+      const int c = __popc(word);
+      int incl = c;
+      for (int off = 1; off < WT; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off, WT);
+        if (w >= off) incl += y;
+      }
+      if (valid) {
+        counts[(d * (WT + 1) + w) * (T + 1) + v] = (uint16_t)(incl - c);
+        if (w == WT - 1) counts[(d * (WT + 1) + WT) * (T + 1) + v] = (uint16_t)incl;
+      }
+    }
   }
 }
 
@@ -602,10 +618,11 @@ cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64
 
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 uint16_t *counts, cudaStream_t s) {
-  const int64_t threads = (int64_t)pool_dims * ((1 << prec) + 1);
+  const int T = 1 << prec;
+  const int64_t threads = (int64_t)pool_dims * (T + 1) * (T >= 32 ? T / 32 : 1);
   const int64_t blocks = (threads + 255) / 256;
-  stream_table_kernel<<<(unsigned)(blocks < 296 ? blocks : 296), 256, 0, s>>>(pool, pool_dims,
-                                                                               prec, table, counts);
+  stream_table_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, s>>>(
+      pool, pool_dims, prec, table, counts);
   return cudaGetLastError();
 }
 
