@@ -59,7 +59,8 @@ enum scmp_io_flags {
   SCMP_IO_A_BF16 = 1,   /* a is bf16: widened exactly to fp32 before quantisation */
   SCMP_IO_B_BF16 = 2,   /* b is bf16 */
   SCMP_IO_OUT_BF16 = 4, /* out is bf16: the fp32 result (bias included) rounded to nearest even */
-  SCMP_IO_B_PACKED = 8  /* b is a buffer written by scmp_prepack_b for the same b arguments */
+  SCMP_IO_B_PACKED = 8, /* b is a buffer written by scmp_prepack_b for the same b arguments */
+  SCMP_IO_A_QUANT = 16  /* a is a buffer written by scmp_softmax_quantize (per_row, group_a 1) */
 };
 enum scmp_engine {
   SCMP_ENGINE_AUTO = 0,
@@ -153,6 +154,27 @@ SCMP_API int scmp_sc_matmul_noalloc(const scmp_matmul_args *args, void *stream);
 SCMP_API size_t scmp_prepack_b_size(const scmp_matmul_args *args);
 SCMP_API int scmp_prepack_b(const scmp_matmul_args *args, void *packed, size_t packed_bytes,
                             void *stream);
+
+/* Softmax fused into the Attn@V a operand.  Replaces, in one call, the
+ * `attn.to(x.dtype) * self.scale` and `attn.softmax(dim=-1)` steps of
+ * cls/sc_attention_patch.py:292-295 and the per-row quantisation that the
+ * following sc_matmul(attn, v, granularity="per_row") applies to attn
+ * (sc_integration/sc_linear.py:95-111).  For `rows` rows of K fp32 scores
+ * (32 < K <= 1024), p = softmax(scale * scores) along each row with the
+ * arithmetic of torch.softmax's fp32 kernel for such rows (the same bits),
+ * then p quantised per row (mode, sc_prec) exactly as scmp_sc_matmul would
+ * quantise it, into `a_quant`: int16 codes [rows][ceil8(K)], then per-row
+ * scale, zero point and magnitude row sum, each region 256-byte aligned.
+ * Pass that buffer as `a` of scmp_sc_matmul with SCMP_IO_A_QUANT, batch * M
+ * = rows, the same K, mode and sc_prec, granularity per_row, group_a = 1:
+ * the result is bit-identical to passing the probabilities, which never have
+ * to be stored.  `probs` (nullable) receives them ([rows][K] fp32) anyway.
+ * scmp_softmax_quantize_size returns the buffer's size (0 on bad sizes).
+ * Asynchronous on `stream`; one launch. */
+SCMP_API size_t scmp_softmax_quantize_size(int64_t rows, int64_t K);
+SCMP_API int scmp_softmax_quantize(const float *scores, int64_t rows, int64_t K, float scale,
+                                   int mode, int sc_prec, void *a_quant, size_t a_quant_bytes,
+                                   float *probs, void *stream);
 
 /* Split the fused qkv projection output of an attention block into the SC
  * matmul operands (the reshape / unbind / transpose of the qkv output in

@@ -22,7 +22,7 @@ STATUS_NAMES = {
 GRANULARITY = {"per_row": 0, "per_head": 1, "per_tensor": 2}
 MODE = {"bipolar": 0, "unipolar": 1}
 ENGINE = {"auto": 0, "popc": 1, "tcgen05": 2}
-IO_A_BF16, IO_B_BF16, IO_OUT_BF16, IO_B_PACKED = 1, 2, 4, 8  # scmp_matmul_args.io_flags bits
+IO_A_BF16, IO_B_BF16, IO_OUT_BF16, IO_B_PACKED, IO_A_QUANT = 1, 2, 4, 8, 16  # io_flags bits
 
 EXPORTED_SYMBOLS = (
     "scmp_sc_matmul_workspace_size",
@@ -38,6 +38,8 @@ EXPORTED_SYMBOLS = (
     "scmp_prepack_b_size",
     "scmp_prepack_b",
     "scmp_split_qkv",
+    "scmp_softmax_quantize_size",
+    "scmp_softmax_quantize",
 )
 
 
@@ -125,6 +127,13 @@ def load() -> ctypes.CDLL:
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p]
         lib.scmp_split_qkv.restype = ctypes.c_int
+        lib.scmp_softmax_quantize_size.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        lib.scmp_softmax_quantize_size.restype = ctypes.c_size_t
+        lib.scmp_softmax_quantize.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_float, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                              ctypes.c_void_p]
+        lib.scmp_softmax_quantize.restype = ctypes.c_int
         lib.scmp_debug_set_wait_limit.argtypes = [ctypes.c_uint64]
         lib.scmp_debug_set_wait_limit.restype = ctypes.c_int
         lib.scmp_debug_hold_producers.argtypes = [ctypes.c_int]

@@ -33,7 +33,7 @@ from .mp import (
 from .mp_linear import sc_prec_for_stoc_len
 from .noise_matmul import _noisy_matmul_core
 from .config_helpers import make_sobol_simple_config
-from .sc import sc_matmul
+from .sc import sc_matmul, softmax_quantize
 
 CfgFor = Callable[[int, int], dict]
 
@@ -310,6 +310,40 @@ def sc_av(attn: torch.Tensor, v: torch.Tensor, sc_prec: int, *, mode: str = "bip
     return out.reshape(B, H, N, D)
 
 
+# Whether the attention forward fuses `* scale`, the softmax and the Attn@V
+# a-operand quantisation into one pass (scmp_softmax_quantize) where the
+# result is bit-identical to the unfused steps: fp32 glue, uniform Attn@V
+# stream length, rows of 33 to 1024 tokens.
+FUSED_SOFTMAX = True
+
+
+def set_fused_softmax(flag: bool) -> None:
+    """Turn the fused softmax + Attn@V quantisation on or off (results are
+    identical either way; off runs torch.softmax and quantises its output)."""
+    global FUSED_SOFTMAX
+    FUSED_SOFTMAX = bool(flag)
+
+
+def sc_softmax_av(scores: torch.Tensor, scale: float, v: torch.Tensor, sc_prec: int, *,
+                  mode: str = "bipolar", cfg_for: Optional[CfgFor] = None) -> torch.Tensor:
+    """``sc_av(softmax(scores * scale), v)`` for fp32 scores ``[B, H, N, N]``
+    and v ``[B, H, N, D]``, with the softmax and the per-row quantisation of
+    its probabilities in one engine pass: the probabilities are never
+    stored, and the result equals the unfused steps bit for bit."""
+    cfg_for = cfg_for or _scl._get_config
+    B, H, N, D = v.shape
+    qa = softmax_quantize(scores.reshape(B * H, N, N), scale, mode=mode, sc_prec=sc_prec)
+    out = sc_matmul(qa, v.transpose(-1, -2).reshape(B * H, D, N), granularity="per_row",
+                    group_a=1, group_b=1, mode=mode, sc_prec=sc_prec, config=cfg_for(N, sc_prec))
+    return out.reshape(B, H, N, D)
+
+
+def _fused_softmax_applies(scores: torch.Tensor, x: torch.Tensor, av_mp_cfg) -> bool:
+    return (FUSED_SOFTMAX and av_mp_cfg is None and not _scl.USE_NOISE_MODEL
+            and sc_av_fn is sc_av and x.dtype == torch.float32 and scores.is_cuda
+            and scores.dtype == torch.float32 and 32 < scores.shape[-1] <= 1024)
+
+
 def _glue_dtype(x: torch.Tensor) -> Optional[torch.dtype]:
     """bf16 models take SC results in bf16 straight from the engine (the same
     values ``.to(torch.bfloat16)`` gives); otherwise fp32."""
@@ -358,6 +392,10 @@ def make_sc_attention_forward(sc_prec: int, sc_av: bool, sc_qk: bool = True,
         if sc_qk:
             attn = sc_qk_fn(q, k, sc_prec, mp_cfg=qk_mp_cfg, cfg_for=cfg_for,
                             out_dtype=_glue_dtype(x))
+            if do_av and _fused_softmax_applies(attn, x, av_mp_cfg):
+                out = sc_softmax_av(attn, self.scale, v, sc_prec, mode=av_mode, cfg_for=cfg_for)
+                out = out.transpose(1, 2).reshape(B, N, C)
+                return self.proj_drop(self.proj(out))
             attn = attn.to(x.dtype) * self.scale
         else:
             attn = (q @ k.transpose(-2, -1)) * self.scale

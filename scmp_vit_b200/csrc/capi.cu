@@ -148,8 +148,15 @@ int validate(const scmp_matmul_args *x) {
         (x->granularity != SCMP_PER_ROW || x->group_a != 1 || x->group_b != 1))
       return fail(SCMP_EINVAL, "k_segment needs granularity per_row with group_a=group_b=1");
   }
-  if (x->io_flags & ~(SCMP_IO_A_BF16 | SCMP_IO_B_BF16 | SCMP_IO_OUT_BF16 | SCMP_IO_B_PACKED))
+  if (x->io_flags & ~(SCMP_IO_A_BF16 | SCMP_IO_B_BF16 | SCMP_IO_OUT_BF16 | SCMP_IO_B_PACKED |
+                      SCMP_IO_A_QUANT))
     return fail(SCMP_EINVAL, "unknown io_flags bits 0x%x", (unsigned)x->io_flags);
+  if ((x->io_flags & SCMP_IO_A_QUANT) &&
+      ((x->io_flags & SCMP_IO_A_BF16) || x->granularity != SCMP_PER_ROW || x->group_a != 1 ||
+       (x->k_segment > 0 && x->k_segment != x->K)))
+    return fail(SCMP_EINVAL,
+                "a quantised a (SCMP_IO_A_QUANT) needs granularity per_row, group_a = 1 and "
+                "no k_segment");
   if (x->engine != SCMP_ENGINE_AUTO && x->engine != SCMP_ENGINE_POPC &&
       x->engine != SCMP_ENGINE_TCGEN05)
     return fail(SCMP_EINVAL, "unknown engine %d", x->engine);
@@ -263,7 +270,10 @@ Plan make_plan(const scmp_matmul_args *x) {
   Carver c;
   // Segmented K is quantised as [rows * nseg, kseg] with one group per row.
   const int64_t kseg = seg_len(x), nseg = x->K / kseg;
-  p.A.g = make_groups(x->granularity, x->batch, x->M * nseg, nseg > 1 ? 1 : x->group_a);
+  // a quantised a (SCMP_IO_A_QUANT) brings its own codes: no a planes here
+  const bool a_quant = (x->io_flags & SCMP_IO_A_QUANT) != 0;
+  p.A.g = make_groups(x->granularity, a_quant ? 0 : x->batch, x->M * nseg,
+                      nseg > 1 ? 1 : x->group_a);
   p.B.g = make_groups(x->granularity, x->batch_b, x->N * nseg, nseg > 1 ? 1 : x->group_b);
   // unsegmented code rows are padded to a multiple of 8 (16-byte rows)
   const int64_t ldc = nseg > 1 ? kseg : (kseg + 7) / 8 * 8;
@@ -281,6 +291,25 @@ Plan make_plan(const scmp_matmul_args *x) {
     p.split = c.take(sizeof(int32_t) * (size_t)p.ksplit * (size_t)(x->batch * x->M * x->N));
   p.total = c.off;
   return p;
+}
+
+// Layout of a quantised a operand (scmp_softmax_quantize, SCMP_IO_A_QUANT):
+// int16 codes [rows][ldc] (ldc = K rounded up to 8, zero codes past K), then
+// per-row scale (fp32), zero point and magnitude row sum (int32).
+struct QuantALayout {
+  size_t code = 0, rscale = 0, rzero = 0, rsum = 0, total = 0;
+  int64_t ldc = 0;
+};
+QuantALayout quant_a_layout(int64_t rows, int64_t K) {
+  QuantALayout q;
+  Carver c;
+  q.ldc = (K + 7) / 8 * 8;
+  q.code = c.take(sizeof(int16_t) * (size_t)rows * (size_t)q.ldc);
+  q.rscale = c.take(sizeof(float) * (size_t)rows);
+  q.rzero = c.take(sizeof(int32_t) * (size_t)rows);
+  q.rsum = c.take(sizeof(int32_t) * (size_t)rows);
+  q.total = c.off;
+  return q;
 }
 
 int quantize_operand(const void *x, bool x_bf16, const OperandLayout &o, int64_t K, int mode,
@@ -436,6 +465,41 @@ int scmp_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D, 
   return SCMP_OK;
 }
 
+size_t scmp_softmax_quantize_size(int64_t rows, int64_t K) {
+  if (rows < 0 || K <= 0) return 0;
+  return quant_a_layout(rows, K).total;
+}
+
+int scmp_softmax_quantize(const float *scores, int64_t rows, int64_t K, float scale, int mode,
+                          int sc_prec, void *a_quant, size_t a_quant_bytes, float *probs,
+                          void *stream) {
+  g_last_error.clear();
+  if (rows < 0 || K <= 0)
+    return fail(SCMP_EINVAL, "bad shape rows=%lld K=%lld", (long long)rows, (long long)K);
+  if (K <= 32 || K > 1024)
+    return fail(SCMP_EUNSUPPORTED, "softmax_quantize takes rows of 33 to 1024 values, got %lld",
+                (long long)K);
+  if (mode != SCMP_BIPOLAR && mode != SCMP_UNIPOLAR)
+    return fail(SCMP_EINVAL, "unknown mode %d", mode);
+  if (sc_prec < 1 || sc_prec > kMaxPrec || (mode == SCMP_BIPOLAR && sc_prec < 2))
+    return fail(SCMP_EINVAL, "sc_prec=%d out of range for mode %d", sc_prec, mode);
+  const QuantALayout q = quant_a_layout(rows, K);
+  if (rows == 0) return SCMP_OK;
+  if (!scores || !a_quant) return fail(SCMP_EINVAL, "scores and a_quant must be non-NULL");
+  if (a_quant_bytes < q.total)
+    return fail(SCMP_EWORKSPACE, "a_quant needs %zu bytes, got %zu", q.total, a_quant_bytes);
+  if ((reinterpret_cast<uintptr_t>(a_quant) & (kAlign - 1)) != 0)
+    return fail(SCMP_EINVAL, "a_quant must be %zu-byte aligned", kAlign);
+  auto *pa = static_cast<unsigned char *>(a_quant);
+  const cudaError_t e = launch_softmax_quantize(
+      scores, rows, (int)K, scale, mode, sc_prec, q.ldc, reinterpret_cast<int16_t *>(pa + q.code),
+      reinterpret_cast<float *>(pa + q.rscale), reinterpret_cast<int32_t *>(pa + q.rzero),
+      reinterpret_cast<int32_t *>(pa + q.rsum), probs, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "softmax_quantize launch");
+  count_launches(1);
+  return SCMP_OK;
+}
+
 size_t scmp_sc_matmul_workspace_size(const scmp_matmul_args *args) {
   if (validate(args) != SCMP_OK) return 0;
   if (args->batch == 0 || args->M == 0 || args->N == 0) return kAlign;
@@ -459,9 +523,10 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
 
   const int64_t kseg = seg_len(&x);
   const bool packed = (x.io_flags & SCMP_IO_B_PACKED) != 0;
+  const bool a_quant = (x.io_flags & SCMP_IO_A_QUANT) != 0;
   if (packed && (rc = check_packable(&x)) != SCMP_OK) return rc;
-  if ((rc = quantize_operand(x.a, (x.io_flags & SCMP_IO_A_BF16) != 0, plan.A, kseg, x.mode,
-                             x.sc_prec, ws, s)) != SCMP_OK)
+  if (!a_quant && (rc = quantize_operand(x.a, (x.io_flags & SCMP_IO_A_BF16) != 0, plan.A, kseg,
+                                         x.mode, x.sc_prec, ws, s)) != SCMP_OK)
     return rc;
   if (!packed && (rc = quantize_operand(x.b, (x.io_flags & SCMP_IO_B_BF16) != 0, plan.B, kseg,
                                         x.mode, x.sc_prec, ws, s)) != SCMP_OK)
@@ -470,7 +535,17 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   cudaError_t e;
 
   GemmProblem P{};
-  P.qa = plane_of(plan.A, ws);
+  if (a_quant) {
+    // codes and row records written by scmp_softmax_quantize for these rows
+    const QuantALayout qa = quant_a_layout(x.batch * x.M, x.K);
+    auto *pa = static_cast<unsigned char *>(const_cast<void *>(x.a));
+    P.qa.code = reinterpret_cast<const int16_t *>(pa + qa.code);
+    P.qa.scale = reinterpret_cast<const float *>(pa + qa.rscale);
+    P.qa.zero = reinterpret_cast<const int32_t *>(pa + qa.rzero);
+    P.qa.rowsum = reinterpret_cast<const int32_t *>(pa + qa.rsum);
+  } else {
+    P.qa = plane_of(plan.A, ws);
+  }
   if (packed) {
     // b's codes, scales and operand bytes were written by scmp_prepack_b
     const PackPlan pk = make_pack_plan(&x);

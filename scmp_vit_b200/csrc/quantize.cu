@@ -367,6 +367,100 @@ __global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int6
   }
 }
 
+// Softmax of scale * x along rows of K (32 < K <= 1024) values, then the
+// per-row quantisation of the probabilities (the a operand of a per-row
+// Attn@V call), in one pass with one warp per row.  The softmax repeats the
+// arithmetic of torch.softmax's warp-per-row kernel for fp32 rows of up to
+// 1024 values, so the probabilities carry the same bits: lane l holds the
+// elements l + 32 i (i < NI, NI = the next power of two >= K, over 32;
+// -inf past K); the row maximum is taken by lane, in i order, then by xor
+// butterfly; e = expf(v - max) is summed by lane in i order starting from
+// 0, then by xor butterfly; p = e / sum (IEEE division).  The quantisation
+// is that of quantize_rows_kernel (group_scale_of, round half to even, the
+// same clamps and row sums), so codes and row records are identical to
+// quantising the probabilities after torch.softmax.  probs (nullable)
+// receives the probabilities.
+template <int NI>
+__global__ void __launch_bounds__(256) softmax_quantize_kernel(
+    const float *__restrict__ x, int64_t rows, int K, float scale, int mode, int prec,
+    int64_t ldc, int16_t *__restrict__ code, float *__restrict__ rscale,
+    int32_t *__restrict__ rzero, int32_t *__restrict__ rsum, float *__restrict__ probs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const bool bip = mode == SCMP_BIPOLAR;
+  const int iq = bip ? (1 << (prec - 1)) - 1 : (1 << prec) - 1;
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += nwarps) {
+    const float *xr = x + r * K;
+    float v[NI];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int idx = lane + 32 * i;
+      v[i] = idx < K ? __fmul_rn(__ldg(xr + idx), scale) : -INFINITY;
+    }
+    float mx = v[0];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) mx = mx > v[i] ? mx : v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, mx, o);
+      mx = mx < t ? t : mx;
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      v[i] = expf(__fsub_rn(v[i], mx));
+      sum = __fadd_rn(sum, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int idx = lane + 32 * i;
+      if (idx < K) {
+        v[i] = __fdiv_rn(v[i], sum);
+        if (probs) probs[r * K + idx] = v[i];
+        if (bip) {
+          hi = fmaxf(hi, fabsf(v[i]));
+        } else {
+          lo = fminf(lo, v[i]);
+          hi = fmaxf(hi, v[i]);
+        }
+      }
+    }
+    hi = warp_max(hi);
+    lo = warp_min(lo);
+    float sc, inv;
+    int32_t z;
+    group_scale_of(lo, hi, mode, prec, sc, inv, z);
+    int16_t *cr = code + r * ldc;
+    int acc = 0;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int idx = lane + 32 * i;
+      if (idx < K) {
+        int q = __float2int_rn(__fmul_rn(v[i], inv));
+        if (bip) {
+          q = max(-iq, min(iq, q));
+          cr[idx] = (int16_t)(2 * q);
+          acc += 2 * abs(q);
+        } else {
+          q = max(0, min(iq, q + z));
+          cr[idx] = (int16_t)q;
+          acc += q;
+        }
+      }
+    }
+    for (int64_t i = K + lane; i < ldc; i += 32) cr[i] = 0;
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      rscale[r] = sc;
+      rzero[r] = z;
+      rsum[r] = acc;
+    }
+  }
+}
+
 // ST[d][v][w]: bit j of word w = [R[d][32w+j] < v] for 32w+j < 2^p; with
 // counts, CT[d][w][v] = #{t < 32 w : R[d][t] < v} for w = 0 .. WT.  One
 // thread per word; the WT words of a (d, v) sit in adjacent lanes, which
@@ -524,6 +618,29 @@ cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, i
   else
     pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift,
                                                            pool_period, pool_comp, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_softmax_quantize(const float *x, int64_t rows, int K, float scale, int mode,
+                                    int prec, int64_t ldc, int16_t *code, float *rscale,
+                                    int32_t *rzero, int32_t *rsum, float *probs, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  int64_t blocks = (rows + 7) / 8;  // 8 warps per block, one row per warp
+  if (blocks > 148 * 16) blocks = 148 * 16;
+#define SCMP_SOFTMAX_Q(NI)                                                                      \
+  softmax_quantize_kernel<NI><<<(unsigned)blocks, 256, 0, s>>>(x, rows, K, scale, mode, prec, ldc, \
+                                                               code, rscale, rzero, rsum, probs)
+  if (K <= 64)
+    SCMP_SOFTMAX_Q(2);
+  else if (K <= 128)
+    SCMP_SOFTMAX_Q(4);
+  else if (K <= 256)
+    SCMP_SOFTMAX_Q(8);
+  else if (K <= 512)
+    SCMP_SOFTMAX_Q(16);
+  else
+    SCMP_SOFTMAX_Q(32);
+#undef SCMP_SOFTMAX_Q
   return cudaGetLastError();
 }
 

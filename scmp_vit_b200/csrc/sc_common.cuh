@@ -129,6 +129,12 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
 cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64_t K,
                                  int64_t ldc, int mode, int prec, int16_t *code, float *rscale,
                                  int32_t *rzero, int32_t *rsum, cudaStream_t s);
+// Row softmax of scale * x (fp32, 32 < K <= 1024; torch.softmax's bits)
+// and its per-row quantisation into codes [rows][ldc] and row records;
+// probs (nullable) receives the probabilities.
+cudaError_t launch_softmax_quantize(const float *x, int64_t rows, int K, float scale, int mode,
+                                    int prec, int64_t ldc, int16_t *code, float *rscale,
+                                    int32_t *rzero, int32_t *rsum, float *probs, cudaStream_t s);
 // The stream table and, when counts != NULL, its prefix counts (see
 // GemmProblem::count_table), from one pass over the pool.
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,

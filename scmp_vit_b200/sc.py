@@ -30,7 +30,7 @@ from . import _lib
 from .config_helpers import make_sobol_simple_config, pool_table
 
 __all__ = ["sc_matmul", "device_pool", "default_config", "set_default_engine", "prepack_b",
-           "PackedWeight"]
+           "PackedWeight", "softmax_quantize", "QuantizedRows"]
 
 _DEFAULT_ENGINE = "auto"
 
@@ -107,6 +107,58 @@ class PackedWeight:
                 sc_prec == self.sc_prec and config["uid"] == self.config["uid"] and
                 int(k_segment) == self.k_segment and
                 (granularity != "per_row" or max(int(group_b), 1) == self.group_b))
+
+
+class QuantizedRows:
+    """Softmax probabilities already quantised as the a operand of a per-row
+    ``sc_matmul`` (``softmax_quantize``): int16 codes and per-row scale /
+    zero point / row sum in the engine's layout.  Pass it as ``a`` with
+    ``granularity="per_row"``, ``group_a=1`` and the same ``mode`` and
+    ``sc_prec``; the result is bit-identical to passing the probabilities.
+    ``probs`` holds the probabilities when they were asked for."""
+
+    def __init__(self, buf: torch.Tensor, shape, mode: str, sc_prec: int,
+                 probs: Optional[torch.Tensor] = None):
+        self.buf = buf
+        self.shape = tuple(int(d) for d in shape)
+        self.mode, self.sc_prec = mode, int(sc_prec)
+        self.probs = probs
+        self.device = buf.device
+        self.is_cuda = buf.is_cuda
+
+    def dim(self) -> int:
+        return len(self.shape)
+
+
+@torch.no_grad()
+def softmax_quantize(scores: torch.Tensor, scale: float, *, mode: str = "bipolar",
+                     sc_prec: int = 8, keep_probs: bool = False) -> QuantizedRows:
+    """``softmax(scores * scale, dim=-1)`` quantised per row for the a operand
+    of ``sc_matmul``, in one pass (``scmp_softmax_quantize``): the
+    probabilities carry torch.softmax's fp32 bits and their codes are those
+    ``sc_matmul`` would compute, without storing the probabilities
+    (``keep_probs`` stores them in ``.probs`` as well).  ``scores``: fp32
+    CUDA ``[..., K]`` with 32 < K <= 1024."""
+    if mode not in _lib.MODE:
+        raise ValueError(f"unknown mode {mode!r}")
+    if not scores.is_cuda or scores.dtype != torch.float32:
+        raise ValueError("softmax_quantize takes fp32 CUDA scores")
+    x = scores.contiguous()
+    K = x.shape[-1]
+    rows = x.numel() // K if K else 0
+    lib = _lib.load()
+    nbytes = lib.scmp_softmax_quantize_size(rows, K)
+    if nbytes == 0:
+        raise ValueError(f"bad softmax_quantize shape {tuple(x.shape)}")
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    probs = torch.empty_like(x) if keep_probs else None
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(lib.scmp_softmax_quantize(
+            ctypes.c_void_p(x.data_ptr()), rows, K, float(scale), _lib.MODE[mode], int(sc_prec),
+            ctypes.c_void_p(buf.data_ptr()), nbytes, ctypes.c_void_p(_ptr(probs)),
+            ctypes.c_void_p(stream)))
+    return QuantizedRows(buf, x.shape, mode, sc_prec, probs)
 
 
 def _base_args(engine: str, granularity: str, mode: str, p: int, L: int, group_a: int,
@@ -207,6 +259,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     if engine not in _lib.ENGINE:
         raise ValueError(f"unknown engine {engine!r}")
     packed = b if isinstance(b, PackedWeight) else None
+    qa = a if isinstance(a, QuantizedRows) else None
     if a.dim() not in (2, 3) or (packed is None and b.dim() not in (2, 3)):
         raise ValueError(f"sc_matmul expects 2-D or 3-D operands, got {tuple(a.shape)} "
                          f"and {tuple(b.shape)}")
@@ -216,8 +269,16 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     if a.device != b.device:
         raise ValueError(f"operands on different devices: {a.device} vs {b.device}")
     batched = a.dim() == 3
-    a3 = a if batched else a.unsqueeze(0)
-    BH, M, K = a3.shape
+    if qa is not None:
+        a3 = None
+        BH, M, K = qa.shape if batched else (1,) + qa.shape
+        if (granularity != "per_row" or max(int(group_a), 1) != 1 or mode != qa.mode
+                or int(sc_prec) != qa.sc_prec or chunk_d or int(k_segment or 0) not in (0, K)):
+            raise ValueError("a quantised a runs per_row with group_a=1, its own mode and "
+                             "sc_prec, and no chunk_d / k_segment")
+    else:
+        a3 = a if batched else a.unsqueeze(0)
+        BH, M, K = a3.shape
     if packed is not None:
         BHb, N, Kb = 1, packed.N, packed.K
         b3 = None
@@ -240,7 +301,8 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
         if t.dtype not in (torch.float32, torch.bfloat16):
             t = t.float()
         return t.contiguous()
-    a3 = _operand(a3)
+    if qa is None:
+        a3 = _operand(a3)
     if packed is not None:
         if chunk_d:
             raise ValueError("a prepacked b runs without chunk_d")
@@ -303,7 +365,7 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     args = _lib.MatmulArgs()
     args.abi_version = _lib.ABI_VERSION
     args.engine = _lib.ENGINE[engine]
-    args.a = a3.data_ptr()
+    args.a = qa.buf.data_ptr() if qa is not None else a3.data_ptr()
     args.b = packed.buf.data_ptr() if packed is not None else b3.data_ptr()
     args.batch, args.batch_b, args.M, args.N, args.K = BH, BHb, M, N, K
     args.granularity = _lib.GRANULARITY[granularity]
@@ -320,7 +382,8 @@ def sc_matmul(a: torch.Tensor, b: torch.Tensor, *, granularity: str = "per_row",
     args.bias = _ptr(bias)
     args.out = out.data_ptr()
     args.acc_out = _ptr(acc_out)
-    args.io_flags = ((_lib.IO_A_BF16 if a3.dtype == torch.bfloat16 else 0)
+    args.io_flags = ((_lib.IO_A_BF16 if a3 is not None and a3.dtype == torch.bfloat16 else 0)
+                     | (_lib.IO_A_QUANT if qa is not None else 0)
                      | (_lib.IO_B_BF16 if b3 is not None and b3.dtype == torch.bfloat16 else 0)
                      | (_lib.IO_B_PACKED if packed is not None else 0)
                      | (_lib.IO_OUT_BF16 if out.dtype == torch.bfloat16 else 0))

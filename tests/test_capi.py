@@ -60,7 +60,10 @@ def _args(**kw):
     (dict(group_a=0), "group"),
     (dict(pool_dims=0), "pool_dims"),
     (dict(engine=5), "engine"),
-    (dict(io_flags=16), "io_flags"),
+    (dict(io_flags=32), "io_flags"),
+    (dict(io_flags=16, granularity=1), "SCMP_IO_A_QUANT"),
+    (dict(io_flags=16 | 1), "SCMP_IO_A_QUANT"),
+    (dict(io_flags=16, K=8, k_segment=4), "SCMP_IO_A_QUANT"),
 ])
 def test_invalid_arguments_are_rejected(kw, msg):
     lib = _lib.load()
@@ -93,3 +96,18 @@ def test_workspace_grows_with_problem():
     small = lib.scmp_sc_matmul_workspace_size(ctypes.byref(_args()))
     big = lib.scmp_sc_matmul_workspace_size(ctypes.byref(_args(M=400, N=500, K=64, pool_dims=64)))
     assert big > small
+
+
+def test_softmax_quantize_rejects_bad_arguments():
+    """Sizes and arguments of scmp_softmax_quantize are checked before any
+    launch (no GPU needed)."""
+    lib = _lib.load()
+    assert lib.scmp_softmax_quantize_size(-1, 257) == 0
+    assert lib.scmp_softmax_quantize_size(4, 0) == 0
+    assert lib.scmp_softmax_quantize_size(514, 257) >= 514 * 264 * 2 + 3 * 514 * 4
+    for rows, K, mode, prec, code in ((4, 32, 0, 8, -4), (4, 1025, 0, 8, -4), (4, 257, 3, 8, -1),
+                                      (4, 257, 0, 9, -1), (-1, 257, 0, 8, -1)):
+        rc = lib.scmp_softmax_quantize(None, rows, K, 0.125, mode, prec, None, 0, None, None)
+        assert rc == code, (rows, K, mode, prec, rc)
+    rc = lib.scmp_softmax_quantize(None, 4, 257, 0.125, 0, 8, None, 0, None, None)
+    assert rc == -1 and "non-NULL" in _lib.last_error()
