@@ -105,6 +105,9 @@ def _record_block(monkeypatch, cfg_id):
     rec = Recorder(sc_mod.sc_matmul)
     for mod in (attention, sc_linear, sc_mod):
         monkeypatch.setattr(mod, "sc_matmul", rec)
+    # record the probabilities as the Attn@V operand: the unfused softmax
+    # (the fused one gives the same bits: tests/test_softmax_quant_gpu.py)
+    monkeypatch.setattr(attention, "FUSED_SOFTMAX", False)
     # one full-width block, patched as the benchmark patches its 24 (config 5:
     # the LFSR-16 pool of block 0 and the head-aligned compensation on it)
     model = bench.build_model(cfg_id, torch.device("cuda", 0), torch.float32, depth=1,
