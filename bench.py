@@ -525,11 +525,13 @@ def measure_config1(dev, peaks, peak_i8, peak_popc) -> dict:
 def measure_config2(dev, peaks, peak_i8, peak_popc) -> dict:
     """Attention core: Q, K, V fp32 [64,16,257,64] ~ N(0,1); SC Q@K^T
     (per_head, pool (64,7), L=128), x scale, fp32 softmax, SC Attn@V (per_row,
-    probabilities unipolar, pool (257,7), L=128)."""
+    probabilities unipolar, pool (257,7), L=128).  The scale, the softmax and
+    the quantisation of the probabilities run as one fused pass (the same
+    bits as torch.softmax followed by sc_matmul on the probabilities)."""
     import torch
 
     from scmp_vit_b200 import sc_linear as scl
-    from scmp_vit_b200.attention import sc_av, sc_qk
+    from scmp_vit_b200.attention import sc_qk, sc_softmax_av
     g = torch.Generator().manual_seed(0)
     q, k, v = (torch.randn(64, 16, 257, 64, generator=g).to(dev) for _ in range(3))
     scale = 64 ** -0.5
@@ -540,8 +542,7 @@ def measure_config2(dev, peaks, peak_i8, peak_popc) -> dict:
         e[0].record()
         a = sc_qk(q, k, 7, cfg_for=scl._get_config)
         e[1].record()
-        a = (a * scale).softmax(dim=-1)
-        o = sc_av(a, v, 7, mode="unipolar", cfg_for=scl._get_config)
+        o = sc_softmax_av(a, scale, v, 7, mode="unipolar", cfg_for=scl._get_config)
         e[2].record()
         if rec is not None:
             rec.append(e)
