@@ -176,6 +176,23 @@ SCMP_API int scmp_softmax_quantize(const float *scores, int64_t rows, int64_t K,
                                    int mode, int sc_prec, void *a_quant, size_t a_quant_bytes,
                                    float *probs, void *stream);
 
+/* The fp32 elementwise steps of a transformer block around its matmuls,
+ * fused (the block forward of the DINOv2 model the reference patches,
+ * cls/sc_attention_patch.py:459-636: `x + ls1(attn(...))`, `fc2(act(fc1(...)))`,
+ * `x + ls2(mlp(...))`, plus `block(x) + comp(x)` where a compensation is
+ * installed).  Each step is rounded on its own in the order of the unfused
+ * ops, so the results carry their bits.  Row-major [rows][cols] fp32;
+ * asynchronous on `stream`; one launch each.
+ * scmp_bias_gelu: y = gelu(y + bias) in place (exact GELU, erf form), for an
+ * fc1 output computed without its bias.
+ * scmp_scale_residual: out = (x + (y [+ bias]) * gamma) [+ extra]; bias and
+ * extra nullable; out may alias x or y. */
+SCMP_API int scmp_bias_gelu(float *y, const float *bias, int64_t rows, int64_t cols,
+                            void *stream);
+SCMP_API int scmp_scale_residual(float *out, const float *x, const float *y, const float *bias,
+                                 const float *gamma, const float *extra, int64_t rows,
+                                 int64_t cols, void *stream);
+
 /* Split the fused qkv projection output of an attention block into the SC
  * matmul operands (the reshape / unbind / transpose of the qkv output in
  * cls/sc_attention_patch.py:248-328): qkv [B, N, 3, H, D] row-major ->

@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "scmp_split_qkv",
     "scmp_softmax_quantize_size",
     "scmp_softmax_quantize",
+    "scmp_bias_gelu",
+    "scmp_scale_residual",
 )
 
 
@@ -134,6 +136,13 @@ def load() -> ctypes.CDLL:
                                               ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
                                               ctypes.c_void_p]
         lib.scmp_softmax_quantize.restype = ctypes.c_int
+        lib.scmp_bias_gelu.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_void_p]
+        lib.scmp_bias_gelu.restype = ctypes.c_int
+        lib.scmp_scale_residual.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64,
+                                                                    ctypes.c_int64,
+                                                                    ctypes.c_void_p]
+        lib.scmp_scale_residual.restype = ctypes.c_int
         lib.scmp_debug_set_wait_limit.argtypes = [ctypes.c_uint64]
         lib.scmp_debug_set_wait_limit.restype = ctypes.c_int
         lib.scmp_debug_hold_producers.argtypes = [ctypes.c_int]

@@ -465,6 +465,31 @@ int scmp_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D, 
   return SCMP_OK;
 }
 
+int scmp_bias_gelu(float *y, const float *bias, int64_t rows, int64_t cols, void *stream) {
+  g_last_error.clear();
+  if (rows < 0 || cols < 0) return fail(SCMP_EINVAL, "negative size");
+  if (rows == 0 || cols == 0) return SCMP_OK;
+  if (!y || !bias) return fail(SCMP_EINVAL, "y and bias must be non-NULL");
+  const cudaError_t e = launch_bias_gelu(y, bias, rows, cols, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bias_gelu launch");
+  count_launches(1);
+  return SCMP_OK;
+}
+
+int scmp_scale_residual(float *out, const float *x, const float *y, const float *bias,
+                        const float *gamma, const float *extra, int64_t rows, int64_t cols,
+                        void *stream) {
+  g_last_error.clear();
+  if (rows < 0 || cols < 0) return fail(SCMP_EINVAL, "negative size");
+  if (rows == 0 || cols == 0) return SCMP_OK;
+  if (!out || !x || !y || !gamma) return fail(SCMP_EINVAL, "out, x, y and gamma must be non-NULL");
+  const cudaError_t e = launch_scale_residual(out, x, y, bias, gamma, extra, rows, cols,
+                                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "scale_residual launch");
+  count_launches(1);
+  return SCMP_OK;
+}
+
 size_t scmp_softmax_quantize_size(int64_t rows, int64_t K) {
   if (rows < 0 || K <= 0) return 0;
   return quant_a_layout(rows, K).total;

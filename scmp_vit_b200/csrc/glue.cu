@@ -110,7 +110,110 @@ cudaError_t launch_split(const void *qkv, int64_t B, int64_t N, int64_t H, int64
   return cudaGetLastError();
 }
 
+// ---- the fp32 elementwise steps of a transformer block around its matmuls,
+// fused.  Each operation is rounded on its own (no contraction), in the order
+// of the unfused torch ops, so the results carry their bits.
+
+// y = gelu(y + bias[c]) in place, gelu(t) = (t * 0.5) * (1 + erf(t * (1/sqrt 2)))
+// (exact GELU), for an fc1 output without its bias.
+__device__ __forceinline__ float gelu_exact(float t) {
+  const float kInvSqrt2 = 0.70710678118654752440f;
+  return __fmul_rn(__fmul_rn(t, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(t, kInvSqrt2))));
+}
+__global__ void bias_gelu_kernel(float *__restrict__ y, const float *__restrict__ bias,
+                                 int64_t rows, int64_t cols) {
+  const int64_t total = rows * cols;
+  if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(bias) & 15) == 0) {
+    float4 *y4 = reinterpret_cast<float4 *>(y);
+    const float4 *b4 = reinterpret_cast<const float4 *>(bias);
+    const int64_t c4 = cols >> 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (total >> 2);
+         i += (int64_t)gridDim.x * blockDim.x) {
+      float4 v = y4[i];
+      const float4 b = __ldg(b4 + i % c4);
+      v.x = gelu_exact(__fadd_rn(v.x, b.x));
+      v.y = gelu_exact(__fadd_rn(v.y, b.y));
+      v.z = gelu_exact(__fadd_rn(v.z, b.z));
+      v.w = gelu_exact(__fadd_rn(v.w, b.w));
+      y4[i] = v;
+    }
+    return;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = gelu_exact(__fadd_rn(y[i], __ldg(bias + i % cols)));
+}
+
+// out = (x + (y [+ bias[c]]) * gamma[c]) [+ extra]: a branch output y (a
+// matmul without its bias, or with it when bias is NULL) scaled by the layer
+// scale and added to the residual x, then the optional extra term (a
+// compensation output).  out may alias x or y.
+__device__ __forceinline__ float scale_residual_one(float x, float y, float b, float g, float e,
+                                                    bool has_b, bool has_e) {
+  float t = has_b ? __fadd_rn(y, b) : y;
+  t = __fadd_rn(x, __fmul_rn(t, g));
+  return has_e ? __fadd_rn(t, e) : t;
+}
+__global__ void scale_residual_kernel(float *out, const float *x, const float *y,
+                                      const float *__restrict__ bias,
+                                      const float *__restrict__ gamma, const float *extra,
+                                      int64_t rows, int64_t cols) {
+  const int64_t total = rows * cols;
+  const bool hb = bias != nullptr, he = extra != nullptr;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(x) |
+                       reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(gamma) |
+                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(extra);
+  if ((cols & 3) == 0 && (al & 15) == 0) {
+    const int64_t c4 = cols >> 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (total >> 2);
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const float4 xv = reinterpret_cast<const float4 *>(x)[i];
+      const float4 yv = reinterpret_cast<const float4 *>(y)[i];
+      const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + i % c4);
+      const float4 b = hb ? __ldg(reinterpret_cast<const float4 *>(bias) + i % c4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 e = he ? reinterpret_cast<const float4 *>(extra)[i]
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      o.x = scale_residual_one(xv.x, yv.x, b.x, g.x, e.x, hb, he);
+      o.y = scale_residual_one(xv.y, yv.y, b.y, g.y, e.y, hb, he);
+      o.z = scale_residual_one(xv.z, yv.z, b.z, g.z, e.z, hb, he);
+      o.w = scale_residual_one(xv.w, yv.w, b.w, g.w, e.w, hb, he);
+      reinterpret_cast<float4 *>(out)[i] = o;
+    }
+    return;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % cols;
+    out[i] = scale_residual_one(x[i], y[i], hb ? bias[c] : 0.f, gamma[c], he ? extra[i] : 0.f,
+                                hb, he);
+  }
+}
+
+unsigned glue_blocks(int64_t n) {
+  const int64_t b = (n + 255) / 256;
+  return (unsigned)(b < 148 * 16 ? b : 148 * 16);
+}
+
 }  // namespace
+
+cudaError_t launch_bias_gelu(float *y, const float *bias, int64_t rows, int64_t cols,
+                             cudaStream_t s) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  bias_gelu_kernel<<<glue_blocks(rows * cols / 4 + 1), 256, 0, s>>>(y, bias, rows, cols);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scale_residual(float *out, const float *x, const float *y, const float *bias,
+                                  const float *gamma, const float *extra, int64_t rows,
+                                  int64_t cols, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  scale_residual_kernel<<<glue_blocks(rows * cols / 4 + 1), 256, 0, s>>>(out, x, y, bias, gamma,
+                                                                           extra, rows, cols);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D,
                              int elem_bytes, void *q, void *k, void *vt, cudaStream_t s) {

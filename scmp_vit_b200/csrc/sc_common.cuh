@@ -139,6 +139,13 @@ cudaError_t launch_softmax_quantize(const float *x, int64_t rows, int K, float s
 // GemmProblem::count_table), from one pass over the pool.
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
                                 uint16_t *counts, cudaStream_t s);
+// fp32 block glue (glue.cu): y = gelu(y + bias) in place; out = (x + (y [+
+// bias]) * gamma) [+ extra], each step rounded on its own.
+cudaError_t launch_bias_gelu(float *y, const float *bias, int64_t rows, int64_t cols,
+                             cudaStream_t s);
+cudaError_t launch_scale_residual(float *out, const float *x, const float *y, const float *bias,
+                                  const float *gamma, const float *extra, int64_t rows,
+                                  int64_t cols, cudaStream_t s);
 // qkv [B, N, 3, H, D] -> q, k [B, H, N, D], vt [B, H, D, N] (elem_bytes 2 or 4)
 cudaError_t launch_split_qkv(const void *qkv, int64_t B, int64_t N, int64_t H, int64_t D,
                              int elem_bytes, void *q, void *k, void *vt, cudaStream_t s);

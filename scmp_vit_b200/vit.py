@@ -45,6 +45,54 @@ def _fp_linear(lin: nn.Module, x: torch.Tensor) -> torch.Tensor:
     return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
+# Whether the blocks run their fp32 elementwise steps fused on the engine
+# (scmp_bias_gelu, scmp_scale_residual); identical bits either way.
+FUSED_GLUE = True
+
+
+def set_fused_glue(flag: bool) -> None:
+    """Turn the fused fp32 block glue on or off (results are identical)."""
+    global FUSED_GLUE
+    FUSED_GLUE = bool(flag)
+
+
+def _stream(t: torch.Tensor):
+    import ctypes
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def bias_gelu_(t: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """``t = gelu(t + bias)`` in place (fp32 CUDA ``[..., C]``, exact GELU):
+    the bias add and torch's erf-form GELU in one pass, same bits."""
+    from . import _lib
+    C = t.shape[-1]
+    _lib.check(_lib.load().scmp_bias_gelu(t.data_ptr(), bias.data_ptr(), t.numel() // C, C,
+                                          _stream(t)))
+    return t
+
+
+def scale_residual(x: torch.Tensor, y: torch.Tensor, gamma: torch.Tensor,
+                   bias: Optional[torch.Tensor] = None, extra: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``(x + (y [+ bias]) * gamma) [+ extra]`` (fp32 CUDA ``[..., C]``, all
+    contiguous and of one shape): a block's layer-scaled residual add, with an
+    unfused bias and a compensation term, in one pass; each step rounded as
+    the separate torch ops round it.  ``out`` may be ``x`` or ``y``."""
+    from . import _lib
+    C = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _lib.check(_lib.load().scmp_scale_residual(
+        out.data_ptr(), x.data_ptr(), y.data_ptr(), None if bias is None else bias.data_ptr(),
+        gamma.data_ptr(), None if extra is None else extra.data_ptr(), x.numel() // C, C,
+        _stream(x)))
+    return out
+
+
+def _plain_linear(m: nn.Module) -> bool:
+    return (type(m) is nn.Linear and m.bias is not None and m.weight.dtype == torch.float32
+            and m.weight.is_contiguous() and m.bias.is_contiguous())
+
+
 class Mlp(nn.Module):
     def __init__(self, dim: int, hidden: int):
         super().__init__()
@@ -98,11 +146,42 @@ class Block(nn.Module):
 
     def forward(self, x):
         set_current_block_idx(self.block_idx)
+        if self._fused_glue_applies(x):
+            return self._forward_fused_glue(x)
         y = x + self.ls1(self.attn(self.norm1(x)))
         y = y + self.ls2(self.mlp(self.norm2(y)))
         if self.comp is not None:
             y = y + self.comp(x).to(y.dtype)
         return y
+
+    def _fused_glue_applies(self, x: torch.Tensor) -> bool:
+        return (FUSED_GLUE and x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+                and not torch.is_grad_enabled() and type(self.ls1) is LayerScale
+                and type(self.ls2) is LayerScale)
+
+    def _forward_fused_glue(self, x: torch.Tensor) -> torch.Tensor:
+        """The forward above with its fp32 elementwise steps on the engine:
+        ``x + ls1(a)`` in one pass, fc1's bias with the GELU, fc2's bias with
+        ``ls2``, the residual add and the compensation term in another (the
+        matmuls stay cuBLAS fp32).  Bit-identical to the unfused forward."""
+        a = self.attn(self.norm1(x)).contiguous()
+        y = scale_residual(x, a, self.ls1.gamma)
+        h = self.norm2(y)
+        mlp = self.mlp
+        ub = None
+        if (type(mlp) is Mlp and _plain_linear(mlp.fc1) and _plain_linear(mlp.fc2)
+                and type(mlp.act) is nn.GELU and mlp.act.approximate == "none"):
+            h2 = h.reshape(-1, h.shape[-1])
+            t = bias_gelu_(torch.mm(h2, mlp.fc1.weight.t()), mlp.fc1.bias)
+            u = torch.mm(t, mlp.fc2.weight.t())
+            ub = mlp.fc2.bias
+        else:
+            u = mlp(h)
+        e = None
+        if self.comp is not None:
+            e = self.comp(x).to(torch.float32).contiguous()
+        return scale_residual(y, u.reshape(y.shape).contiguous(), self.ls2.gamma, bias=ub,
+                              extra=e, out=y)
 
 
 class Backbone(nn.Module):

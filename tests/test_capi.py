@@ -111,3 +111,15 @@ def test_softmax_quantize_rejects_bad_arguments():
         assert rc == code, (rows, K, mode, prec, rc)
     rc = lib.scmp_softmax_quantize(None, 4, 257, 0.125, 0, 8, None, 0, None, None)
     assert rc == -1 and "non-NULL" in _lib.last_error()
+
+
+def test_block_glue_rejects_bad_arguments():
+    """Argument checks of the fused block glue (no launch, no GPU needed)."""
+    lib = _lib.load()
+    assert lib.scmp_bias_gelu(None, None, -1, 4, None) == -1
+    assert lib.scmp_bias_gelu(None, None, 0, 4, None) == 0
+    assert lib.scmp_bias_gelu(None, None, 2, 4, None) == -1
+    assert "non-NULL" in _lib.last_error()
+    assert lib.scmp_scale_residual(None, None, None, None, None, None, 3, -2, None) == -1
+    assert lib.scmp_scale_residual(None, None, None, None, None, None, 3, 4, None) == -1
+    assert "non-NULL" in _lib.last_error()
