@@ -45,6 +45,7 @@ def main(argv=None) -> int:
     from . import config_helpers as ch
     from .sc import prepack_b, sc_matmul
     torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False  # fp32 convolutions, as the benchmark runs them
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(0)
     random.seed(0)
