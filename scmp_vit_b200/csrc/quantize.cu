@@ -372,8 +372,8 @@ __global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int6
 // Attn@V call), in one pass with one warp per row.  The softmax repeats the
 // arithmetic of torch.softmax's warp-per-row kernel for fp32 rows of up to
 // 1024 values, so the probabilities carry the same bits: lane l holds the
-// elements l + 32 i (i < NI, NI = the next power of two >= K, over 32;
-// -inf past K); the row maximum is taken by lane, in i order, then by xor
+// elements l + 32 i (i < NI; -inf past K; torch holds NI = the next power
+// of two >= K, over 32, and any NI >= K / 32 gives the same sums); the row maximum is taken by lane, in i order, then by xor
 // butterfly; e = expf(v - max) is summed by lane in i order starting from
 // 0, then by xor butterfly; p = e / sum (IEEE division).  The quantisation
 // is that of quantize_rows_kernel (group_scale_of, round half to even, the
@@ -630,12 +630,17 @@ cudaError_t launch_softmax_quantize(const float *x, int64_t rows, int K, float s
 #define SCMP_SOFTMAX_Q(NI)                                                                      \
   softmax_quantize_kernel<NI><<<(unsigned)blocks, 256, 0, s>>>(x, rows, K, scale, mode, prec, ldc, \
                                                                code, rscale, rzero, rsum, probs)
+  // NI = ceil(K / 32) would do for the arithmetic: the elements torch's
+  // kernel holds past that (up to the next power of two) are -inf, whose e =
+  // +0 leaves the lane sums unchanged; 9 covers 257-token rows
   if (K <= 64)
     SCMP_SOFTMAX_Q(2);
   else if (K <= 128)
     SCMP_SOFTMAX_Q(4);
   else if (K <= 256)
     SCMP_SOFTMAX_Q(8);
+  else if (K <= 288)
+    SCMP_SOFTMAX_Q(9);
   else if (K <= 512)
     SCMP_SOFTMAX_Q(16);
   else

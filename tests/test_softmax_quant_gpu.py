@@ -13,7 +13,7 @@ from scmp_vit_b200.sc import QuantizedRows, sc_matmul, softmax_quantize
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("K", [33, 64, 100, 257, 513, 1000])
+@pytest.mark.parametrize("K", [33, 64, 100, 256, 257, 288, 289, 513, 1000])
 def test_probabilities_match_torch_softmax(cuda_device, K):
     g = torch.Generator().manual_seed(K)
     rows = 700
