@@ -330,6 +330,16 @@ int quantize_operand(const void *x, bool x_bf16, const OperandLayout &o, int64_t
     if (o.g.rows > 0) count_launches(1);
     return SCMP_OK;
   }
+  if (!x_bf16 &&
+      launch_quantize_slices(static_cast<const float *>(x), o.g, K, o.ldc, mode, prec,
+                             reinterpret_cast<int16_t *>(ws + o.code),
+                             reinterpret_cast<float *>(ws + o.rscale),
+                             reinterpret_cast<int32_t *>(ws + o.rzero),
+                             reinterpret_cast<int32_t *>(ws + o.rsum), s, &e)) {
+    if (e != cudaSuccess) return cuda_fail(e, "quantize_slices launch");
+    if (o.g.rows > 0) count_launches(1);
+    return SCMP_OK;
+  }
   if ((e = launch_row_stats(x, x_bf16, o.g.rows, K, mode, stat, s)) != cudaSuccess)
     return cuda_fail(e, "row_stats launch");
   if ((e = launch_group_stats(stat, o.g, mode, prec, gscale, ginv, gzero, s)) != cudaSuccess)

@@ -367,6 +367,105 @@ __global__ void quantize_rows_kernel(const T *__restrict__ x, int64_t rows, int6
   }
 }
 
+// Per-slice scale groups of short rows (per-head scaling of attention
+// slices: 257 rows of 64), fused: one block per slice holds the whole slice
+// in registers (up to kSliceVec float4 per thread, 16-byte loads issued
+// together), takes its max |x| (or min / max), the slice's scale, and writes
+// the codes and row records from the registers.  Rows are K = 4 R elements
+// with R dividing 32, so each row's float4s sit in R adjacent lanes, which
+// sum its codes with shuffles.  Same arithmetic as row_stats_kernel +
+// group_stats_kernel + quantize_kernel (min / max are exact in any order), so
+// the codes and scales are identical.
+constexpr int kSliceVec = 20;
+template <int R>
+__global__ void __launch_bounds__(256) quantize_slices_kernel(
+    const float *__restrict__ x, int64_t rows_per_slice, int mode, int prec,
+    int16_t *__restrict__ code, float *__restrict__ rscale, int32_t *__restrict__ rzero,
+    int32_t *__restrict__ rsum) {
+  constexpr int K = 4 * R;
+  const int64_t slice = blockIdx.x;
+  const int nvec = (int)(rows_per_slice * R);  // float4s in the slice
+  const float4 *xs = reinterpret_cast<const float4 *>(x + slice * rows_per_slice * K);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const bool bip = mode == SCMP_BIPOLAR;
+  float4 v[kSliceVec];
+#pragma unroll
+  for (int i = 0; i < kSliceVec; ++i) {
+    const int f = t + 256 * i;
+    v[i] = f < nvec ? __ldg(xs + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kSliceVec; ++i) {
+    if (t + 256 * i < nvec) {
+      const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (bip) {
+          hi = fmaxf(hi, fabsf(e[j]));
+        } else {
+          lo = fminf(lo, e[j]);
+          hi = fmaxf(hi, e[j]);
+        }
+      }
+    }
+  }
+  __shared__ float slo[8], shi[8];
+  lo = warp_min(lo);
+  hi = warp_max(hi);
+  if (lane == 0) {
+    slo[warp] = lo;
+    shi[warp] = hi;
+  }
+  __syncthreads();
+  lo = INFINITY;
+  hi = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    lo = fminf(lo, slo[w]);
+    hi = fmaxf(hi, shi[w]);
+  }
+  float sc, inv;
+  int32_t z;
+  group_scale_of(lo, hi, mode, prec, sc, inv, z);
+  const int iq = bip ? (1 << (prec - 1)) - 1 : (1 << prec) - 1;
+  uint2 *cs = reinterpret_cast<uint2 *>(code + slice * rows_per_slice * K);
+  const int64_t row0 = slice * rows_per_slice;
+#pragma unroll
+  for (int i = 0; i < kSliceVec; ++i) {
+    const int f = t + 256 * i;
+    if (256 * i >= nvec) break;  // block-uniform
+    const bool ok = f < nvec;
+    const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    int c[4], acc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int q = __float2int_rn(__fmul_rn(e[j], inv));
+      if (bip) {
+        q = max(-iq, min(iq, q));
+        c[j] = 2 * q;
+        acc += 2 * abs(q);
+      } else {
+        q = max(0, min(iq, q + z));
+        c[j] = q;
+        acc += q;
+      }
+    }
+    if (ok)
+      cs[f] = make_uint2(((uint32_t)(uint16_t)c[0]) | ((uint32_t)(uint16_t)c[1] << 16),
+                         ((uint32_t)(uint16_t)c[2]) | ((uint32_t)(uint16_t)c[3] << 16));
+    // a row's R float4s are lanes f - f % R .. + R - 1 of this warp
+#pragma unroll
+    for (int o = R / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (ok && f % R == 0) {
+      const int64_t r = row0 + f / R;
+      rscale[r] = sc;
+      rzero[r] = z;
+      rsum[r] = acc;
+    }
+  }
+}
+
 // Softmax of scale * x along rows of K (32 < K <= 1024) values, then the
 // per-row quantisation of the probabilities (the a operand of a per-row
 // Attn@V call), in one pass with one warp per row.  The softmax repeats the
@@ -619,6 +718,36 @@ cudaError_t launch_pack_b_streams(const int16_t *code, int64_t N, int64_t ldk, i
     pack_b_streams_kernel<<<(unsigned)blocks, 256, 0, s>>>(code, N, ldk, prec, shift,
                                                            pool_period, pool_comp, out);
   return cudaGetLastError();
+}
+
+bool launch_quantize_slices(const float *x, const GroupShape &g, int64_t K, int64_t ldc,
+                            int mode, int prec, int16_t *code, float *rscale, int32_t *rzero,
+                            int32_t *rsum, cudaStream_t s, cudaError_t *err) {
+  // per-slice groups of whole slices, rows of 4 R fp32 values (R | 32),
+  // unpadded code rows, 16-byte aligned slices that fit the registers
+  const bool whole = g.group_rows == g.slice_rows && g.rows % g.slice_rows == 0;
+  const int64_t R = K / 4;
+  if (!whole || K % 4 != 0 || ldc != K || (R != 4 && R != 8 && R != 16 && R != 32) ||
+      g.slice_rows * R > 256 * kSliceVec || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+      g.ngroups > 0x7FFFFFFF)
+    return false;
+  *err = cudaSuccess;
+  if (g.ngroups == 0) return true;
+  const unsigned grid = (unsigned)g.ngroups;
+  if (R == 4)
+    quantize_slices_kernel<4><<<grid, 256, 0, s>>>(x, g.slice_rows, mode, prec, code, rscale,
+                                                   rzero, rsum);
+  else if (R == 8)
+    quantize_slices_kernel<8><<<grid, 256, 0, s>>>(x, g.slice_rows, mode, prec, code, rscale,
+                                                   rzero, rsum);
+  else if (R == 16)
+    quantize_slices_kernel<16><<<grid, 256, 0, s>>>(x, g.slice_rows, mode, prec, code, rscale,
+                                                    rzero, rsum);
+  else
+    quantize_slices_kernel<32><<<grid, 256, 0, s>>>(x, g.slice_rows, mode, prec, code, rscale,
+                                                    rzero, rsum);
+  *err = cudaGetLastError();
+  return true;
 }
 
 cudaError_t launch_softmax_quantize(const float *x, int64_t rows, int K, float scale, int mode,

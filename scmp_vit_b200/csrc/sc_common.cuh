@@ -129,6 +129,13 @@ cudaError_t launch_quantize(const void *x, bool x_bf16, const GroupShape &g, int
 cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64_t K,
                                  int64_t ldc, int mode, int prec, int16_t *code, float *rscale,
                                  int32_t *rzero, int32_t *rsum, cudaStream_t s);
+// Whole-slice scale groups of short fp32 rows (per-head scaling of attention
+// slices) in one launch, identical results to launch_row_stats +
+// launch_group_stats + launch_quantize; false (nothing launched) when the
+// shape does not qualify, else *err holds the launch status.
+bool launch_quantize_slices(const float *x, const GroupShape &g, int64_t K, int64_t ldc,
+                            int mode, int prec, int16_t *code, float *rscale, int32_t *rzero,
+                            int32_t *rsum, cudaStream_t s, cudaError_t *err);
 // Row softmax of scale * x (fp32, 32 < K <= 1024; torch.softmax's bits)
 // and its per-row quantisation into codes [rows][ldc] and row records;
 // probs (nullable) receives the probabilities.
