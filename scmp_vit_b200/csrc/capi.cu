@@ -108,7 +108,7 @@ void layout_operand(Carver &c, OperandLayout &o, int64_t K, int64_t ldc) {
 struct Plan {
   OperandLayout A, B;
   size_t table = 0;
-  size_t counts = 0;  // prefix counts of the stream table (thin strips)
+  size_t strips = 0;  // the thin strips' table (stream words with prefix counts)
   size_t pool_comp = 0;
   int64_t pool_comp_rows = 0;
   int64_t ldk = 0;
@@ -283,7 +283,7 @@ Plan make_plan(const scmp_matmul_args *x) {
   const int T = 1 << x->sc_prec;
   const int WT = T >= 32 ? T / 32 : 1;
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
-  p.counts = c.take(sizeof(uint16_t) * (size_t)x->pool_dims * (WT + 1) * (T + 1));
+  p.strips = c.take(sizeof(uint2) * (size_t)x->pool_dims * (T + 1) * (WT + 1));
   p.pool_comp_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
   p.pool_comp = c.take((size_t)p.pool_comp_rows * T);
   p.ksplit = plan_ksplit(x, p.ldk);
@@ -611,7 +611,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.out_bf16 = (x.io_flags & SCMP_IO_OUT_BF16) != 0;
   P.acc_out = x.acc_out;
   P.stream_table = table;
-  P.count_table = reinterpret_cast<const uint16_t *>(ws + plan.counts);
+  P.strip_table = reinterpret_cast<const uint2 *>(ws + plan.strips);
   P.pool_comp = ws + plan.pool_comp;
   P.m_lo = 0;
   P.m_hi = x.M;
@@ -654,7 +654,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   const bool strip_n = use_tc && n_tc < x.N && m_tc > 0;
   if (!use_tc || strip_m || strip_n) {
     if ((e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table,
-                                 reinterpret_cast<uint16_t *>(ws + plan.counts), s)) !=
+                                 reinterpret_cast<uint2 *>(ws + plan.strips), s)) !=
         cudaSuccess)
       return cuda_fail(e, "stream_table launch");
     count_launches(1);

@@ -219,13 +219,16 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_kernel(GemmProblem P) {
 
 // Thin windows with a short reduction (K <= 512, e.g. the 257th row / column
 // of Q@K^T and Attn@V): G lanes per output (G = 8 for K <= 128, else 32)
-// split the reduction indices (lane j of a group takes d = j, j + G, ...);
-// the group's signed counts are summed with shuffles and its first lane
-// rescales and stores.  Consecutive groups take consecutive columns of a row.
-// The count of index d is one prefix-count lookup and one masked stream word:
-//   #{t < k : R[d'][t] < v} = CT[d'][k / 32][v] + popc(ST[d'][v][k / 32] & (2^(k % 32) - 1))
-// (the word is not read past the stream: k = 2^p has no partial word).  Index
-// math is 32-bit: the host launches this kernel when batch x strip < 2^31.
+// split the reduction indices in chunks of 8 (lane j of a group takes
+// indices 8 c .. 8 c + 7 for c = j, j + G, ..., one 16-byte load of each
+// code row per chunk; the code rows are ldk = ceil8(K) long, padded with
+// code 0, which counts nothing); the group's signed counts are summed with
+// shuffles and its first lane rescales and stores.  Consecutive groups take
+// consecutive columns of a row.  The count of index d is one 8-byte entry
+// of the strip table, SW[d'][v][k / 32] = {stream word, prefix count}:
+//   #{t < k : R[d'][t] < v} = count + popc(word & (2^(k % 32) - 1))
+// (at k = 2^p the word is 0 and the mask empty).  Index math is 32-bit: the
+// host launches this kernel when batch x strip < 2^31.
 template <int G>
 __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P) {
   static_assert(G == 8 || G == 32, "lane groups of 8 or 32");
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
   const int T = 1 << P.prec;
   const int WT = T >= 32 ? T / 32 : 1;
   const int pd = P.pool_dims;
-  const int K = (int)P.K;
+  const int nchunk = (int)(P.ldk >> 3);
   const int lane = threadIdx.x & 31;
   const int j = lane & (G - 1);
   constexpr uint32_t kGroupsPerWarp = 32 / G;
@@ -258,38 +261,29 @@ __global__ void __launch_bounds__(256) gemm_popc_thin_lane_kernel(GemmProblem P)
     const int L = row_stream_len(P, slice, grow);
     int acc = 0;
     if (L > 0) {
-      const int16_t *ca = P.qa.code + grow * P.ldk;
-      const int16_t *cb = P.qb.code + brow * P.ldk;
-      int dm = j % pd;  // pool row d mod pool_dims, advanced without a division
-      // four indices per round: their code loads, then their table loads, are
-      // in flight together (indices past K read code 0: an empty window)
-      for (int d = j; d < K; d += 4 * G) {
-        int a[4], b[4], pr[4];
+      const uint4 *ca = reinterpret_cast<const uint4 *>(P.qa.code + grow * P.ldk);
+      const uint4 *cb = reinterpret_cast<const uint4 *>(P.qb.code + brow * P.ldk);
+      for (int c = j; c < nchunk; c += G) {
+        const uint4 av = __ldg(ca + c), bv = __ldg(cb + c);
+        const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        int dm = (8 * c) % pd;  // pool row of the chunk's first index
+        int a[8], b[8], k[8];
+        uint2 e[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int di = d + i * G;
-          a[i] = di < K ? ca[di] : 0;
-          b[i] = di < K ? cb[di] : 0;
-          pr[i] = dm;
-          dm += G;
-          while (dm >= pd) dm -= pd;
-        }
-        int k[4], ct[4];
-        uint32_t word[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 8; ++i) {
+          a[i] = (i & 1) ? ((int)aw[i >> 1] >> 16) : (int)(int16_t)(aw[i >> 1] & 0xFFFFu);
+          b[i] = (i & 1) ? ((int)bw[i >> 1] >> 16) : (int)(int16_t)(bw[i >> 1] & 0xFFFFu);
           // (k <= 2^p for every valid stream length; the clamp keeps the
           // table reads inside their rows whatever the per-row lengths hold)
           k[i] = min(((a[i] < 0 ? -a[i] : a[i]) * L) >> P.prec, T);
           const int v = b[i] < 0 ? -b[i] : b[i];
-          const int w = k[i] >> 5;
-          word[i] = __ldg(P.stream_table + (pr[i] * (T + 1) + v) * WT + (w < WT ? w : WT - 1));
-          ct[i] = (int)__ldg(P.count_table + (pr[i] * (WT + 1) + w) * (T + 1) + v);
+          e[i] = __ldg(P.strip_table + (dm * (T + 1) + v) * (WT + 1) + (k[i] >> 5));
+          if (++dm == pd) dm = 0;
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int cnt =
-              ct[i] + __popc(__funnelshift_lc(0xffffffffu, 0u, (uint32_t)(k[i] & 31)) & word[i]);
+        for (int i = 0; i < 8; ++i) {
+          const int cnt = (int)e[i].y +
+                          __popc(__funnelshift_lc(0xffffffffu, 0u, (uint32_t)(k[i] & 31)) & e[i].x);
           acc += ((a[i] < 0) != (b[i] < 0) ? -cnt : cnt);
         }
       }
@@ -322,7 +316,13 @@ cudaError_t launch_thin_lane(const GemmProblem &P, cudaStream_t s) {
 template <int LW>
 cudaError_t launch_thin(const GemmProblem &P, cudaStream_t s) {
   const int64_t total = P.batch * (P.m_hi - P.m_lo) * (P.n_hi - P.n_lo);
-  if (P.K <= 512 && P.count_table && total < ((int64_t)1 << 31)) return launch_thin_lane(P, s);
+  // (16-byte code loads: unsegmented code rows of ldk = ceil8(K) codes from
+  // 16-byte aligned planes)
+  const bool vec = P.nseg == 1 && (P.ldk & 7) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(P.qa.code) |
+                     reinterpret_cast<uintptr_t>(P.qb.code)) & 15) == 0;
+  if (P.K <= 512 && P.strip_table && vec && total < ((int64_t)1 << 31))
+    return launch_thin_lane(P, s);
   int64_t blocks = (total + 7) / 8;  // 8 warps per block, one output per warp
   if (blocks > 148 * 32) blocks = 148 * 32;
   gemm_popc_thin_kernel<LW><<<(unsigned)blocks, 256, 0, s>>>(P);

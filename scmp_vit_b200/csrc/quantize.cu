@@ -561,13 +561,14 @@ __global__ void __launch_bounds__(256) softmax_quantize_kernel(
 }
 
 // ST[d][v][w]: bit j of word w = [R[d][32w+j] < v] for 32w+j < 2^p; with
-// counts, CT[d][w][v] = #{t < 32 w : R[d][t] < v} for w = 0 .. WT.  One
-// thread per word; the WT words of a (d, v) sit in adjacent lanes, which
-// scan their popcounts with shuffles (WT divides 32, so a group never spans
-// two warps, and the loop runs over warp-aligned bases so that every lane
-// reaches the shuffles).
+// strips != NULL also the thin strips' table SW[d][v][w] = {ST[d][v][w],
+// #{t < 32 w : R[d][t] < v}} for w = 0 .. WT (word 0 at w = WT), one 8-byte
+// entry per lookup.  One thread per word; the WT words of a (d, v) sit in
+// adjacent lanes, which scan their popcounts with shuffles (WT divides 32,
+// so a group never spans two warps, and the loop runs over warp-aligned bases
+// so that every lane reaches the shuffles).
 __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_dims, int prec,
-                                    uint32_t *__restrict__ table, uint16_t *__restrict__ counts) {
+                                    uint32_t *__restrict__ table, uint2 *__restrict__ strips) {
   const int T = 1 << prec;
   const int WT = T >= 32 ? T / 32 : 1;
   const int64_t total = (int64_t)pool_dims * (T + 1) * WT;
@@ -589,7 +590,7 @@ __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_d
         if (32 * w + j < T && (int)R[j] < v) word |= 1u << j;
       table[i] = word;
     }
-    if (counts) {
+    if (strips) {
       const int c = __popc(word);
       int incl = c;
       for (int off = 1; off < WT; off <<= 1) {
@@ -597,8 +598,8 @@ __global__ void stream_table_kernel(const uint8_t *__restrict__ pool, int pool_d
         if (w >= off) incl += y;
       }
       if (valid) {
-        counts[(d * (WT + 1) + w) * (T + 1) + v] = (uint16_t)(incl - c);
-        if (w == WT - 1) counts[(d * (WT + 1) + WT) * (T + 1) + v] = (uint16_t)incl;
+        strips[dv * (WT + 1) + w] = make_uint2(word, (uint32_t)(incl - c));
+        if (w == WT - 1) strips[dv * (WT + 1) + WT] = make_uint2(0u, (uint32_t)incl);
       }
     }
   }
@@ -868,12 +869,12 @@ cudaError_t launch_quantize_rows(const void *x, bool x_bf16, int64_t rows, int64
 }
 
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
-                                uint16_t *counts, cudaStream_t s) {
+                                uint2 *strips, cudaStream_t s) {
   const int T = 1 << prec;
   const int64_t threads = (int64_t)pool_dims * (T + 1) * (T >= 32 ? T / 32 : 1);
   const int64_t blocks = (threads + 255) / 256;
   stream_table_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, s>>>(
-      pool, pool_dims, prec, table, counts);
+      pool, pool_dims, prec, table, strips);
   return cudaGetLastError();
 }
 

@@ -58,9 +58,9 @@ struct GemmProblem {
   int32_t *acc_out;
   // stream table ST[pool_dims][2^p + 1][2^p / 32] (bit t of threshold v)
   const uint32_t *stream_table;
-  // prefix counts of the stream table, CT[pool_dims][2^p / 32 + 1][2^p + 1]:
-  // CT[d][w][v] = #{t < 32 w : R[d][t] < v} (the thin strips' counts)
-  const uint16_t *count_table;
+  // the thin strips' table SW[pool_dims][2^p + 1][2^p / 32 + 1]:
+  // SW[d][v][w] = {ST[d][v][w] (0 at w = 2^p / 32), #{t < 32 w : R[d][t] < v}}
+  const uint2 *strip_table;
   // pool complement PC[pool_dims][2^p] = 0x7F - (R >> shift) (tensor-core
   // row producers; shift = 1 for bipolar p = 8, else 0)
   const uint8_t *pool_comp;
@@ -142,10 +142,10 @@ bool launch_quantize_slices(const float *x, const GroupShape &g, int64_t K, int6
 cudaError_t launch_softmax_quantize(const float *x, int64_t rows, int K, float scale, int mode,
                                     int prec, int64_t ldc, int16_t *code, float *rscale,
                                     int32_t *rzero, int32_t *rsum, float *probs, cudaStream_t s);
-// The stream table and, when counts != NULL, its prefix counts (see
-// GemmProblem::count_table), from one pass over the pool.
+// The stream table and, when strips != NULL, the thin strips' table (see
+// GemmProblem::strip_table), from one pass over the pool.
 cudaError_t launch_stream_table(const uint8_t *pool, int pool_dims, int prec, uint32_t *table,
-                                uint16_t *counts, cudaStream_t s);
+                                uint2 *strips, cudaStream_t s);
 // fp32 block glue (glue.cu): y = gelu(y + bias) in place; out = (x + (y [+
 // bias]) * gamma) [+ extra], each step rounded on its own.
 cudaError_t launch_bias_gelu(float *y, const float *bias, int64_t rows, int64_t cols,
