@@ -109,6 +109,7 @@ struct Plan {
   OperandLayout A, B;
   size_t table = 0;
   size_t strips = 0;  // the thin strips' table (stream words with prefix counts)
+  bool has_strips = false;  // carved only where the lane-group strip kernel can run
   size_t pool_comp = 0;
   int64_t pool_comp_rows = 0;
   int64_t ldk = 0;
@@ -283,7 +284,11 @@ Plan make_plan(const scmp_matmul_args *x) {
   const int T = 1 << x->sc_prec;
   const int WT = T >= 32 ? T / 32 : 1;
   p.table = c.take(sizeof(uint32_t) * (size_t)x->pool_dims * (T + 1) * WT);
-  p.strips = c.take(sizeof(uint2) * (size_t)x->pool_dims * (T + 1) * (WT + 1));
+  // (the lane-group strip kernel takes unsegmented K <= 512; other strips
+  // read the stream table alone)
+  p.has_strips = x->K <= 512 && kseg == x->K;
+  if (p.has_strips)
+    p.strips = c.take(sizeof(uint2) * (size_t)x->pool_dims * (T + 1) * (WT + 1));
   p.pool_comp_rows = p.ldk > x->pool_dims ? p.ldk : x->pool_dims;
   p.pool_comp = c.take((size_t)p.pool_comp_rows * T);
   p.ksplit = plan_ksplit(x, p.ldk);
@@ -611,7 +616,7 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   P.out_bf16 = (x.io_flags & SCMP_IO_OUT_BF16) != 0;
   P.acc_out = x.acc_out;
   P.stream_table = table;
-  P.strip_table = reinterpret_cast<const uint2 *>(ws + plan.strips);
+  P.strip_table = plan.has_strips ? reinterpret_cast<const uint2 *>(ws + plan.strips) : nullptr;
   P.pool_comp = ws + plan.pool_comp;
   P.m_lo = 0;
   P.m_hi = x.M;
@@ -654,7 +659,9 @@ int scmp_sc_matmul(const scmp_matmul_args *args, void *stream) {
   const bool strip_n = use_tc && n_tc < x.N && m_tc > 0;
   if (!use_tc || strip_m || strip_n) {
     if ((e = launch_stream_table(x.pool, x.pool_dims, x.sc_prec, table,
-                                 reinterpret_cast<uint2 *>(ws + plan.strips), s)) !=
+                                 plan.has_strips ? reinterpret_cast<uint2 *>(ws + plan.strips)
+                                                 : nullptr,
+                                 s)) !=
         cudaSuccess)
       return cuda_fail(e, "stream_table launch");
     count_launches(1);
